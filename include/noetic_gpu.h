@@ -1,0 +1,217 @@
+/*
+ * noetic_gpu.h -- C ABI of the B200 token loop of the noetic language model.
+ *
+ * The reference (noetic, Rust, std-only) has no FFI layer; its boundary is the
+ * crate API listed beside each entry point below.  Each declaration cites the
+ * reference interface it replaces (file:line inside the noetic crate).
+ *
+ * Conventions
+ *   - Every call returns nk_status (0 == NK_OK).  Nothing aborts or throws
+ *     across the ABI; nk_last_error() returns a thread-local message for the
+ *     last failing call on the calling thread.
+ *   - Handles are opaque.  A model lives on one CUDA device; a decoder belongs
+ *     to one model and owns its device state, scratch and CUDA stream.
+ *   - Host pointers are borrowed for the duration of the call only.  Entry
+ *     points whose name ends in _device take device pointers instead and do
+ *     not synchronise; everything else synchronises the decoder's stream
+ *     before returning.
+ *   - A handle is not thread-safe; use one decoder per host thread.
+ *   - All arithmetic is f32 with f32 state (f64 where the reference's sampler
+ *     uses f64).  Token ids are u32; invalid ids and shapes are rejected on
+ *     the host before any launch.
+ */
+#ifndef NOETIC_GPU_H
+#define NOETIC_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef enum nk_status {
+    NK_OK = 0,
+    NK_ERR_INVALID = 1,     /* bad argument, shape or token id            */
+    NK_ERR_CUDA = 2,        /* a CUDA runtime/driver call failed          */
+    NK_ERR_OOM = 3,         /* device allocation failed                   */
+    NK_ERR_IO = 4,          /* checkpoint file error (ckpt.rs InvalidData) */
+    NK_ERR_UNSUPPORTED = 5, /* valid for the reference, not supported here */
+    NK_ERR_DEVICE = 6       /* a kernel reported an error status          */
+} nk_status;
+
+/* model.rs:20-30 LmConfig (usize fields widened to u64). */
+typedef struct nk_config {
+    uint64_t vocab, d_model, n_layer, expand, conv_k, mlp_mult;
+    float eps, tau_max;
+} nk_config;
+
+/* infer.rs:211-219 SampleCfg. */
+typedef struct nk_sample_cfg {
+    float temperature;
+    uint64_t top_k;
+    float top_p;
+    float rep_penalty;
+    uint64_t rep_window;
+    uint32_t greedy;
+} nk_sample_cfg;
+
+typedef struct nk_model nk_model;
+typedef struct nk_decoder nk_decoder;
+
+/* Thread-local description of the last error on this thread. */
+const char *nk_last_error(void);
+
+/* Number of CUDA devices visible to this process. */
+nk_status nk_device_count(int *count);
+
+/* model.rs:37-76 LmConfig::check. */
+nk_status nk_config_check(const nk_config *cfg);
+
+/* ---------------------------------------------------------------- model */
+
+/* Graph + Lm parameter storage (autograd.rs:92-112, model.rs:175-180) on
+ * `device`.  Tensors start zeroed; fill them with nk_model_init_random,
+ * nk_model_set_tensor or nk_model_load_ckpt.  device == -1 creates a
+ * host-only model (initialisation and checkpoint I/O, no decoder). */
+nk_status nk_model_create(const nk_config *cfg, int device, nk_model **out);
+nk_status nk_model_destroy(nk_model *model);
+nk_status nk_model_config(const nk_model *model, nk_config *out);
+
+/* Lm::new(g, &mut Rng::new(seed), cfg) (model.rs:183-206): the reference's
+ * seeded initialiser, bit-for-bit (SplitMix64 / xoshiro256++ / Marsaglia
+ * polar draws in creation order).  rng_after[4] (nullable) receives the
+ * generator state after initialisation, which is the sampler state that
+ * `noetic gen` continues with (cli.rs:898-947). */
+nk_status nk_model_init_random(nk_model *model, uint64_t seed, uint64_t rng_after[4]);
+
+/* Number of named tensors and their names / shapes in creation order
+ * (the checkpoint order, ckpt.rs:161-173). */
+nk_status nk_model_tensor_count(const nk_model *model, uint64_t *count);
+nk_status nk_model_tensor_info(const nk_model *model, uint64_t index, const char **name,
+                               uint32_t *rank, uint64_t shape[4]);
+
+/* Copy one named parameter (ckpt tensor name, e.g. "blk0.ssm.in_proj.w")
+ * from host memory.  The shape must match exactly (ckpt.rs:424). */
+nk_status nk_model_set_tensor(nk_model *model, const char *name, const float *data,
+                              const uint64_t *shape, uint32_t rank);
+nk_status nk_model_get_tensor(const nk_model *model, const char *name, float *out,
+                              uint64_t numel);
+
+/* ckpt::load (ckpt.rs:299-383) + the config rules of cmd_gen
+ * (cli.rs:909-920) + apply_exact (ckpt.rs:410-436), into a new model on
+ * `device`.  Rejects corrupt, truncated, inconsistent or mismatched files
+ * with NK_ERR_IO before creating anything. */
+nk_status nk_model_load_ckpt(const char *path, int device, nk_model **out);
+
+/* ckpt::save (ckpt.rs:125-200) of the model tensors with the metadata keys
+ * cmd_gen needs.  Used to hand models between implementations. */
+nk_status nk_model_save_ckpt(const nk_model *model, const char *path);
+
+/* ---------------------------------------------------------------- decoder */
+
+/* Decoder::new (infer.rs:86-88) for n_streams independent streams, each
+ * with its own LmState (infer.rs:21-35). */
+nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **out);
+nk_status nk_decoder_destroy(nk_decoder *dec);
+nk_status nk_decoder_streams(const nk_decoder *dec, uint32_t *n_streams);
+
+/* LmState::reset / Decoder::reset (infer.rs:37-44, 90-92) for streams
+ * [first, first+count). */
+nk_status nk_decoder_reset(nk_decoder *dec, uint32_t first, uint32_t count);
+
+/* Decoder::step (infer.rs:100-103, 106-200) for every stream: tokens[S]
+ * host; logits_out[S*vocab] host (nullable).  The logits also stay on the
+ * device as the input of nk_decoder_sample (Decoder::logits_mut). */
+nk_status nk_decoder_step(nk_decoder *dec, const uint32_t *tokens, float *logits_out);
+
+/* The prompt loop of cli.rs:generate (cli.rs:478-480: one Decoder::step per
+ * prompt token) computed with the chunked parallel scan instead
+ * (model.rs:148-165 semantics).  ids is [S, max_t] row-major; lens[S] are
+ * the prompt lengths (0 <= len <= max_t; a stream with len 0 is left as it
+ * is).  Continues from each stream's current state.  last_logits[S*vocab]
+ * (nullable) receives the logits after each stream's last prompt token. */
+nk_status nk_decoder_prefill(nk_decoder *dec, const uint32_t *ids, const uint32_t *lens,
+                             uint32_t max_t, float *last_logits);
+
+/* sample_token (infer.rs:228-305) applied to the logits of the last step /
+ * prefill for every stream.  history is [S, history_stride] with per-stream
+ * lengths history_len[S] (each <= history_stride; nullable when
+ * rep_window == 0 or rep_penalty <= 1); rng_state[S][4] (host, in/out) is the
+ * per-stream xoshiro256++ state (rng.rs:17-22).  out_tokens[S] host. */
+nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uint32_t *history,
+                            const uint32_t *history_len, uint32_t history_stride,
+                            uint64_t *rng_state, uint32_t *out_tokens);
+
+/* cli.rs:generate (cli.rs:470-518) on token ids for every stream: prefill
+ * each prompt (an empty prompt becomes [10]), then n_new sampled tokens with
+ * a rep_window history, stepping after every token but the last.
+ * rng_state[S][4] in/out; out_tokens[S*n_new] host. */
+nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32_t *lens,
+                              uint32_t max_t, uint32_t n_new, const nk_sample_cfg *cfg,
+                              uint64_t *rng_state, uint32_t *out_tokens);
+
+/* LmState access for streams [first, first+count): state is
+ * [count, n_layer, (conv_k+1)*E] (per layer the conv ring [conv_k, E] then
+ * h [E], infer.rs:12-19), heads[count] the shared conv_head. */
+nk_status nk_decoder_get_state(nk_decoder *dec, uint32_t first, uint32_t count, float *state,
+                               uint32_t *heads);
+nk_status nk_decoder_set_state(nk_decoder *dec, uint32_t first, uint32_t count,
+                               const float *state, const uint32_t *heads);
+
+/* Device-resident greedy step: tokens_in / tokens_out are device u32[S].
+ * One Decoder::step plus sample_token with greedy = true and no repetition
+ * penalty (infer.rs:248-250, tensor.rs:354-365).  Asynchronous on the
+ * decoder's stream. */
+nk_status nk_decoder_step_greedy_device(nk_decoder *dec, const uint32_t *tokens_in,
+                                        uint32_t *tokens_out);
+
+/* Host-buffer greedy step: copies tokens in, steps, copies the argmax
+ * tokens out (synchronous). */
+nk_status nk_decoder_step_greedy(nk_decoder *dec, const uint32_t *tokens_in,
+                                 uint32_t *tokens_out);
+
+/* The decoder's CUDA stream (cudaStream_t) and a wait for it. */
+nk_status nk_decoder_cuda_stream(nk_decoder *dec, void **stream);
+nk_status nk_decoder_sync(nk_decoder *dec);
+
+/* Which projection engine the decoder uses: 0 = automatic (tensor-core
+ * 3xTF32 GEMM where the shape allows it), 1 = f32 CUDA-core kernels only. */
+nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
+
+/* Number of kernels this decoder has launched so far. */
+nk_status nk_decoder_launch_count(const nk_decoder *dec, uint64_t *count);
+
+/* ---------------------------------------------------------------- ops */
+
+/* scan_sequential / scan_chunked (scan.rs:35-57, 98-225):
+ * h[b,t,j] = a[b,t,j] * h[b,t-1,j] + b[b,t,j], h[b,-1,j] = 0, layout
+ * (b*T + t)*D + j.  Host pointers; runs on `device`.  chunked != 0 selects
+ * the time-chunked associative scan. */
+nk_status nk_scan(const float *a, const float *b, float *h, uint64_t batch, uint64_t t,
+                  uint64_t d, int chunked, int device);
+
+/* Same on device pointers, asynchronous on `stream` (cudaStream_t, may be
+ * NULL for the legacy default stream). */
+nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t,
+                         uint64_t d, int chunked, void *stream);
+
+/* sample_token (infer.rs:228-305) on one host logit row, computed on the
+ * device.  logits[vocab] is mutated like the reference (penalised, then
+ * tempered and normalised when not greedy); rng_state[4] in/out. */
+nk_status nk_sample_token(float *logits, uint64_t vocab, const nk_sample_cfg *cfg,
+                          const uint32_t *history, uint64_t n_history, uint64_t *rng_state,
+                          uint32_t *out_token, int device);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NOETIC_GPU_H */

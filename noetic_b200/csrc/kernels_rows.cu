@@ -1,0 +1,539 @@
+// kernels_rows.cu -- per-row and per-channel kernels of the token loop.
+//
+// Decoder state layout in HBM, per layer: [S][k+1][E] f32 -- rows 0..k-1 are
+// the circular conv ring (infer.rs:12-19, [conv_k, inner]) and row k is the
+// recurrent state h.  One conv_head per stream, shared by every layer (all
+// layers advance their head once per token, infer.rs:157).
+
+#include "nk_common.cuh"
+#include "nk_kernels.h"
+
+namespace nk {
+
+namespace {
+
+constexpr int KMAX_UNROLLED = 8;
+constexpr int KMAX = 64;
+
+inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
+
+__global__ void embed_rows_k(const uint32_t *__restrict__ tokens, const float *__restrict__ emb,
+                             float *__restrict__ x, int M, int d, int vocab, int *err) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)M * d) return;
+    const int m = (int)(i / d), j = (int)(i - (int64_t)m * d);
+    uint32_t t = tokens[m];
+    if (t >= (uint32_t)vocab) {
+        if (j == 0) atomicExch(err, 1);
+        t = 0;
+    }
+    x[i] = emb[(size_t)t * d + j];
+}
+
+__global__ void embed_prompt_k(const uint32_t *__restrict__ ids, const uint32_t *__restrict__ lens,
+                               int max_t, int t0, int tc, const float *__restrict__ emb,
+                               float *__restrict__ x, int S, int d, int vocab, int *err) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)S * tc * d) return;
+    const int64_t row = i / d;
+    const int j = (int)(i - row * d);
+    const int s = (int)(row / tc), t = (int)(row - (int64_t)s * tc);
+    uint32_t tok = 0;
+    if (t0 + t < (int)lens[s]) {
+        tok = ids[(size_t)s * max_t + t0 + t];
+        if (tok >= (uint32_t)vocab) {
+            if (j == 0) atomicExch(err, 1);
+            tok = 0;
+        }
+    }
+    x[i] = emb[(size_t)tok * d + j];
+}
+
+// One warp per row.
+__global__ void rmsnorm_k(const float *__restrict__ x, const float *__restrict__ gain, float eps,
+                          float *__restrict__ out, int M, int d) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= M) return;
+    const float *xr = x + (size_t)warp * d;
+    float ms = 0.0f;
+    for (int j = lane; j < d; j += 32) ms = fmaf(xr[j], xr[j], ms);
+    ms = warp_sum(ms);
+    const float r = 1.0f / sqrtf(ms / (float)d + eps);
+    float *orow = out + (size_t)warp * d;
+    for (int j = lane; j < d; j += 32) orow[j] = xr[j] * r * gain[j];
+}
+
+__global__ void advance_heads_k(uint32_t *heads, const uint32_t *adv, int S, int k) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    const uint32_t a = adv ? adv[s] : 1u;
+    heads[s] = (uint32_t)((heads[s] + (uint64_t)a) % (uint32_t)k);
+}
+
+// After a prompt chunk [t0, t0+tc): each stream advanced by its valid count.
+__global__ void advance_heads_prompt_k(uint32_t *heads, const uint32_t *lens, int t0, int tc, int S,
+                                       int k) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= S) return;
+    int nv = (int)lens[s] - t0;
+    nv = nv < 0 ? 0 : (nv > tc ? tc : nv);
+    heads[s] = (uint32_t)((heads[s] + (uint64_t)nv) % (uint32_t)k);
+}
+
+// infer.rs:155-176 for one (stream, channel).
+template <int K>
+__global__ void ssm_decode_k(const float *__restrict__ u, float *__restrict__ state,
+                             const uint32_t *__restrict__ heads, const float *__restrict__ conv_w,
+                             const float *__restrict__ conv_b, float *__restrict__ g, int S, int E,
+                             int k_dyn) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)S * E) return;
+    const int s = (int)(i / E), j = (int)(i - (int64_t)s * E);
+    const int k = K > 0 ? K : k_dyn;
+    const float *ur = u + (size_t)s * 3 * E;
+    float *ring = state + (size_t)s * (k + 1) * E;
+    const uint32_t head = heads[s];
+    const float v = ur[j];
+    ring[(size_t)head * E + j] = v;
+    float sum = conv_b[j];
+    sum = sum + conv_w[j] * v;
+    if (K > 0) {
+#pragma unroll
+        for (int q = 1; q < (K > 0 ? K : 1); ++q) {
+            const uint32_t slot = (head + K - q) % K;
+            sum = sum + conv_w[(size_t)q * E + j] * ring[(size_t)slot * E + j];
+        }
+    } else {
+        for (int q = 1; q < k; ++q) {
+            const uint32_t slot = (head + k - q) % k;
+            sum = sum + conv_w[(size_t)q * E + j] * ring[(size_t)slot * E + j];
+        }
+    }
+    const float value = silu(sum);
+    const float decay = sigmoid(ur[E + j]);
+    float *hp = ring + (size_t)k * E + j;
+    const float h = decay * (*hp) + (1.0f - decay) * value;
+    *hp = h;
+    g[(size_t)s * E + j] = h * silu(ur[2 * E + j]);
+}
+
+// Sequential-in-time prefill of one prompt chunk for one (stream, channel):
+// dwconv (autograd.rs:550-575) continuing from the ring, SiLU, decay, the
+// scan h_t = a_t h_{t-1} + (1 - a_t) v_t (model.rs:156-163), output gate.
+template <int K>
+__global__ void ssm_prefill_seq_k(const float *__restrict__ u, float *__restrict__ state,
+                                  const uint32_t *__restrict__ heads, const uint32_t *__restrict__ lens,
+                                  int t0, int tc, const float *__restrict__ conv_w,
+                                  const float *__restrict__ conv_b, float *__restrict__ y, int S,
+                                  int E, int k_dyn) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)S * E) return;
+    const int s = (int)(i / E), j = (int)(i - (int64_t)s * E);
+    const int k = K > 0 ? K : k_dyn;
+    constexpr int W = K > 0 ? K : KMAX;
+    const int len = (int)lens[s];
+    int nv = len - t0;
+    nv = nv < 0 ? 0 : (nv > tc ? tc : nv);
+    float *ring = state + (size_t)s * (k + 1) * E;
+    const uint32_t head0 = heads[s];
+    float win[W];
+    float w[W];
+    // win[q] = raw v at position (current - q); before the chunk the ring
+    // holds position -1 at head0, -2 at head0-1, ...
+#pragma unroll
+    for (int q = 0; q < W; ++q) {
+        if (q < k) {
+            const uint32_t slot = (head0 + (uint32_t)k - (uint32_t)q) % (uint32_t)k;
+            win[q] = ring[(size_t)slot * E + j];
+            w[q] = conv_w[(size_t)q * E + j];
+        } else {
+            win[q] = 0.0f;
+            w[q] = 0.0f;
+        }
+    }
+    const float bias = conv_b[j];
+    float h = ring[(size_t)k * E + j];
+    const float *ur = u + (size_t)s * tc * 3 * E;
+    float *yr = y + (size_t)s * tc * E;
+    for (int t = 0; t < nv; ++t) {
+        const float *row = ur + (size_t)t * 3 * E;
+        const float v = row[j];
+#pragma unroll
+        for (int q = W - 1; q > 0; --q) win[q] = win[q - 1];
+        win[0] = v;
+        float sum = bias;
+#pragma unroll
+        for (int q = 0; q < W; ++q)
+            if (q < k) sum = sum + w[q] * win[q];
+        const float value = silu(sum);
+        const float decay = sigmoid(row[E + j]);
+        h = decay * h + (1.0f - decay) * value;
+        yr[(size_t)t * E + j] = h * silu(row[2 * E + j]);
+    }
+    for (int t = nv; t < tc; ++t) yr[(size_t)t * E + j] = 0.0f;
+    if (nv > 0) {
+        const uint32_t head1 = (uint32_t)((head0 + (uint64_t)nv) % (uint32_t)k);
+#pragma unroll
+        for (int q = 0; q < W; ++q)
+            if (q < k) {
+                const uint32_t slot = (head1 + (uint32_t)k - (uint32_t)q) % (uint32_t)k;
+                ring[(size_t)slot * E + j] = win[q];
+            }
+        ring[(size_t)k * E + j] = h;
+    }
+}
+
+// ---- time-parallel prefill: blocks of TB positions per (stream, channel)
+constexpr int TB = 64;
+
+__device__ __forceinline__ float raw_v(const float *ur, const float *ring, uint32_t head0, int k,
+                                       int p, int E, int j) {
+    // p >= 0: a position inside the chunk; p < 0: one of the k-1 positions
+    // before it, held in the ring (p = -1 at head0).
+    if (p >= 0) return ur[(size_t)p * 3 * E + j];
+    const uint32_t slot = (uint32_t)(((int)head0 + 1 + p + 2 * k) % k);
+    return ring[(size_t)slot * E + j];
+}
+
+// Pass 1: local scan of one time block from h = 0; writes h_local into y and
+// the block's (decay product, final local h).
+__global__ void ssm_chunk_local_k(const float *__restrict__ u, const float *__restrict__ state,
+                                  const uint32_t *__restrict__ heads, const uint32_t *__restrict__ lens,
+                                  int t0, int tc, const float *__restrict__ conv_w,
+                                  const float *__restrict__ conv_b, float *__restrict__ y,
+                                  float *__restrict__ blkA, float *__restrict__ blkH, int S, int E,
+                                  int k, int nblk) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)S * nblk * E) return;
+    const int j = (int)(i % E);
+    const int64_t sc = i / E;
+    const int c = (int)(sc % nblk), s = (int)(sc / nblk);
+    int nv = (int)lens[s] - t0;
+    nv = nv < 0 ? 0 : (nv > tc ? tc : nv);
+    const int p0 = c * TB, p1 = min(nv, p0 + TB);
+    float A = 1.0f, h = 0.0f;
+    if (p0 < p1) {
+        const float *ur = u + (size_t)s * tc * 3 * E;
+        const float *ring = state + (size_t)s * (k + 1) * E;
+        const uint32_t head0 = heads[s];
+        const float bias = conv_b[j];
+        float *yr = y + (size_t)s * tc * E;
+        for (int p = p0; p < p1; ++p) {
+            float sum = bias;
+            for (int q = 0; q < k; ++q)
+                sum = sum + conv_w[(size_t)q * E + j] * raw_v(ur, ring, head0, k, p - q, E, j);
+            const float value = silu(sum);
+            const float decay = sigmoid(ur[(size_t)p * 3 * E + E + j]);
+            h = decay * h + (1.0f - decay) * value;
+            A = A * decay;
+            yr[(size_t)p * E + j] = h;
+        }
+    }
+    blkA[i] = A;
+    blkH[i] = h;
+}
+
+// Pass 2: compose block maps in order, (A_L, H_L) then (A_R, H_R) ==
+// (A_R A_L, A_R H_L + H_R) (scan.rs:5-8); carry[c] = state entering block c.
+__global__ void ssm_chunk_carry_k(const float *__restrict__ state, const uint32_t *__restrict__ lens,
+                                  int t0, int tc, const float *__restrict__ blkA,
+                                  const float *__restrict__ blkH, float *__restrict__ carry, int S,
+                                  int E, int k, int nblk) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)S * E) return;
+    const int s = (int)(i / E), j = (int)(i - (int64_t)s * E);
+    float c = state[(size_t)s * (k + 1) * E + (size_t)k * E + j];
+    for (int b = 0; b < nblk; ++b) {
+        const size_t o = ((size_t)s * nblk + b) * E + j;
+        carry[o] = c;
+        c = blkA[o] * c + blkH[o];
+    }
+}
+
+// Pass 3: h_t = h_local_t + (prod a) * carry_in, y = h * SiLU(o); the last
+// block of each stream also writes h and the conv ring back to the state.
+__global__ void ssm_chunk_fix_k(const float *__restrict__ u, float *__restrict__ state,
+                                const uint32_t *__restrict__ heads, const uint32_t *__restrict__ lens,
+                                int t0, int tc, float *__restrict__ y, const float *__restrict__ carry,
+                                int S, int E, int k, int nblk) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)S * nblk * E) return;
+    const int j = (int)(i % E);
+    const int64_t sc = i / E;
+    const int c = (int)(sc % nblk), s = (int)(sc / nblk);
+    int nv = (int)lens[s] - t0;
+    nv = nv < 0 ? 0 : (nv > tc ? tc : nv);
+    const int p0 = c * TB, p1 = min(nv, p0 + TB);
+    float *yr = y + (size_t)s * tc * E;
+    if (p0 >= p1) {
+        for (int p = max(p0, nv); p < min(tc, p0 + TB); ++p) yr[(size_t)p * E + j] = 0.0f;
+        return;
+    }
+    const float *ur = u + (size_t)s * tc * 3 * E;
+    const float cin = carry[i];
+    float P = 1.0f, h = 0.0f;
+    for (int p = p0; p < p1; ++p) {
+        const float decay = sigmoid(ur[(size_t)p * 3 * E + E + j]);
+        P = P * decay;
+        h = yr[(size_t)p * E + j] + P * cin;
+        yr[(size_t)p * E + j] = h * silu(ur[(size_t)p * 3 * E + 2 * E + j]);
+    }
+    for (int p = p1; p < min(tc, p0 + TB); ++p) yr[(size_t)p * E + j] = 0.0f;
+    if (p1 == nv) {
+        // Last block holding valid positions: write the state back.
+        float *ring = state + (size_t)s * (k + 1) * E;
+        const uint32_t head0 = heads[s];
+        const uint32_t head1 = (uint32_t)((head0 + (uint64_t)nv) % (uint32_t)k);
+        float win[KMAX];
+        for (int q = 0; q < k; ++q) win[q] = raw_v(ur, ring, head0, k, nv - 1 - q, E, j);
+        for (int q = 0; q < k; ++q) {
+            const uint32_t slot = (head1 + (uint32_t)k - (uint32_t)q) % (uint32_t)k;
+            ring[(size_t)slot * E + j] = win[q];
+        }
+        ring[(size_t)k * E + j] = h;
+    }
+}
+
+__global__ void swiglu_k(const float *__restrict__ up, float *__restrict__ s, int M, int H) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)M * H) return;
+    const int64_t m = i / H;
+    const int j = (int)(i - m * H);
+    const float *r = up + (size_t)m * 2 * H;
+    s[i] = silu(r[j]) * r[H + j];
+}
+
+// Block per row: first index of the maximum over non-NaN entries; 0 when
+// the maximum is -inf or every entry is NaN (tensor.rs:354-365).
+__global__ void argmax_rows_k(const float *__restrict__ x, uint32_t *__restrict__ out, int V) {
+    const float *row = x + (size_t)blockIdx.x * V;
+    float bv = -INFINITY;
+    int bi = V;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = row[i];
+        if (!isnan(v) && (v > bv || (v == bv && i < bi))) {
+            bv = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : V;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) out[blockIdx.x] = (bv == -INFINITY || bi >= V) ? 0u : (uint32_t)bi;
+    }
+}
+
+__global__ void gather_last_k(const float *__restrict__ x, const uint32_t *__restrict__ lens, int t0,
+                              int tc, float *__restrict__ last, int S, int d) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)S * d) return;
+    const int s = (int)(i / d), j = (int)(i - (int64_t)s * d);
+    const int p = (int)lens[s] - 1 - t0;
+    if (p >= 0 && p < tc) last[i] = x[((size_t)s * tc + p) * d + j];
+}
+
+__global__ void gather_rows_k(const float *__restrict__ src, const uint32_t *__restrict__ idx,
+                              float *__restrict__ dst, int n, int d) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n * d) return;
+    const int r = (int)(i / d), j = (int)(i - (int64_t)r * d);
+    dst[i] = src[(size_t)idx[r] * d + j];
+}
+
+__global__ void scatter_rows_k(const float *__restrict__ src, const uint32_t *__restrict__ idx,
+                               float *__restrict__ dst, int n, int d) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n * d) return;
+    const int r = (int)(i / d), j = (int)(i - (int64_t)r * d);
+    dst[(size_t)idx[r] * d + j] = src[i];
+}
+
+__global__ void history_push_k(uint32_t *history, uint32_t *history_len, const uint32_t *tok, int S,
+                               int window) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= S || window <= 0) return;
+    uint32_t *h = history + (size_t)s * window;
+    uint32_t n = history_len[s];
+    if (n < (uint32_t)window) {
+        h[n] = tok[s];
+        history_len[s] = n + 1;
+    } else {
+        for (int i = 0; i + 1 < window; ++i) h[i] = h[i + 1];
+        h[window - 1] = tok[s];
+    }
+}
+
+}  // namespace
+
+cudaError_t embed_rows(const uint32_t *tokens, const float *emb, float *x, int M, int d, int vocab,
+                       int *err, cudaStream_t st) {
+    const int64_t n = (int64_t)M * d;
+    if (n == 0) return cudaSuccess;
+    embed_rows_k<<<blocks_for(n, 256), 256, 0, st>>>(tokens, emb, x, M, d, vocab, err);
+    return cudaGetLastError();
+}
+
+cudaError_t embed_prompt_chunk(const uint32_t *ids, const uint32_t *lens, int max_t, int t0, int tc,
+                               const float *emb, float *x, int S, int d, int vocab, int *err,
+                               cudaStream_t st) {
+    const int64_t n = (int64_t)S * tc * d;
+    if (n == 0) return cudaSuccess;
+    embed_prompt_k<<<blocks_for(n, 256), 256, 0, st>>>(ids, lens, max_t, t0, tc, emb, x, S, d, vocab,
+                                                       err);
+    return cudaGetLastError();
+}
+
+cudaError_t rmsnorm_rows(const float *x, const float *gain, float eps, float *out, int M, int d,
+                         cudaStream_t st) {
+    if (M == 0) return cudaSuccess;
+    rmsnorm_k<<<blocks_for((int64_t)M * 32, 256), 256, 0, st>>>(x, gain, eps, out, M, d);
+    return cudaGetLastError();
+}
+
+cudaError_t advance_heads(uint32_t *heads, const uint32_t *adv, int S, int k, cudaStream_t st) {
+    if (S == 0) return cudaSuccess;
+    advance_heads_k<<<blocks_for(S, 256), 256, 0, st>>>(heads, adv, S, k);
+    return cudaGetLastError();
+}
+
+cudaError_t advance_heads_prompt(uint32_t *heads, const uint32_t *lens, int t0, int tc, int S, int k,
+                                 cudaStream_t st) {
+    if (S == 0) return cudaSuccess;
+    advance_heads_prompt_k<<<blocks_for(S, 256), 256, 0, st>>>(heads, lens, t0, tc, S, k);
+    return cudaGetLastError();
+}
+
+cudaError_t ssm_decode(const float *u, float *state, const uint32_t *heads, const float *conv_w,
+                       const float *conv_b, float *g, int S, int E, int k, cudaStream_t st) {
+    const int64_t n = (int64_t)S * E;
+    if (n == 0) return cudaSuccess;
+    const unsigned grid = blocks_for(n, 256);
+    switch (k) {
+#define NK_CASE(KK) \
+    case KK: ssm_decode_k<KK><<<grid, 256, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k); break;
+        NK_CASE(1) NK_CASE(2) NK_CASE(3) NK_CASE(4) NK_CASE(5) NK_CASE(6) NK_CASE(7) NK_CASE(8)
+#undef NK_CASE
+        default: ssm_decode_k<0><<<grid, 256, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t ssm_prefill_seq(const float *u, float *state, const uint32_t *heads,
+                            const uint32_t *lens, int t0, int tc, const float *conv_w,
+                            const float *conv_b, float *y, int S, int E, int k, cudaStream_t st) {
+    const int64_t n = (int64_t)S * E;
+    if (n == 0) return cudaSuccess;
+    if (k > KMAX) return cudaErrorInvalidValue;
+    const unsigned grid = blocks_for(n, 128);
+    switch (k) {
+#define NK_CASE(KK)                                                                                 \
+    case KK:                                                                                        \
+        ssm_prefill_seq_k<KK><<<grid, 128, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, \
+                                                    y, S, E, k);                                    \
+        break;
+        NK_CASE(1) NK_CASE(2) NK_CASE(3) NK_CASE(4) NK_CASE(5) NK_CASE(6) NK_CASE(7) NK_CASE(8)
+#undef NK_CASE
+        default:
+            ssm_prefill_seq_k<0><<<grid, 128, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b,
+                                                        y, S, E, k);
+    }
+    return cudaGetLastError();
+}
+
+size_t ssm_prefill_chunked_scratch_floats(int S, int E, int tc) {
+    const int nblk = (tc + TB - 1) / TB;
+    return (size_t)3 * S * nblk * E;
+}
+
+cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *heads,
+                                const uint32_t *lens, int t0, int tc, const float *conv_w,
+                                const float *conv_b, float *y, float *scratch, int S, int E, int k,
+                                cudaStream_t st) {
+    if ((int64_t)S * E == 0 || tc == 0) return cudaSuccess;
+    if (k > KMAX) return cudaErrorInvalidValue;
+    const int nblk = (tc + TB - 1) / TB;
+    const size_t per = (size_t)S * nblk * E;
+    float *blkA = scratch, *blkH = scratch + per, *carry = scratch + 2 * per;
+    const int64_t n = (int64_t)per;
+    ssm_chunk_local_k<<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, conv_w,
+                                                          conv_b, y, blkA, blkH, S, E, k, nblk);
+    ssm_chunk_carry_k<<<blocks_for((int64_t)S * E, 128), 128, 0, st>>>(state, lens, t0, tc, blkA,
+                                                                       blkH, carry, S, E, k, nblk);
+    ssm_chunk_fix_k<<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, y, carry, S,
+                                                        E, k, nblk);
+    return cudaGetLastError();
+}
+
+cudaError_t swiglu_rows(const float *up, float *s, int M, int H, cudaStream_t st) {
+    const int64_t n = (int64_t)M * H;
+    if (n == 0) return cudaSuccess;
+    swiglu_k<<<blocks_for(n, 256), 256, 0, st>>>(up, s, M, H);
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_rows(const float *x, uint32_t *out, int M, int V, cudaStream_t st) {
+    if (M == 0) return cudaSuccess;
+    argmax_rows_k<<<M, 256, 0, st>>>(x, out, V);
+    return cudaGetLastError();
+}
+
+cudaError_t gather_last_rows(const float *x, const uint32_t *lens, int t0, int tc, float *last,
+                             int S, int d, cudaStream_t st) {
+    const int64_t n = (int64_t)S * d;
+    if (n == 0) return cudaSuccess;
+    gather_last_k<<<blocks_for(n, 256), 256, 0, st>>>(x, lens, t0, tc, last, S, d);
+    return cudaGetLastError();
+}
+
+cudaError_t gather_rows(const float *src, const uint32_t *idx, float *dst, int n, int d,
+                        cudaStream_t st) {
+    const int64_t t = (int64_t)n * d;
+    if (t == 0) return cudaSuccess;
+    gather_rows_k<<<blocks_for(t, 256), 256, 0, st>>>(src, idx, dst, n, d);
+    return cudaGetLastError();
+}
+
+cudaError_t scatter_rows(const float *src, const uint32_t *idx, float *dst, int n, int d,
+                         cudaStream_t st) {
+    const int64_t t = (int64_t)n * d;
+    if (t == 0) return cudaSuccess;
+    scatter_rows_k<<<blocks_for(t, 256), 256, 0, st>>>(src, idx, dst, n, d);
+    return cudaGetLastError();
+}
+
+cudaError_t history_push(uint32_t *history, uint32_t *history_len, const uint32_t *tok, int S,
+                         int window, cudaStream_t st) {
+    if (S == 0 || window <= 0) return cudaSuccess;
+    history_push_k<<<blocks_for(S, 128), 128, 0, st>>>(history, history_len, tok, S, window);
+    return cudaGetLastError();
+}
+
+}  // namespace nk

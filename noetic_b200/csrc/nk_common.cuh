@@ -1,0 +1,79 @@
+// nk_common.cuh -- device helpers shared by the token-loop kernels.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nk {
+
+// tensor.rs:276-283: the branchy stable sigmoid.  CUDA's expf is used (the
+// reference calls the platform libm expf); results agree within expf's
+// error bound, not bit-for-bit.
+__device__ __forceinline__ float sigmoid(float x) {
+    if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
+    float e = expf(x);
+    return e / (1.0f + e);
+}
+
+__device__ __forceinline__ float silu(float x) { return x * sigmoid(x); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---- xoshiro256++ (rng.rs:46-56), f32_unit (rng.rs:65-67), below (rng.rs:75-90)
+__device__ __forceinline__ uint64_t rotl64(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+
+__device__ __forceinline__ uint64_t xoshiro_next(uint64_t s[4]) {
+    const uint64_t result = rotl64(s[0] + s[3], 23) + s[0];
+    const uint64_t t = s[1] << 17;
+    s[2] ^= s[0];
+    s[3] ^= s[1];
+    s[1] ^= s[2];
+    s[0] ^= s[3];
+    s[2] ^= t;
+    s[3] = rotl64(s[3], 45);
+    return result;
+}
+
+__device__ __forceinline__ float xoshiro_f32_unit(uint64_t s[4]) {
+    return (float)(xoshiro_next(s) >> 40) * (1.0f / 16777216.0f);
+}
+
+// Lemire threshold rejection then modulo.  The expected number of draws is
+// below 2 for every n; the loop is capped (a cap that can only be reached
+// with probability < 2^-64) so that a corrupted state cannot spin forever.
+__device__ __forceinline__ uint64_t xoshiro_below(uint64_t s[4], uint64_t n, int *err) {
+    if (n <= 1) return 0;
+    const uint64_t threshold = (0ull - n) % n;
+    for (int it = 0; it < 64; ++it) {
+        uint64_t r = xoshiro_next(s);
+        if (r >= threshold) return r % n;
+    }
+    if (err) *err = 1;
+    return 0;
+}
+
+// f32::total_cmp as an order-preserving signed integer.
+__device__ __forceinline__ int32_t total_key(float f) {
+    int32_t b = __float_as_int(f);
+    return b ^ (int32_t)((uint32_t)(b >> 31) >> 1);
+}
+
+// 3xTF32 operand split: hi keeps the tf32-representable leading bits
+// (round to nearest, ties away), lo is the exact remainder rounded to tf32.
+__device__ __forceinline__ float tf32_round(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+}  // namespace nk

@@ -1,0 +1,112 @@
+// nk_kernels.h -- host-side launchers of the token-loop kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace nk {
+
+// C[M,N] = (A[M,K] . B[N,K]^T) (+ bias[N]) (R[M,N] + ...).
+struct GemmArgs {
+    const float *A;
+    int lda;
+    const float *B;
+    int ldb;
+    float *C;
+    int ldc;
+    int M, N, K;
+    const float *bias;  // nullable
+    const float *R;     // nullable residual, may alias C
+    int ldr;
+};
+
+constexpr int GEMV_MAX_ROWS = 8;
+
+cudaError_t gemm_nt_simt(const GemmArgs &p, cudaStream_t st);
+
+// ---- elementwise / row kernels (kernels_rows.cu)
+
+// x[m,:] = emb[tokens[m],:]; tokens >= vocab set *err and read row 0.
+cudaError_t embed_rows(const uint32_t *tokens, const float *emb, float *x, int M, int d, int vocab,
+                       int *err, cudaStream_t st);
+
+// Prompt-chunk gather: row (s, t) of x = emb[ids[s*max_t + t0 + t]] for
+// t < tc (rows past a stream's length read token 0 and are ignored).
+cudaError_t embed_prompt_chunk(const uint32_t *ids, const uint32_t *lens, int max_t, int t0, int tc,
+                               const float *emb, float *x, int S, int d, int vocab, int *err,
+                               cudaStream_t st);
+
+// out = x * (1 / sqrt(mean(x^2) + eps)) * gain, per row (tensor.rs:298-312).
+cudaError_t rmsnorm_rows(const float *x, const float *gain, float eps, float *out, int M, int d,
+                         cudaStream_t st);
+
+// heads[s] = (heads[s] + adv[s]) % k, adv == nullptr means +1.
+cudaError_t advance_heads(uint32_t *heads, const uint32_t *adv, int S, int k, cudaStream_t st);
+// heads[s] += clamp(lens[s] - t0, 0, tc) (mod k): a prompt chunk's advance.
+cudaError_t advance_heads_prompt(uint32_t *heads, const uint32_t *lens, int t0, int tc, int S, int k,
+                                 cudaStream_t st);
+
+// One decode step of the recurrent branch for layer state [S][k+1][E]:
+// ring write, causal conv, SiLU, sigmoid decay, h update, output gate
+// (infer.rs:155-176).  heads[] are the already-advanced slots.
+cudaError_t ssm_decode(const float *u, float *state, const uint32_t *heads, const float *conv_w,
+                       const float *conv_b, float *g, int S, int E, int k, cudaStream_t st);
+
+// Prefill of one prompt chunk for layer state [S][k+1][E] (sequential in time
+// per (stream, channel)); y[S*tc, E]; heads[] are the slots at chunk start.
+cudaError_t ssm_prefill_seq(const float *u, float *state, const uint32_t *heads,
+                            const uint32_t *lens, int t0, int tc, const float *conv_w,
+                            const float *conv_b, float *y, int S, int E, int k, cudaStream_t st);
+
+// Same result, time-parallel: local scans over time blocks, carry composition,
+// fix-up (the chunked associative scan of scan.rs:98-225 fused with the conv).
+cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *heads,
+                                const uint32_t *lens, int t0, int tc, const float *conv_w,
+                                const float *conv_b, float *y, float *scratch, int S, int E, int k,
+                                cudaStream_t st);
+size_t ssm_prefill_chunked_scratch_floats(int S, int E, int tc);
+
+// s[m,j] = SiLU(up[m,j]) * up[m,H+j] (infer.rs:188-190).
+cudaError_t swiglu_rows(const float *up, float *s, int M, int H, cudaStream_t st);
+
+// out[m] = argmax(x[m,:]) (tensor.rs:354-365), first strict maximum, NaN skipped.
+cudaError_t argmax_rows(const float *x, uint32_t *out, int M, int V, cudaStream_t st);
+
+// Gather rows x[s*tc + (lens[s]-1-t0)] for streams whose last prompt token lies
+// in [t0, t0+tc) into last[s].
+cudaError_t gather_last_rows(const float *x, const uint32_t *lens, int t0, int tc, float *last,
+                             int S, int d, cudaStream_t st);
+
+// Row gather / scatter by index list.
+cudaError_t gather_rows(const float *src, const uint32_t *idx, float *dst, int n, int d,
+                        cudaStream_t st);
+cudaError_t scatter_rows(const float *src, const uint32_t *idx, float *dst, int n, int d,
+                         cudaStream_t st);
+
+// ---- sampler (sampler.cu): sample_token for every row.
+struct SampleParams {
+    float temperature;
+    uint64_t top_k;
+    float top_p;
+    float rep_penalty;
+    uint64_t rep_window;
+    uint32_t greedy;
+};
+cudaError_t sample_rows(float *logits, int S, int V, SampleParams cfg, const uint32_t *history,
+                        const uint32_t *history_len, int history_stride, uint64_t *rng,
+                        uint32_t *out, int *err, cudaStream_t st);
+int sample_max_vocab();
+
+// History ring maintenance for generate (cli.rs:495-503).
+cudaError_t history_push(uint32_t *history, uint32_t *history_len, const uint32_t *tok, int S,
+                         int window, cudaStream_t st);
+
+// ---- scans (scan.cu)
+cudaError_t scan_sequential(const float *a, const float *b, float *h, int64_t batch, int64_t t,
+                            int64_t d, cudaStream_t st);
+cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch, int64_t t,
+                         int64_t d, float *scratch, cudaStream_t st);
+size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d);
+
+}  // namespace nk

@@ -1,0 +1,1224 @@
+// runtime.cu -- host runtime and C ABI of the B200 token loop.
+//
+// Owns: model parameters (host copy + one device allocation), the seeded
+// initialiser (rng.rs / nn.rs / model.rs), the checkpoint format (ckpt.rs),
+// and the decoder (infer.rs Decoder over S streams, cli.rs generate loop).
+// Every entry point returns nk_status and records a thread-local message.
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/noetic_gpu.h"
+#include "nk_kernels.h"
+#include "nk_tc.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+struct NkError {
+    nk_status code;
+    std::string msg;
+};
+
+[[noreturn]] void fail(nk_status code, const std::string &msg) { throw NkError{code, msg}; }
+
+void cuda_check(cudaError_t e, const char *what) {
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(e == cudaErrorMemoryAllocation ? NK_ERR_OOM : NK_ERR_CUDA,
+             std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+template <class F>
+nk_status guard(F &&f) {
+    try {
+        f();
+        return NK_OK;
+    } catch (const NkError &e) {
+        g_err = e.msg;
+        return e.code;
+    } catch (const std::bad_alloc &) {
+        g_err = "host allocation failed";
+        return NK_ERR_OOM;
+    } catch (const std::exception &e) {
+        g_err = e.what();
+        return NK_ERR_INVALID;
+    }
+}
+
+// ---------------------------------------------------------------- rng.rs
+// splitmix64 (rng.rs:9-15), Rng::new (rng.rs:25-38), xoshiro256++
+// (rng.rs:46-56), f32_unit (rng.rs:65-67), uniform (rng.rs:70-72) and the
+// Marsaglia polar normal with its cached spare (rng.rs:93-109).
+struct HostRng {
+    uint64_t s[4];
+    float spare = 0.0f;
+    bool has_spare = false;
+
+    static uint64_t splitmix(uint64_t &z) {
+        z += 0x9E3779B97F4A7C15ull;
+        uint64_t r = z;
+        r = (r ^ (r >> 30)) * 0xBF58476D1CE4E5B9ull;
+        r = (r ^ (r >> 27)) * 0x94D049BB133111EBull;
+        return r ^ (r >> 31);
+    }
+    explicit HostRng(uint64_t seed) {
+        uint64_t z = seed ^ 0xA0761D6478BD642Full;
+        for (auto &w : s) w = splitmix(z);
+        if (!s[0] && !s[1] && !s[2] && !s[3]) s[0] = 0x9E3779B97F4A7C15ull;
+    }
+    static uint64_t rotl(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+    uint64_t next() {
+        const uint64_t r = rotl(s[0] + s[3], 23) + s[0];
+        const uint64_t t = s[1] << 17;
+        s[2] ^= s[0];
+        s[3] ^= s[1];
+        s[1] ^= s[2];
+        s[0] ^= s[3];
+        s[2] ^= t;
+        s[3] = rotl(s[3], 45);
+        return r;
+    }
+    float unit() { return (float)(next() >> 40) * (1.0f / 16777216.0f); }
+    float uniform(float lo, float hi) { return lo + (hi - lo) * unit(); }
+    float normal() {
+        if (has_spare) {
+            has_spare = false;
+            return spare;
+        }
+        for (;;) {
+            const float u = uniform(-1.0f, 1.0f);
+            const float v = uniform(-1.0f, 1.0f);
+            const float q = u * u + v * v;
+            if (q > 0.0f && q < 1.0f) {
+                const float f = std::sqrt(-2.0f * std::log(q) / q);
+                spare = v * f;
+                has_spare = true;
+                return u * f;
+            }
+        }
+    }
+};
+
+// ---------------------------------------------------------------- config
+std::string config_error(const nk_config &c) {  // model.rs:37-76
+    if (c.vocab == 0) return "vocabulary size must be positive";
+    if (c.vocab > 0xFFFFFFFFull) return "vocabulary exceeds the u32 token-id space";
+    if (c.d_model == 0) return "d_model must be positive";
+    if (c.n_layer == 0) return "n_layer must be positive";
+    if (c.expand == 0) return "expand must be positive";
+    if (c.conv_k == 0) return "conv_k must be positive";
+    if (c.mlp_mult == 0) return "mlp_mult must be positive";
+    if (!std::isfinite(c.eps) || c.eps <= 0.0f) return "RMSNorm epsilon must be finite and positive";
+    if (!std::isfinite(c.tau_max) || c.tau_max < 1.0f) return "tau_max must be finite and at least one";
+    const uint64_t lim = 1ull << 40;
+    if (c.d_model > lim / c.expand || c.d_model > lim / c.mlp_mult || c.vocab > lim / c.d_model)
+        return "model width overflow";
+    return "";
+}
+
+// Sizes this build supports on the device (int indexing inside kernels).
+std::string device_limits_error(const nk_config &c) {
+    const uint64_t d = c.d_model, e = d * c.expand, h = d * c.mlp_mult;
+    if (d > (1u << 16) || e > (1u << 16) || h > (1u << 17)) return "model width exceeds the device kernels' limit";
+    if (c.conv_k > 64) return "conv_k above 64 is not supported by the device kernels";
+    if (c.vocab * d > (1ull << 34)) return "embedding table exceeds the device kernels' limit";
+    return "";
+}
+
+struct Tensor {
+    std::string name;
+    std::vector<uint64_t> shape;
+    std::vector<float> host;
+    size_t dev_off = 0;  // float offset into the device arena
+    uint64_t numel() const {
+        uint64_t n = 1;
+        for (auto d : shape) n *= d;
+        return n;
+    }
+};
+
+struct LayerIx {
+    int n1, in_w, in_b, conv_w, conv_b, out_w, out_b, n2, up_w, up_b, down_w, down_b;
+};
+
+}  // namespace
+
+struct nk_model {
+    nk_config cfg{};
+    int device = 0;
+    std::vector<Tensor> tensors;
+    std::map<std::string, int> by_name;
+    int emb = -1, norm_f = -1;
+    std::vector<LayerIx> layers;
+    float *arena = nullptr;
+    size_t arena_floats = 0;
+    bool dirty = true;
+    nk::TcWeights tc;  // tensor-core operand forms (built with the arena)
+
+    uint64_t d() const { return cfg.d_model; }
+    uint64_t e() const { return cfg.d_model * cfg.expand; }
+    uint64_t hidden() const { return cfg.d_model * cfg.mlp_mult; }
+    uint64_t k() const { return cfg.conv_k; }
+    const float *dp(int id) const { return arena + tensors[id].dev_off; }
+
+    int add(const std::string &name, std::vector<uint64_t> shape) {
+        Tensor t;
+        t.name = name;
+        t.shape = std::move(shape);
+        t.host.assign(t.numel(), 0.0f);
+        tensors.push_back(std::move(t));
+        by_name[name] = (int)tensors.size() - 1;
+        return (int)tensors.size() - 1;
+    }
+
+    // Parameter set in Lm::new creation order (model.rs:183-206,
+    // model.rs:111-146, nn.rs:23-99) -- also the checkpoint order.
+    void build_layout() {
+        const uint64_t d = this->d(), e = this->e(), hd = hidden(), k = this->k();
+        emb = add("emb", {cfg.vocab, d});
+        for (uint64_t l = 0; l < cfg.n_layer; ++l) {
+            const std::string b = "blk" + std::to_string(l);
+            LayerIx L{};
+            L.n1 = add(b + ".n1.gain", {d});
+            L.in_w = add(b + ".ssm.in_proj.w", {3 * e, d});
+            L.in_b = add(b + ".ssm.in_proj.b", {3 * e});
+            L.conv_w = add(b + ".ssm.conv_w", {k, e});
+            L.conv_b = add(b + ".ssm.conv_b", {e});
+            L.out_w = add(b + ".ssm.out_proj.w", {d, e});
+            L.out_b = add(b + ".ssm.out_proj.b", {d});
+            L.n2 = add(b + ".n2.gain", {d});
+            L.up_w = add(b + ".mlp.up.w", {2 * hd, d});
+            L.up_b = add(b + ".mlp.up.b", {2 * hd});
+            L.down_w = add(b + ".mlp.down.w", {d, hd});
+            L.down_b = add(b + ".mlp.down.b", {d});
+            layers.push_back(L);
+        }
+        norm_f = add("norm_f.gain", {d});
+    }
+
+    // Lm::new's draws, in order, from one generator (Appendix of the
+    // reference's model: emb N(0,1)*0.02; per layer in_proj.w, conv taps
+    // q>=1, out_proj.w, up.w, down.w; deterministic gains/biases).
+    void init_random(HostRng &rng) {
+        const uint64_t d = this->d(), e = this->e(), hd = hidden(), k = this->k();
+        for (auto &t : tensors) std::fill(t.host.begin(), t.host.end(), 0.0f);
+        for (auto &x : tensors[emb].host) x = rng.normal() * 0.02f;
+        const float depth_scale = 1.0f / std::sqrt(2.0f * (float)cfg.n_layer);
+        auto init_std = [](uint64_t fan_in) { return std::sqrt(2.0f / (float)std::max<uint64_t>(fan_in, 1)); };
+        auto fill = [&](int id, float sd) {
+            for (auto &x : tensors[id].host) x = rng.normal() * sd;
+        };
+        for (uint64_t l = 0; l < cfg.n_layer; ++l) {
+            const LayerIx &L = layers[l];
+            std::fill(tensors[L.n1].host.begin(), tensors[L.n1].host.end(), 1.0f);
+            fill(L.in_w, init_std(d));
+            float *bias = tensors[L.in_b].host.data();
+            for (uint64_t j = 0; j < e; ++j) {  // model.rs:116-128
+                const float fraction = e > 1 ? (float)j / (float)(e - 1) : 0.0f;
+                const float tau = std::pow(cfg.tau_max, fraction);
+                float decay = std::exp(-1.0f / tau);
+                decay = std::min(std::max(decay, 0.001f), 0.9999f);
+                bias[e + j] = std::log(decay / (1.0f - decay));
+            }
+            float *cw = tensors[L.conv_w].host.data();  // model.rs:130-142
+            for (uint64_t j = 0; j < e; ++j) cw[j] = 1.0f;
+            for (uint64_t q = 1; q < k; ++q)
+                for (uint64_t j = 0; j < e; ++j) cw[q * e + j] = rng.normal() * 0.1f;
+            fill(L.out_w, init_std(e) * depth_scale);
+            std::fill(tensors[L.n2].host.begin(), tensors[L.n2].host.end(), 1.0f);
+            fill(L.up_w, init_std(d));
+            fill(L.down_w, init_std(hd) * depth_scale);
+        }
+        std::fill(tensors[norm_f].host.begin(), tensors[norm_f].host.end(), 1.0f);
+        dirty = true;
+    }
+
+    void upload() {
+        if (!dirty) return;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        if (!arena) {
+            size_t off = 0;
+            for (auto &t : tensors) {
+                t.dev_off = off;
+                off += (t.numel() + 63) & ~size_t(63);  // 256-byte aligned tensors
+            }
+            arena_floats = off;
+            cuda_check(cudaMalloc(&arena, arena_floats * sizeof(float)), "cudaMalloc(weights)");
+        }
+        for (auto &t : tensors)
+            cuda_check(cudaMemcpy(arena + t.dev_off, t.host.data(), t.numel() * sizeof(float),
+                                  cudaMemcpyHostToDevice),
+                       "cudaMemcpy(weights)");
+        nk::tc_weights_free(tc);
+        dirty = false;
+    }
+
+    ~nk_model() {
+        if (arena) {
+            cudaSetDevice(device);
+            cudaFree(arena);
+        }
+        if (device < 0) return;
+        nk::tc_weights_free(tc);
+    }
+};
+
+// ---------------------------------------------------------------- ckpt.rs
+namespace {
+
+const uint8_t MAGIC[8] = {'N', 'O', 'E', 'T', 'I', 'C', 0, 1};
+const uint64_t MAX_CKPT_BYTES = 8ull << 30;
+
+uint32_t crc32(const uint8_t *p, size_t n) {  // ckpt.rs:35-54
+    static uint32_t table[256];
+    static bool ready = false;
+    if (!ready) {
+        for (uint32_t i = 0; i < 256; ++i) {
+            uint32_t c = i;
+            for (int b = 0; b < 8; ++b) c = (c & 1) ? (0xEDB88320u ^ (c >> 1)) : (c >> 1);
+            table[i] = c;
+        }
+        ready = true;
+    }
+    uint32_t crc = 0xFFFFFFFFu;
+    for (size_t i = 0; i < n; ++i) crc = table[(crc ^ p[i]) & 0xFF] ^ (crc >> 8);
+    return crc ^ 0xFFFFFFFFu;
+}
+
+struct CkptData {
+    std::map<std::string, std::string> meta;
+    std::map<std::string, std::pair<std::vector<uint64_t>, std::vector<float>>> tensors;
+};
+
+// ckpt.rs:299-383: every malformed / truncated / duplicate / trailing /
+// inconsistent / non-finite case is rejected before anything is applied.
+CkptData read_ckpt(const char *path) {
+    std::ifstream f(path, std::ios::binary | std::ios::ate);
+    if (!f) fail(NK_ERR_IO, std::string("cannot open checkpoint ") + path);
+    const std::streamoff size = f.tellg();
+    if (size < 0 || (uint64_t)size > MAX_CKPT_BYTES) fail(NK_ERR_IO, "checkpoint file exceeds the supported size limit");
+    if (size < 24) fail(NK_ERR_IO, "checkpoint too small");
+    std::vector<uint8_t> raw((size_t)size);
+    f.seekg(0);
+    f.read((char *)raw.data(), size);
+    if (!f) fail(NK_ERR_IO, "checkpoint read failed");
+    const size_t body = raw.size() - 4;
+    const uint32_t want = raw[body] | (raw[body + 1] << 8) | (raw[body + 2] << 16) | ((uint32_t)raw[body + 3] << 24);
+    if (crc32(raw.data(), body) != want) fail(NK_ERR_IO, "checkpoint CRC mismatch (corrupt file)");
+    size_t off = 0;
+    auto take = [&](size_t n) -> const uint8_t * {
+        if (n > body - off) fail(NK_ERR_IO, "checkpoint truncated");
+        const uint8_t *p = raw.data() + off;
+        off += n;
+        return p;
+    };
+    auto u32 = [&]() -> uint32_t {
+        const uint8_t *p = take(4);
+        return p[0] | (p[1] << 8) | (p[2] << 16) | ((uint32_t)p[3] << 24);
+    };
+    auto str = [&]() {
+        const uint32_t n = u32();
+        const uint8_t *p = take(n);
+        return std::string((const char *)p, n);
+    };
+    if (std::memcmp(take(8), MAGIC, 8) != 0) fail(NK_ERR_IO, "not a noetic checkpoint");
+    if (u32() != 1) fail(NK_ERR_IO, "unsupported checkpoint version");
+    CkptData c;
+    const uint32_t n_meta = u32();
+    if (n_meta > 1000000) fail(NK_ERR_IO, "checkpoint contains too many metadata entries");
+    for (uint32_t i = 0; i < n_meta; ++i) {
+        std::string k = str(), v = str();
+        if (k.empty() || c.meta.count(k)) fail(NK_ERR_IO, "checkpoint metadata contains an empty or duplicate key");
+        c.meta[k] = v;
+    }
+    const uint32_t n_t = u32();
+    if (n_t > 1000000) fail(NK_ERR_IO, "checkpoint contains too many tensors");
+    for (uint32_t i = 0; i < n_t; ++i) {
+        std::string name = str();
+        if (name.empty() || c.tensors.count(name)) fail(NK_ERR_IO, "checkpoint contains an empty or duplicate tensor name");
+        const uint32_t rank = u32();
+        if (rank > 32 || rank > (body - off) / 4) fail(NK_ERR_IO, "checkpoint tensor rank is invalid");
+        std::vector<uint64_t> shape(rank);
+        uint64_t expect = 1;
+        bool overflow = false;
+        for (auto &d : shape) {
+            d = u32();
+            if (d != 0 && expect > UINT64_MAX / d) overflow = true;
+            expect *= d;
+        }
+        const uint32_t numel = u32();
+        if (numel > (body - off) / 4) fail(NK_ERR_IO, "checkpoint tensor payload is truncated");
+        if (overflow || expect != numel) fail(NK_ERR_IO, "checkpoint tensor shape does not match its element count");
+        std::vector<float> v(numel);
+        std::memcpy(v.data(), take(4ull * numel), 4ull * numel);
+        for (float x : v)
+            if (!std::isfinite(x)) fail(NK_ERR_IO, "checkpoint tensor contains a non-finite value");
+        c.tensors[name] = {std::move(shape), std::move(v)};
+    }
+    if (off != body) fail(NK_ERR_IO, "checkpoint has trailing data");
+    return c;
+}
+
+uint64_t meta_usize(const CkptData &c, const char *key) {  // Ckpt::require_usize
+    auto it = c.meta.find(key);
+    if (it == c.meta.end()) fail(NK_ERR_IO, std::string("checkpoint metadata is missing '") + key + "'");
+    const std::string &s = it->second;
+    if (s.empty() || s.find_first_not_of("0123456789") != std::string::npos)
+        fail(NK_ERR_IO, std::string("checkpoint metadata '") + key + "' is not a valid integer");
+    try {
+        return std::stoull(s);
+    } catch (...) {
+        fail(NK_ERR_IO, std::string("checkpoint metadata '") + key + "' is not a valid integer");
+    }
+}
+
+float meta_f32(const CkptData &c, const char *key, bool required, float dflt) {
+    auto it = c.meta.find(key);
+    if (it == c.meta.end()) {
+        if (required) fail(NK_ERR_IO, std::string("checkpoint metadata is missing '") + key + "'");
+        return dflt;
+    }
+    char *end = nullptr;
+    const float v = std::strtof(it->second.c_str(), &end);
+    if (it->second.empty() || *end != 0) fail(NK_ERR_IO, std::string("checkpoint metadata '") + key + "' is not a valid number");
+    if (!std::isfinite(v)) fail(NK_ERR_IO, std::string("checkpoint metadata '") + key + "' must be finite");
+    return v;
+}
+
+void put_u32(std::vector<uint8_t> &b, uint32_t v) {
+    for (int i = 0; i < 4; ++i) b.push_back((uint8_t)(v >> (8 * i)));
+}
+void put_str(std::vector<uint8_t> &b, const std::string &s) {
+    put_u32(b, (uint32_t)s.size());
+    b.insert(b.end(), s.begin(), s.end());
+}
+
+std::string fmt_f32(float v) {
+    char buf[64];
+    std::snprintf(buf, sizeof buf, "%.9g", (double)v);
+    return buf;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- decoder
+struct nk_decoder {
+    nk_model *model = nullptr;
+    uint32_t S = 0;
+    cudaStream_t stream = nullptr;
+    int engine = 0;
+    uint64_t launches = 0;
+
+    float *state = nullptr;  // [L][S][k+1][E]
+    uint32_t *heads = nullptr;
+    float *x = nullptr, *nrm = nullptr, *u = nullptr, *g = nullptr, *logits = nullptr;
+    uint32_t *tok_a = nullptr, *tok_b = nullptr;
+    int *err = nullptr;
+    uint64_t *rng = nullptr;
+    uint32_t *hist = nullptr, *hist_len = nullptr;
+    uint32_t hist_cap = 0;
+    // prefill scratch (grown on demand)
+    float *p_x = nullptr, *p_n = nullptr, *p_u = nullptr, *p_y = nullptr, *p_last = nullptr,
+          *p_scan = nullptr, *p_logits = nullptr;
+    size_t p_rows = 0, p_scan_floats = 0;
+    uint32_t *p_ids = nullptr, *p_lens = nullptr;
+    size_t p_ids_cap = 0;
+    nk::TcScratch tcs;
+
+    uint64_t L() const { return model->cfg.n_layer; }
+    size_t layer_state_floats() const { return (size_t)S * (model->k() + 1) * model->e(); }
+    float *layer_state(uint64_t l) { return state + l * layer_state_floats(); }
+
+    ~nk_decoder() {
+        cudaSetDevice(model->device);
+        if (stream) cudaStreamSynchronize(stream);
+        for (void *p : {(void *)state, (void *)heads, (void *)x, (void *)nrm, (void *)u, (void *)g,
+                        (void *)logits, (void *)tok_a, (void *)tok_b, (void *)err, (void *)rng,
+                        (void *)hist, (void *)hist_len, (void *)p_x, (void *)p_n, (void *)p_u,
+                        (void *)p_y, (void *)p_last, (void *)p_scan, (void *)p_logits, (void *)p_ids,
+                        (void *)p_lens})
+            if (p) cudaFree(p);
+        nk::tc_scratch_free(tcs);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+namespace {
+
+template <class T>
+void dalloc(T **p, size_t n, const char *what) {
+    cuda_check(cudaMalloc((void **)p, std::max<size_t>(n, 1) * sizeof(T)), what);
+}
+
+void launch_ok(nk_decoder *dec, cudaError_t e, const char *what, int count = 1) {
+    cuda_check(e, what);
+    dec->launches += (uint64_t)count;
+}
+
+// One projection: tensor-core 3xTF32 GEMM when eligible, else the f32
+// CUDA-core kernels.
+void project(nk_decoder *dec, const float *A, int M, int K, const float *W, const nk::TcOperand *Wtc,
+             int N, const float *bias, float *C, const float *R) {
+    nk::GemmArgs p{A, K, W, K, C, N, M, N, K, bias, R, N};
+    if (!(dec->engine & 1) && Wtc && nk::tc_eligible(M, N, K)) {
+        int launches = 0;
+        cuda_check(nk::tc_gemm(p, *Wtc, dec->tcs, dec->stream, &launches), "tcgen05 projection");
+        dec->launches += (uint64_t)launches;
+        return;
+    }
+    launch_ok(dec, nk::gemm_nt_simt(p, dec->stream), "f32 projection");
+}
+
+void ensure_ready(nk_decoder *dec) {
+    nk_model *m = dec->model;
+    cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
+    if (m->dirty) {
+        cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        m->upload();
+    }
+    if (!(dec->engine & 1) && !m->tc.ready) {
+        std::vector<nk::TcSource> srcs;
+        for (const LayerIx &L : m->layers) {
+            srcs.push_back({m->dp(L.in_w), (int)(3 * m->e()), (int)m->d()});
+            srcs.push_back({m->dp(L.out_w), (int)m->d(), (int)m->e()});
+            srcs.push_back({m->dp(L.up_w), (int)(2 * m->hidden()), (int)m->d()});
+            srcs.push_back({m->dp(L.down_w), (int)m->d(), (int)m->hidden()});
+        }
+        srcs.push_back({m->dp(m->emb), (int)m->cfg.vocab, (int)m->d()});
+        cuda_check(nk::tc_weights_build(m->tc, srcs), "tensor-core weight split");
+    }
+}
+
+const nk::TcOperand *tc_op(nk_model *m, size_t i) { return m->tc.ready ? &m->tc.ops[i] : nullptr; }
+
+void check_err_flag(nk_decoder *dec) {
+    int h = 0;
+    cuda_check(cudaMemcpyAsync(&h, dec->err, sizeof(int), cudaMemcpyDeviceToHost, dec->stream), "read error flag");
+    cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+    if (h) {
+        cuda_check(cudaMemsetAsync(dec->err, 0, sizeof(int), dec->stream), "clear error flag");
+        cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+        fail(NK_ERR_DEVICE, "a kernel reported an invalid token id or a failed bounded draw");
+    }
+}
+
+// Decoder::step over every stream (infer.rs:106-200), tokens on the device.
+void step_device(nk_decoder *dec, const uint32_t *tokens) {
+    nk_model *m = dec->model;
+    const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(),
+              k = (int)m->k(), V = (int)m->cfg.vocab;
+    cudaStream_t st = dec->stream;
+    launch_ok(dec, nk::embed_rows(tokens, m->dp(m->emb), dec->x, S, d, V, dec->err, st), "embed");
+    launch_ok(dec, nk::advance_heads(dec->heads, nullptr, S, k, st), "advance heads");
+    for (uint64_t l = 0; l < m->cfg.n_layer; ++l) {
+        const LayerIx &L = m->layers[l];
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n1), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
+        project(dec, dec->nrm, S, d, m->dp(L.in_w), tc_op(m, 4 * l + 0), 3 * E, m->dp(L.in_b), dec->u, nullptr);
+        launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w),
+                                      m->dp(L.conv_b), dec->g, S, E, k, st), "ssm step");
+        project(dec, dec->g, S, E, m->dp(L.out_w), tc_op(m, 4 * l + 1), d, m->dp(L.out_b), dec->x, dec->x);
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n2), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
+        project(dec, dec->nrm, S, d, m->dp(L.up_w), tc_op(m, 4 * l + 2), 2 * H, m->dp(L.up_b), dec->u, nullptr);
+        launch_ok(dec, nk::swiglu_rows(dec->u, dec->g, S, H, st), "swiglu");
+        project(dec, dec->g, S, H, m->dp(L.down_w), tc_op(m, 4 * l + 3), d, m->dp(L.down_b), dec->x, dec->x);
+    }
+    launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
+    project(dec, dec->nrm, S, d, m->dp(m->emb), tc_op(m, 4 * m->cfg.n_layer), V, nullptr, dec->logits, nullptr);
+}
+
+void validate_tokens(const nk_model *m, const uint32_t *t, size_t n) {
+    for (size_t i = 0; i < n; ++i)
+        if (t[i] >= m->cfg.vocab) fail(NK_ERR_INVALID, "streaming token is outside the vocabulary");
+}
+
+// The prompt loop as a chunked scan (model.rs:148-165 over each prompt,
+// continuing from the current LmState).  ids/lens already on the device.
+void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_lens,
+                    const std::vector<uint32_t> &lens, uint32_t max_t, float *last_logits_host) {
+    nk_model *m = dec->model;
+    const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(),
+              k = (int)m->k(), V = (int)m->cfg.vocab;
+    cudaStream_t st = dec->stream;
+    if (max_t == 0) return;
+    // Rows per chunk: bounded scratch (about 3 GiB at most).
+    const size_t row_bytes = 4 * (2 * (size_t)d + std::max(3 * (size_t)E, 2 * (size_t)H) + std::max((size_t)E, (size_t)H));
+    size_t rows_budget = std::max<size_t>((size_t)3 << 30, 0) / row_bytes;
+    rows_budget = std::min<size_t>(std::max<size_t>(rows_budget, (size_t)S), (size_t)1 << 20);
+    int tc = (int)std::max<size_t>(1, std::min<size_t>(max_t, rows_budget / (size_t)S));
+    const size_t rows = (size_t)S * tc;
+    if (rows > dec->p_rows) {
+        for (float **p : {&dec->p_x, &dec->p_n, &dec->p_u, &dec->p_y})
+            if (*p) cudaFree(*p), *p = nullptr;
+        dalloc(&dec->p_x, rows * d, "prefill x");
+        dalloc(&dec->p_n, rows * d, "prefill norm");
+        dalloc(&dec->p_u, rows * std::max(3 * E, 2 * H), "prefill projection");
+        dalloc(&dec->p_y, rows * std::max(E, H), "prefill gated");
+        dec->p_rows = rows;
+    }
+    if (!dec->p_last) dalloc(&dec->p_last, (size_t)S * d, "prefill last rows");
+    // Time-parallel scan when streams x channels cannot fill the GPU.
+    bool chunked = (size_t)S * E < 148 * 512 && tc > 64;
+    if (dec->engine & 2) chunked = true;
+    if (dec->engine & 4) chunked = false;
+    if (chunked) {
+        const size_t need = nk::ssm_prefill_chunked_scratch_floats(S, E, tc);
+        if (need > dec->p_scan_floats) {
+            if (dec->p_scan) cudaFree(dec->p_scan), dec->p_scan = nullptr;
+            dalloc(&dec->p_scan, need, "prefill scan scratch");
+            dec->p_scan_floats = need;
+        }
+    }
+    for (uint32_t t0 = 0; t0 < max_t; t0 += tc) {
+        const int tcc = (int)std::min<uint32_t>(tc, max_t - t0);
+        const int R = S * tcc;
+        launch_ok(dec, nk::embed_prompt_chunk(d_ids, d_lens, (int)max_t, (int)t0, tcc, m->dp(m->emb),
+                                              dec->p_x, S, d, V, dec->err, st), "prompt embed");
+        for (uint64_t l = 0; l < m->cfg.n_layer; ++l) {
+            const LayerIx &L = m->layers[l];
+            launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n1), m->cfg.eps, dec->p_n, R, d, st), "rmsnorm");
+            project(dec, dec->p_n, R, d, m->dp(L.in_w), tc_op(m, 4 * l + 0), 3 * E, m->dp(L.in_b), dec->p_u, nullptr);
+            if (chunked)
+                launch_ok(dec, nk::ssm_prefill_chunked(dec->p_u, dec->layer_state(l), dec->heads, d_lens,
+                                                       (int)t0, tcc, m->dp(L.conv_w), m->dp(L.conv_b),
+                                                       dec->p_y, dec->p_scan, S, E, k, st),
+                          "prefill scan", 3);
+            else
+                launch_ok(dec, nk::ssm_prefill_seq(dec->p_u, dec->layer_state(l), dec->heads, d_lens,
+                                                   (int)t0, tcc, m->dp(L.conv_w), m->dp(L.conv_b),
+                                                   dec->p_y, S, E, k, st),
+                          "prefill scan");
+            project(dec, dec->p_y, R, E, m->dp(L.out_w), tc_op(m, 4 * l + 1), d, m->dp(L.out_b), dec->p_x, dec->p_x);
+            launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n2), m->cfg.eps, dec->p_n, R, d, st), "rmsnorm");
+            project(dec, dec->p_n, R, d, m->dp(L.up_w), tc_op(m, 4 * l + 2), 2 * H, m->dp(L.up_b), dec->p_u, nullptr);
+            launch_ok(dec, nk::swiglu_rows(dec->p_u, dec->p_y, R, H, st), "swiglu");
+            project(dec, dec->p_y, R, H, m->dp(L.down_w), tc_op(m, 4 * l + 3), d, m->dp(L.down_b), dec->p_x, dec->p_x);
+        }
+        launch_ok(dec, nk::gather_last_rows(dec->p_x, d_lens, (int)t0, tcc, dec->p_last, S, d, st), "gather last");
+        launch_ok(dec, nk::advance_heads_prompt(dec->heads, d_lens, (int)t0, tcc, S, k, st), "advance heads");
+    }
+    // Final norm + tied logits at each stream's last prompt position.
+    std::vector<uint32_t> live;
+    for (int s = 0; s < S; ++s)
+        if (lens[s] > 0) live.push_back((uint32_t)s);
+    if (live.empty()) return;
+    if ((int)live.size() == S) {
+        launch_ok(dec, nk::rmsnorm_rows(dec->p_last, m->dp(m->norm_f), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
+        project(dec, dec->nrm, S, d, m->dp(m->emb), tc_op(m, 4 * m->cfg.n_layer), V, nullptr, dec->logits, nullptr);
+    } else {
+        const int n = (int)live.size();
+        uint32_t *d_idx = dec->tok_b;  // S u32 of scratch
+        cuda_check(cudaMemcpyAsync(d_idx, live.data(), n * sizeof(uint32_t), cudaMemcpyHostToDevice, st), "upload index");
+        launch_ok(dec, nk::gather_rows(dec->p_last, d_idx, dec->x, n, d, st), "gather");
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, dec->nrm, n, d, st), "rmsnorm");
+        if (!dec->p_logits) dalloc(&dec->p_logits, (size_t)S * V, "compacted logits");
+        project(dec, dec->nrm, n, d, m->dp(m->emb), tc_op(m, 4 * m->cfg.n_layer), V, nullptr, dec->p_logits, nullptr);
+        launch_ok(dec, nk::scatter_rows(dec->p_logits, d_idx, dec->logits, n, V, st), "scatter");
+        cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+    }
+    if (last_logits_host)
+        cuda_check(cudaMemcpyAsync(last_logits_host, dec->logits, (size_t)S * V * sizeof(float),
+                                   cudaMemcpyDeviceToHost, st), "download logits");
+}
+
+void upload_prompts(nk_decoder *dec, const uint32_t *ids, const uint32_t *lens, uint32_t max_t) {
+    const size_t n = (size_t)dec->S * max_t;
+    if (n > dec->p_ids_cap) {
+        if (dec->p_ids) cudaFree(dec->p_ids), dec->p_ids = nullptr;
+        dalloc(&dec->p_ids, n, "prompt ids");
+        dec->p_ids_cap = n;
+    }
+    if (!dec->p_lens) dalloc(&dec->p_lens, dec->S, "prompt lengths");
+    if (n) cuda_check(cudaMemcpyAsync(dec->p_ids, ids, n * sizeof(uint32_t), cudaMemcpyHostToDevice, dec->stream), "upload ids");
+    cuda_check(cudaMemcpyAsync(dec->p_lens, lens, dec->S * sizeof(uint32_t), cudaMemcpyHostToDevice, dec->stream), "upload lens");
+}
+
+void ensure_history(nk_decoder *dec, uint32_t window) {
+    if (window <= dec->hist_cap && dec->hist) return;
+    if (dec->hist) cudaFree(dec->hist), dec->hist = nullptr;
+    dalloc(&dec->hist, (size_t)dec->S * std::max<uint32_t>(window, 1), "history");
+    if (!dec->hist_len) dalloc(&dec->hist_len, dec->S, "history lengths");
+    dec->hist_cap = std::max<uint32_t>(window, 1);
+}
+
+nk::SampleParams to_params(const nk_sample_cfg &c) {
+    return nk::SampleParams{c.temperature, c.top_k, c.top_p, c.rep_penalty, c.rep_window, c.greedy};
+}
+
+void check_sample_cfg(const nk_model *m, const nk_sample_cfg &c) {
+    if (!c.greedy && m->cfg.vocab > (uint64_t)nk::sample_max_vocab())
+        fail(NK_ERR_UNSUPPORTED, "stochastic sampling is limited to vocab <= " + std::to_string(nk::sample_max_vocab()));
+}
+
+}  // namespace
+
+// ================================================================ C ABI
+extern "C" {
+
+const char *nk_last_error(void) { return g_err.c_str(); }
+
+nk_status nk_device_count(int *count) {
+    return guard([&] {
+        if (!count) fail(NK_ERR_INVALID, "null output");
+        cuda_check(cudaGetDeviceCount(count), "cudaGetDeviceCount");
+    });
+}
+
+nk_status nk_config_check(const nk_config *cfg) {
+    return guard([&] {
+        if (!cfg) fail(NK_ERR_INVALID, "null config");
+        std::string e = config_error(*cfg);
+        if (!e.empty()) fail(NK_ERR_INVALID, e);
+    });
+}
+
+nk_status nk_model_create(const nk_config *cfg, int device, nk_model **out) {
+    return guard([&] {
+        if (!cfg || !out) fail(NK_ERR_INVALID, "null argument");
+        *out = nullptr;
+        std::string e = config_error(*cfg);
+        if (!e.empty()) fail(NK_ERR_INVALID, e);
+        e = device_limits_error(*cfg);
+        if (!e.empty()) fail(NK_ERR_UNSUPPORTED, e);
+        if (device != -1) {  // -1: host-only model (init, checkpoint I/O)
+            int n = 0;
+            cuda_check(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+            if (device < 0 || device >= n) fail(NK_ERR_INVALID, "device index out of range");
+        }
+        auto m = std::make_unique<nk_model>();
+        m->cfg = *cfg;
+        m->device = device;
+        m->build_layout();
+        *out = m.release();
+    });
+}
+
+nk_status nk_model_destroy(nk_model *model) {
+    return guard([&] { delete model; });
+}
+
+nk_status nk_model_config(const nk_model *model, nk_config *out) {
+    return guard([&] {
+        if (!model || !out) fail(NK_ERR_INVALID, "null argument");
+        *out = model->cfg;
+    });
+}
+
+nk_status nk_model_init_random(nk_model *model, uint64_t seed, uint64_t rng_after[4]) {
+    return guard([&] {
+        if (!model) fail(NK_ERR_INVALID, "null model");
+        HostRng rng(seed);
+        model->init_random(rng);
+        if (rng_after)
+            for (int i = 0; i < 4; ++i) rng_after[i] = rng.s[i];
+    });
+}
+
+nk_status nk_model_tensor_count(const nk_model *model, uint64_t *count) {
+    return guard([&] {
+        if (!model || !count) fail(NK_ERR_INVALID, "null argument");
+        *count = model->tensors.size();
+    });
+}
+
+nk_status nk_model_tensor_info(const nk_model *model, uint64_t index, const char **name,
+                               uint32_t *rank, uint64_t shape[4]) {
+    return guard([&] {
+        if (!model) fail(NK_ERR_INVALID, "null model");
+        if (index >= model->tensors.size()) fail(NK_ERR_INVALID, "tensor index out of range");
+        const Tensor &t = model->tensors[index];
+        if (name) *name = t.name.c_str();
+        if (rank) *rank = (uint32_t)t.shape.size();
+        if (shape)
+            for (size_t i = 0; i < 4; ++i) shape[i] = i < t.shape.size() ? t.shape[i] : 0;
+    });
+}
+
+nk_status nk_model_set_tensor(nk_model *model, const char *name, const float *data,
+                              const uint64_t *shape, uint32_t rank) {
+    return guard([&] {
+        if (!model || !name || (!data) || (!shape && rank)) fail(NK_ERR_INVALID, "null argument");
+        auto it = model->by_name.find(name);
+        if (it == model->by_name.end()) fail(NK_ERR_INVALID, std::string("unknown tensor '") + name + "'");
+        Tensor &t = model->tensors[it->second];
+        if (rank != t.shape.size() || !std::equal(t.shape.begin(), t.shape.end(), shape))
+            fail(NK_ERR_INVALID, std::string("tensor '") + name + "' has the wrong shape");
+        const uint64_t n = t.numel();
+        for (uint64_t i = 0; i < n; ++i)
+            if (!std::isfinite(data[i])) fail(NK_ERR_INVALID, std::string("tensor '") + name + "' contains a non-finite value");
+        std::memcpy(t.host.data(), data, n * sizeof(float));
+        model->dirty = true;
+    });
+}
+
+nk_status nk_model_get_tensor(const nk_model *model, const char *name, float *out, uint64_t numel) {
+    return guard([&] {
+        if (!model || !name || !out) fail(NK_ERR_INVALID, "null argument");
+        auto it = model->by_name.find(name);
+        if (it == model->by_name.end()) fail(NK_ERR_INVALID, std::string("unknown tensor '") + name + "'");
+        const Tensor &t = model->tensors[it->second];
+        if (numel != t.numel()) fail(NK_ERR_INVALID, "wrong element count");
+        std::memcpy(out, t.host.data(), numel * sizeof(float));
+    });
+}
+
+nk_status nk_model_load_ckpt(const char *path, int device, nk_model **out) {
+    return guard([&] {
+        if (!path || !out) fail(NK_ERR_INVALID, "null argument");
+        *out = nullptr;
+        CkptData c = read_ckpt(path);
+        nk_config cfg{};  // cmd_gen's metadata rules (cli.rs:909-920)
+        cfg.vocab = meta_usize(c, "vocab");
+        cfg.d_model = meta_usize(c, "d_model");
+        cfg.n_layer = meta_usize(c, "n_layer");
+        cfg.expand = meta_usize(c, "expand");
+        cfg.conv_k = meta_usize(c, "conv_k");
+        cfg.mlp_mult = meta_usize(c, "mlp_mult");
+        cfg.eps = meta_f32(c, "eps", false, 1e-5f);
+        cfg.tau_max = meta_f32(c, "tau_max", true, 0.0f);
+        std::string e = config_error(cfg);
+        if (!e.empty()) fail(NK_ERR_IO, "checkpoint model configuration is invalid: " + e);
+        nk_model *m = nullptr;
+        nk_status st = nk_model_create(&cfg, device, &m);
+        if (st != NK_OK) fail(st, g_err);
+        std::unique_ptr<nk_model> own(m);
+        // apply_exact (ckpt.rs:410-436): exact model tensor set, aux.* ignored.
+        size_t model_tensors = 0;
+        for (auto &kv : c.tensors)
+            if (kv.first.rfind("aux.", 0) != 0) ++model_tensors;
+        if (model_tensors != own->tensors.size()) fail(NK_ERR_IO, "checkpoint tensor set does not exactly match the model");
+        for (auto &t : own->tensors) {
+            auto it = c.tensors.find(t.name);
+            if (it == c.tensors.end()) fail(NK_ERR_IO, "checkpoint is missing tensor '" + t.name + "'");
+            if (it->second.first != t.shape) fail(NK_ERR_IO, "checkpoint tensor '" + t.name + "' has the wrong shape");
+        }
+        for (auto &t : own->tensors) t.host = std::move(c.tensors[t.name].second);
+        own->dirty = true;
+        *out = own.release();
+    });
+}
+
+nk_status nk_model_save_ckpt(const nk_model *model, const char *path) {
+    return guard([&] {
+        if (!model || !path) fail(NK_ERR_INVALID, "null argument");
+        const nk_config &c = model->cfg;
+        std::vector<std::pair<std::string, std::string>> meta = {
+            {"vocab", std::to_string(c.vocab)},       {"d_model", std::to_string(c.d_model)},
+            {"n_layer", std::to_string(c.n_layer)},   {"expand", std::to_string(c.expand)},
+            {"conv_k", std::to_string(c.conv_k)},     {"mlp_mult", std::to_string(c.mlp_mult)},
+            {"eps", fmt_f32(c.eps)},                  {"tau_max", fmt_f32(c.tau_max)}};
+        std::vector<uint8_t> b;
+        b.insert(b.end(), MAGIC, MAGIC + 8);
+        put_u32(b, 1);
+        put_u32(b, (uint32_t)meta.size());
+        for (auto &kv : meta) {
+            put_str(b, kv.first);
+            put_str(b, kv.second);
+        }
+        put_u32(b, (uint32_t)model->tensors.size());
+        for (const Tensor &t : model->tensors) {
+            put_str(b, t.name);
+            put_u32(b, (uint32_t)t.shape.size());
+            for (auto dmn : t.shape) put_u32(b, (uint32_t)dmn);
+            put_u32(b, (uint32_t)t.numel());
+            const size_t off = b.size();
+            b.resize(off + 4 * t.numel());
+            std::memcpy(b.data() + off, t.host.data(), 4 * t.numel());
+        }
+        put_u32(b, crc32(b.data(), b.size()));
+        const std::string tmp = std::string(path) + ".tmp";
+        {
+            std::ofstream f(tmp, std::ios::binary);
+            if (!f) fail(NK_ERR_IO, "cannot open checkpoint for writing");
+            f.write((const char *)b.data(), (std::streamsize)b.size());
+            if (!f) fail(NK_ERR_IO, "checkpoint write failed");
+        }
+        if (std::rename(tmp.c_str(), path) != 0) fail(NK_ERR_IO, "checkpoint rename failed");
+    });
+}
+
+nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **out) {
+    return guard([&] {
+        if (!model || !out) fail(NK_ERR_INVALID, "null argument");
+        if (n_streams == 0) fail(NK_ERR_INVALID, "n_streams must be positive");
+        if (model->device < 0) fail(NK_ERR_INVALID, "a host-only model (device -1) cannot run a decoder");
+        *out = nullptr;
+        cuda_check(cudaSetDevice(model->device), "cudaSetDevice");
+        auto dec = std::make_unique<nk_decoder>();
+        dec->model = model;
+        dec->S = n_streams;
+        cuda_check(cudaStreamCreateWithFlags(&dec->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+        const size_t S = n_streams, d = model->d(), E = model->e(), H = model->hidden(), V = model->cfg.vocab;
+        const size_t state_floats = model->cfg.n_layer * S * (model->k() + 1) * E;
+        if ((double)S * V > 2.0e9 || (double)S * std::max(3 * E, 2 * H) > 2.0e9)
+            fail(NK_ERR_UNSUPPORTED, "streams x vocabulary exceeds the decoder's logit buffer limit");
+        dalloc(&dec->state, state_floats, "decoder state");
+        dalloc(&dec->heads, S, "heads");
+        dalloc(&dec->x, S * d, "x");
+        dalloc(&dec->nrm, S * d, "norm");
+        dalloc(&dec->u, S * std::max(3 * E, 2 * H), "projection");
+        dalloc(&dec->g, S * std::max(E, H), "gated");
+        dalloc(&dec->logits, S * V, "logits");
+        dalloc(&dec->tok_a, S, "tokens");
+        dalloc(&dec->tok_b, S, "tokens");
+        dalloc(&dec->err, 1, "error flag");
+        dalloc(&dec->rng, S * 4, "rng");
+        cuda_check(cudaMemset(dec->err, 0, sizeof(int)), "memset");
+        cuda_check(cudaMemset(dec->logits, 0, S * V * sizeof(float)), "memset");
+        *out = dec.release();
+        nk_status st = nk_decoder_reset(*out, 0, n_streams);
+        if (st != NK_OK) {
+            delete *out;
+            *out = nullptr;
+            fail(st, g_err);
+        }
+    });
+}
+
+nk_status nk_decoder_destroy(nk_decoder *dec) {
+    return guard([&] { delete dec; });
+}
+
+nk_status nk_decoder_streams(const nk_decoder *dec, uint32_t *n) {
+    return guard([&] {
+        if (!dec || !n) fail(NK_ERR_INVALID, "null argument");
+        *n = dec->S;
+    });
+}
+
+nk_status nk_decoder_reset(nk_decoder *dec, uint32_t first, uint32_t count) {
+    return guard([&] {
+        if (!dec) fail(NK_ERR_INVALID, "null decoder");
+        if ((uint64_t)first + count > dec->S) fail(NK_ERR_INVALID, "stream range out of bounds");
+        cuda_check(cudaSetDevice(dec->model->device), "cudaSetDevice");
+        const size_t per = (dec->model->k() + 1) * dec->model->e();
+        for (uint64_t l = 0; l < dec->L(); ++l)
+            cuda_check(cudaMemsetAsync(dec->layer_state(l) + (size_t)first * per, 0,
+                                       (size_t)count * per * sizeof(float), dec->stream), "reset state");
+        std::vector<uint32_t> h(count, (uint32_t)(dec->model->k() - 1));  // infer.rs:32, 42
+        cuda_check(cudaMemcpyAsync(dec->heads + first, h.data(), count * sizeof(uint32_t),
+                                   cudaMemcpyHostToDevice, dec->stream), "reset heads");
+        cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+    });
+}
+
+nk_status nk_decoder_step(nk_decoder *dec, const uint32_t *tokens, float *logits_out) {
+    return guard([&] {
+        if (!dec || !tokens) fail(NK_ERR_INVALID, "null argument");
+        validate_tokens(dec->model, tokens, dec->S);
+        ensure_ready(dec);
+        cuda_check(cudaMemcpyAsync(dec->tok_a, tokens, dec->S * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                   dec->stream), "upload tokens");
+        step_device(dec, dec->tok_a);
+        if (logits_out)
+            cuda_check(cudaMemcpyAsync(logits_out, dec->logits, (size_t)dec->S * dec->model->cfg.vocab * sizeof(float),
+                                       cudaMemcpyDeviceToHost, dec->stream), "download logits");
+        check_err_flag(dec);
+    });
+}
+
+nk_status nk_decoder_step_greedy_device(nk_decoder *dec, const uint32_t *tokens_in, uint32_t *tokens_out) {
+    return guard([&] {
+        if (!dec || !tokens_in || !tokens_out) fail(NK_ERR_INVALID, "null argument");
+        ensure_ready(dec);
+        step_device(dec, tokens_in);
+        launch_ok(dec, nk::argmax_rows(dec->logits, tokens_out, (int)dec->S, (int)dec->model->cfg.vocab, dec->stream),
+                  "argmax");
+    });
+}
+
+nk_status nk_decoder_step_greedy(nk_decoder *dec, const uint32_t *tokens_in, uint32_t *tokens_out) {
+    return guard([&] {
+        if (!dec || !tokens_in || !tokens_out) fail(NK_ERR_INVALID, "null argument");
+        validate_tokens(dec->model, tokens_in, dec->S);
+        ensure_ready(dec);
+        cuda_check(cudaMemcpyAsync(dec->tok_a, tokens_in, dec->S * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                   dec->stream), "upload tokens");
+        step_device(dec, dec->tok_a);
+        launch_ok(dec, nk::argmax_rows(dec->logits, dec->tok_b, (int)dec->S, (int)dec->model->cfg.vocab, dec->stream),
+                  "argmax");
+        cuda_check(cudaMemcpyAsync(tokens_out, dec->tok_b, dec->S * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                   dec->stream), "download tokens");
+        check_err_flag(dec);
+    });
+}
+
+nk_status nk_decoder_prefill(nk_decoder *dec, const uint32_t *ids, const uint32_t *lens, uint32_t max_t,
+                             float *last_logits) {
+    return guard([&] {
+        if (!dec || !lens || (!ids && max_t)) fail(NK_ERR_INVALID, "null argument");
+        std::vector<uint32_t> lv(lens, lens + dec->S);
+        for (uint32_t s = 0; s < dec->S; ++s) {
+            if (lv[s] > max_t) fail(NK_ERR_INVALID, "prompt length exceeds max_t");
+            validate_tokens(dec->model, ids + (size_t)s * max_t, lv[s]);
+        }
+        ensure_ready(dec);
+        upload_prompts(dec, ids, lens, max_t);
+        prefill_device(dec, dec->p_ids, dec->p_lens, lv, max_t, last_logits);
+        check_err_flag(dec);
+    });
+}
+
+nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uint32_t *history,
+                            const uint32_t *history_len, uint32_t history_stride, uint64_t *rng_state,
+                            uint32_t *out_tokens) {
+    return guard([&] {
+        if (!dec || !cfg || !rng_state || !out_tokens) fail(NK_ERR_INVALID, "null argument");
+        check_sample_cfg(dec->model, *cfg);
+        ensure_ready(dec);
+        const bool use_hist = history && history_len && history_stride > 0;
+        if (use_hist) {
+            for (uint32_t s = 0; s < dec->S; ++s)
+                if (history_len[s] > history_stride) fail(NK_ERR_INVALID, "history length exceeds its stride");
+            ensure_history(dec, history_stride);
+            cuda_check(cudaMemcpyAsync(dec->hist, history, (size_t)dec->S * history_stride * sizeof(uint32_t),
+                                       cudaMemcpyHostToDevice, dec->stream), "upload history");
+            cuda_check(cudaMemcpyAsync(dec->hist_len, history_len, dec->S * sizeof(uint32_t),
+                                       cudaMemcpyHostToDevice, dec->stream), "upload history lengths");
+        }
+        cuda_check(cudaMemcpyAsync(dec->rng, rng_state, (size_t)dec->S * 4 * sizeof(uint64_t),
+                                   cudaMemcpyHostToDevice, dec->stream), "upload rng");
+        launch_ok(dec, nk::sample_rows(dec->logits, (int)dec->S, (int)dec->model->cfg.vocab, to_params(*cfg),
+                                       use_hist ? dec->hist : nullptr, use_hist ? dec->hist_len : nullptr,
+                                       (int)history_stride, dec->rng, dec->tok_b, dec->err, dec->stream),
+                  "sample");
+        cuda_check(cudaMemcpyAsync(out_tokens, dec->tok_b, dec->S * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                   dec->stream), "download tokens");
+        cuda_check(cudaMemcpyAsync(rng_state, dec->rng, (size_t)dec->S * 4 * sizeof(uint64_t),
+                                   cudaMemcpyDeviceToHost, dec->stream), "download rng");
+        check_err_flag(dec);
+    });
+}
+
+nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32_t *lens, uint32_t max_t,
+                              uint32_t n_new, const nk_sample_cfg *cfg, uint64_t *rng_state,
+                              uint32_t *out_tokens) {
+    return guard([&] {
+        if (!dec || !lens || !cfg || !rng_state || (n_new && !out_tokens) || (!ids && max_t))
+            fail(NK_ERR_INVALID, "null argument");
+        check_sample_cfg(dec->model, *cfg);
+        const uint32_t S = dec->S;
+        // An empty prompt becomes the newline byte token (cli.rs:474-476).
+        const uint32_t mt = std::max<uint32_t>(max_t, 1);
+        std::vector<uint32_t> pid((size_t)S * mt, 0), plen(S);
+        for (uint32_t s = 0; s < S; ++s) {
+            if (lens[s] > max_t) fail(NK_ERR_INVALID, "prompt length exceeds max_t");
+            if (lens[s] == 0) {
+                if (10 >= dec->model->cfg.vocab) fail(NK_ERR_INVALID, "streaming token is outside the vocabulary");
+                pid[(size_t)s * mt] = 10;
+                plen[s] = 1;
+            } else {
+                std::memcpy(&pid[(size_t)s * mt], ids + (size_t)s * max_t, lens[s] * sizeof(uint32_t));
+                plen[s] = lens[s];
+            }
+            validate_tokens(dec->model, &pid[(size_t)s * mt], plen[s]);
+        }
+        ensure_ready(dec);
+        upload_prompts(dec, pid.data(), plen.data(), mt);
+        prefill_device(dec, dec->p_ids, dec->p_lens, plen, mt, nullptr);
+        // History = the last rep_window prompt ids (cli.rs:484-486).
+        const uint32_t W = (uint32_t)std::min<uint64_t>(cfg->rep_window, 1u << 20);
+        const bool use_hist = W > 0 && std::isfinite(cfg->rep_penalty) && cfg->rep_penalty > 1.0f;
+        if (W > 0) {
+            ensure_history(dec, W);
+            std::vector<uint32_t> h((size_t)S * W, 0), hl(S);
+            for (uint32_t s = 0; s < S; ++s) {
+                const uint32_t n = plen[s], st = n > W ? n - W : 0;
+                hl[s] = n - st;
+                std::memcpy(&h[(size_t)s * W], &pid[(size_t)s * mt + st], hl[s] * sizeof(uint32_t));
+            }
+            cuda_check(cudaMemcpyAsync(dec->hist, h.data(), h.size() * sizeof(uint32_t), cudaMemcpyHostToDevice, dec->stream), "upload history");
+            cuda_check(cudaMemcpyAsync(dec->hist_len, hl.data(), S * sizeof(uint32_t), cudaMemcpyHostToDevice, dec->stream), "upload history");
+            cuda_check(cudaStreamSynchronize(dec->stream), "sync");
+        }
+        cuda_check(cudaMemcpyAsync(dec->rng, rng_state, (size_t)S * 4 * sizeof(uint64_t), cudaMemcpyHostToDevice,
+                                   dec->stream), "upload rng");
+        uint32_t *d_out = nullptr;
+        dalloc(&d_out, (size_t)S * std::max<uint32_t>(n_new, 1), "generated tokens");
+        std::unique_ptr<uint32_t, void (*)(uint32_t *)> own(d_out, [](uint32_t *p) { cudaFree(p); });
+        const nk::SampleParams sp = to_params(*cfg);
+        for (uint32_t gi = 0; gi < n_new; ++gi) {
+            launch_ok(dec, nk::sample_rows(dec->logits, (int)S, (int)dec->model->cfg.vocab, sp,
+                                           use_hist ? dec->hist : nullptr, use_hist ? dec->hist_len : nullptr,
+                                           (int)W, dec->rng, dec->tok_b, dec->err, dec->stream), "sample");
+            cuda_check(cudaMemcpy2DAsync(d_out + gi, (size_t)n_new * sizeof(uint32_t), dec->tok_b, sizeof(uint32_t),
+                                         sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, dec->stream), "collect tokens");
+            if (W > 0) launch_ok(dec, nk::history_push(dec->hist, dec->hist_len, dec->tok_b, (int)S, (int)W, dec->stream), "history");
+            if (gi + 1 < n_new) step_device(dec, dec->tok_b);
+        }
+        if (n_new)
+            cuda_check(cudaMemcpyAsync(out_tokens, d_out, (size_t)S * n_new * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                       dec->stream), "download tokens");
+        cuda_check(cudaMemcpyAsync(rng_state, dec->rng, (size_t)S * 4 * sizeof(uint64_t), cudaMemcpyDeviceToHost,
+                                   dec->stream), "download rng");
+        check_err_flag(dec);
+    });
+}
+
+nk_status nk_decoder_get_state(nk_decoder *dec, uint32_t first, uint32_t count, float *state, uint32_t *heads) {
+    return guard([&] {
+        if (!dec || !state) fail(NK_ERR_INVALID, "null argument");
+        if ((uint64_t)first + count > dec->S) fail(NK_ERR_INVALID, "stream range out of bounds");
+        cuda_check(cudaSetDevice(dec->model->device), "cudaSetDevice");
+        const size_t per = (dec->model->k() + 1) * dec->model->e();
+        for (uint64_t l = 0; l < dec->L(); ++l)
+            cuda_check(cudaMemcpy2DAsync(state + l * per, dec->L() * per * sizeof(float),
+                                         dec->layer_state(l) + (size_t)first * per, per * sizeof(float),
+                                         per * sizeof(float), count, cudaMemcpyDeviceToHost, dec->stream),
+                       "download state");
+        if (heads)
+            cuda_check(cudaMemcpyAsync(heads, dec->heads + first, count * sizeof(uint32_t), cudaMemcpyDeviceToHost,
+                                       dec->stream), "download heads");
+        cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+    });
+}
+
+nk_status nk_decoder_set_state(nk_decoder *dec, uint32_t first, uint32_t count, const float *state,
+                               const uint32_t *heads) {
+    return guard([&] {
+        if (!dec || !state || !heads) fail(NK_ERR_INVALID, "null argument");
+        if ((uint64_t)first + count > dec->S) fail(NK_ERR_INVALID, "stream range out of bounds");
+        const uint64_t k = dec->model->k();
+        std::vector<uint32_t> hv(heads, heads + count);
+        for (auto &h : hv)
+            if (h >= k) fail(NK_ERR_INVALID, "conv head out of range");
+        cuda_check(cudaSetDevice(dec->model->device), "cudaSetDevice");
+        const size_t per = (k + 1) * dec->model->e();
+        for (uint64_t l = 0; l < dec->L(); ++l)
+            cuda_check(cudaMemcpy2DAsync(dec->layer_state(l) + (size_t)first * per, per * sizeof(float),
+                                         state + l * per, dec->L() * per * sizeof(float), per * sizeof(float), count,
+                                         cudaMemcpyHostToDevice, dec->stream),
+                       "upload state");
+        cuda_check(cudaMemcpyAsync(dec->heads + first, hv.data(), count * sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                   dec->stream), "upload heads");
+        cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+    });
+}
+
+nk_status nk_decoder_cuda_stream(nk_decoder *dec, void **stream) {
+    return guard([&] {
+        if (!dec || !stream) fail(NK_ERR_INVALID, "null argument");
+        *stream = (void *)dec->stream;
+    });
+}
+
+nk_status nk_decoder_sync(nk_decoder *dec) {
+    return guard([&] {
+        if (!dec) fail(NK_ERR_INVALID, "null decoder");
+        cuda_check(cudaSetDevice(dec->model->device), "cudaSetDevice");
+        check_err_flag(dec);
+    });
+}
+
+nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
+    return guard([&] {
+        if (!dec) fail(NK_ERR_INVALID, "null decoder");
+        if (engine < 0 || engine > 7) fail(NK_ERR_INVALID, "unknown engine flags");
+        dec->engine = engine;
+    });
+}
+
+nk_status nk_decoder_launch_count(const nk_decoder *dec, uint64_t *count) {
+    return guard([&] {
+        if (!dec || !count) fail(NK_ERR_INVALID, "null argument");
+        *count = dec->launches;
+    });
+}
+
+nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
+                         int chunked, void *stream) {
+    return guard([&] {
+        if (batch * t * d == 0) return;
+        if (!a || !b || !h) fail(NK_ERR_INVALID, "null argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        if (!chunked) {
+            cuda_check(nk::scan_sequential(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan");
+            return;
+        }
+        float *scratch = nullptr;
+        dalloc(&scratch, nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d), "scan scratch");
+        cudaError_t e = nk::scan_chunked(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, scratch, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cudaFree(scratch);
+        cuda_check(e, "scan");
+        cuda_check(e2, "scan sync");
+    });
+}
+
+nk_status nk_scan(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
+                  int chunked, int device) {
+    return guard([&] {
+        const size_t n = batch * t * d;
+        if (n == 0) return;
+        if (!a || !b || !h) fail(NK_ERR_INVALID, "null argument");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        float *da = nullptr, *db = nullptr, *dh = nullptr;
+        dalloc(&da, n, "scan a");
+        std::unique_ptr<float, void (*)(float *)> oa(da, [](float *p) { cudaFree(p); });
+        dalloc(&db, n, "scan b");
+        std::unique_ptr<float, void (*)(float *)> ob(db, [](float *p) { cudaFree(p); });
+        dalloc(&dh, n, "scan h");
+        std::unique_ptr<float, void (*)(float *)> oh(dh, [](float *p) { cudaFree(p); });
+        cuda_check(cudaMemcpy(da, a, n * 4, cudaMemcpyHostToDevice), "upload a");
+        cuda_check(cudaMemcpy(db, b, n * 4, cudaMemcpyHostToDevice), "upload b");
+        nk_status s = nk_scan_device(da, db, dh, batch, t, d, chunked, nullptr);
+        if (s != NK_OK) fail(s, g_err);
+        cuda_check(cudaMemcpy(h, dh, n * 4, cudaMemcpyDeviceToHost), "download h");
+    });
+}
+
+nk_status nk_sample_token(float *logits, uint64_t vocab, const nk_sample_cfg *cfg, const uint32_t *history,
+                          uint64_t n_history, uint64_t *rng_state, uint32_t *out_token, int device) {
+    return guard([&] {
+        if (!logits || !cfg || !rng_state || !out_token || (n_history && !history)) fail(NK_ERR_INVALID, "null argument");
+        if (vocab == 0) fail(NK_ERR_INVALID, "cannot sample from an empty vocabulary");
+        if (vocab > (1u << 30)) fail(NK_ERR_UNSUPPORTED, "vocabulary too large");
+        if (!cfg->greedy && vocab > (uint64_t)nk::sample_max_vocab())
+            fail(NK_ERR_UNSUPPORTED, "stochastic sampling is limited to vocab <= " + std::to_string(nk::sample_max_vocab()));
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        float *dl = nullptr;
+        uint64_t *dr = nullptr;
+        uint32_t *dh = nullptr, *dhl = nullptr, *dt = nullptr;
+        int *de = nullptr;
+        dalloc(&dl, vocab, "logits");
+        std::unique_ptr<float, void (*)(float *)> o1(dl, [](float *p) { cudaFree(p); });
+        dalloc(&dr, 4, "rng");
+        std::unique_ptr<uint64_t, void (*)(uint64_t *)> o2(dr, [](uint64_t *p) { cudaFree(p); });
+        dalloc(&dh, std::max<uint64_t>(n_history, 1), "history");
+        std::unique_ptr<uint32_t, void (*)(uint32_t *)> o3(dh, [](uint32_t *p) { cudaFree(p); });
+        dalloc(&dhl, 1, "history length");
+        std::unique_ptr<uint32_t, void (*)(uint32_t *)> o4(dhl, [](uint32_t *p) { cudaFree(p); });
+        dalloc(&dt, 1, "token");
+        std::unique_ptr<uint32_t, void (*)(uint32_t *)> o5(dt, [](uint32_t *p) { cudaFree(p); });
+        dalloc(&de, 1, "error flag");
+        std::unique_ptr<int, void (*)(int *)> o6(de, [](int *p) { cudaFree(p); });
+        const uint32_t hl = (uint32_t)n_history;
+        cuda_check(cudaMemcpy(dl, logits, vocab * 4, cudaMemcpyHostToDevice), "upload logits");
+        cuda_check(cudaMemcpy(dr, rng_state, 32, cudaMemcpyHostToDevice), "upload rng");
+        if (n_history) cuda_check(cudaMemcpy(dh, history, n_history * 4, cudaMemcpyHostToDevice), "upload history");
+        cuda_check(cudaMemcpy(dhl, &hl, 4, cudaMemcpyHostToDevice), "upload history length");
+        cuda_check(cudaMemset(de, 0, 4), "memset");
+        cuda_check(nk::sample_rows(dl, 1, (int)vocab, to_params(*cfg), n_history ? dh : nullptr, n_history ? dhl : nullptr,
+                                   (int)std::max<uint64_t>(n_history, 1), dr, dt, de, nullptr),
+                   "sample");
+        int e = 0;
+        cuda_check(cudaMemcpy(out_token, dt, 4, cudaMemcpyDeviceToHost), "download token");
+        cuda_check(cudaMemcpy(rng_state, dr, 32, cudaMemcpyDeviceToHost), "download rng");
+        cuda_check(cudaMemcpy(logits, dl, vocab * 4, cudaMemcpyDeviceToHost), "download logits");
+        cuda_check(cudaMemcpy(&e, de, 4, cudaMemcpyDeviceToHost), "download error flag");
+        if (e) fail(NK_ERR_DEVICE, "the bounded rejection draw failed");
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+"""Scan prefill on the GPU vs stepping the oracle through the prompt.
+
+The reference's gen path prefills with one Decoder::step per prompt token
+(cli.rs:478-480); the batched forward with the scan (model.rs:148-165) is
+pinned equal to it by selftest.rs:273-299.  The GPU prefill must leave the
+same LmState (conv ring, head, h) and the same last-position logits."""
+
+import numpy as np
+import pytest
+
+from conftest import c1_cfg, same_model, state_rel_err, tiny_cfg
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3
+STATE_TOL = 1e-4
+SEQ, CHUNKED = 4, 2  # engine bits forcing the prefill scan variant
+
+
+def _ragged(S, T, V, lens, seed):
+    import oracle as O
+
+    ids = np.zeros((S, T), dtype=np.uint32)
+    for s in range(S):
+        r = O.Rng(seed + s)
+        ids[s, : lens[s]] = [r.below(V) for _ in range(lens[s])]
+    return ids
+
+
+def _check(dec, od_list, last, lens, kw, live_logits):
+    k, E = kw["conv_k"], kw["d_model"] * kw["expand"]
+    st, heads = dec.get_state()
+    for s, od in enumerate(od_list):
+        ost, oh = od.get_state()
+        assert heads[s] == oh, s
+        for layer in range(ost.shape[0]):
+            assert state_rel_err(st[s, layer, k * E:], ost[layer, k * E:]) <= STATE_TOL, (s, layer)
+            assert state_rel_err(st[s, layer, : k * E], ost[layer, : k * E]) <= STATE_TOL, (s, layer)
+        if lens[s] > 0:
+            assert np.abs(last[s] - live_logits[s]).max() <= LOGIT_TOL, s
+
+
+@pytest.mark.parametrize("engine", [SEQ, CHUNKED])
+def test_ragged_prefill_matches_stepping(gpu, orc, engine):
+    kw = c1_cfg(dict)
+    om, gm = same_model(orc, gpu, kw, seed=0)
+    lens = [0, 1, 3, 17, 70, 200]
+    S, T = len(lens), max(lens)
+    ids = _ragged(S, T, kw["vocab"], lens, 1000)
+    dec = gpu.Decoder(gm, S)
+    dec.set_engine(engine)
+    last = dec.prefill(ids, lens).copy()
+    ods, live = [], []
+    for s in range(S):
+        od = orc.Decoder(om)
+        lg = None
+        for t in ids[s, : lens[s]]:
+            lg = od.step(t).copy()
+        ods.append(od)
+        live.append(lg)
+    _check(dec, ods, last, lens, kw, live)
+
+
+@pytest.mark.parametrize("engine", [SEQ, CHUNKED])
+def test_prefill_continues_from_a_stepped_state(gpu, orc, engine):
+    kw = tiny_cfg(dict, 31, conv_k=4, n_layer=3)
+    om, gm = same_model(orc, gpu, kw, seed=9)
+    S = 3
+    dec = gpu.Decoder(gm, S)
+    dec.set_engine(engine)
+    ods = [orc.Decoder(om) for _ in range(S)]
+    for t in [4, 5]:
+        dec.step([t] * S)
+        for od in ods:
+            od.step(t)
+    lens = [1, 2, 130]
+    ids = _ragged(S, 130, 31, lens, 40)
+    last = dec.prefill(ids, lens).copy()
+    live = []
+    for s, od in enumerate(ods):
+        lg = None
+        for t in ids[s, : lens[s]]:
+            lg = od.step(t).copy()
+        live.append(lg)
+    _check(dec, ods, last, lens, kw, live)
+    # And decoding continues identically afterwards.
+    nxt = dec.step([7, 8, 9])
+    for s, od in enumerate(ods):
+        assert np.abs(nxt[s] - od.step([7, 8, 9][s])).max() <= LOGIT_TOL
+
+
+@pytest.mark.parametrize("conv_k", [1, 2, 7])
+def test_prefill_awkward_conv_widths(gpu, orc, conv_k):
+    kw = tiny_cfg(dict, 17, conv_k=conv_k, n_layer=2)
+    om, gm = same_model(orc, gpu, kw, seed=20250816)
+    lens = [1, conv_k, conv_k + 1, 9]
+    S = len(lens)
+    ids = _ragged(S, 9, 17, lens, 5)
+    for engine in [SEQ, CHUNKED]:
+        dec = gpu.Decoder(gm, S)
+        dec.set_engine(engine)
+        last = dec.prefill(ids, lens).copy()
+        ods, live = [], []
+        for s in range(S):
+            od = orc.Decoder(om)
+            lg = None
+            for t in ids[s, : lens[s]]:
+                lg = od.step(t).copy()
+            ods.append(od)
+            live.append(lg)
+        _check(dec, ods, last, lens, kw, live)
+
+
+def test_long_prompt_chunked_scan_matches_batched_oracle(gpu, orc):
+    # A prompt much longer than the scan's time block, two streams: the
+    # time-parallel scan path, checked against the oracle's batched forward.
+    kw = tiny_cfg(dict, 23, conv_k=4, n_layer=2)
+    om, gm = same_model(orc, gpu, kw, seed=6)
+    S, T = 2, 1500
+    ids = _ragged(S, T, 23, [T, T - 37], 900)
+    lens = [T, T - 37]
+    dec = gpu.Decoder(gm, S)
+    dec.set_engine(CHUNKED)
+    last = dec.prefill(ids, lens).copy()
+    st, heads = dec.get_state()
+    k, E = kw["conv_k"], kw["d_model"] * kw["expand"]
+    for s in range(S):
+        ost, oh, olast = om.prefill_state(ids[s, : lens[s]], 1, lens[s])
+        assert heads[s] == oh[0]
+        assert state_rel_err(st[s][:, k * E:], ost[0][:, k * E:]) <= STATE_TOL
+        assert np.abs(last[s] - olast[0]).max() <= LOGIT_TOL
+
+
+def test_prefill_rejects_bad_input(gpu, orc):
+    kw = tiny_cfg(dict, 19)
+    _, gm = same_model(orc, gpu, kw, seed=1)
+    dec = gpu.Decoder(gm, 2)
+    with pytest.raises(gpu.NoeticError):
+        dec.prefill(np.array([[1, 2], [3, 19]], dtype=np.uint32))
+    with pytest.raises(gpu.NoeticError):
+        dec.prefill(np.array([[1, 2], [3, 4]], dtype=np.uint32), lens=[3, 1])
