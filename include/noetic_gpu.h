@@ -186,6 +186,20 @@ nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 /* Number of kernels this decoder has launched so far. */
 nk_status nk_decoder_launch_count(const nk_decoder *dec, uint64_t *count);
 
+/* Device-time profile of the projections (the dominant kernels), measured
+ * with CUDA events recorded on the decoder's stream around every projection
+ * launch between nk_decoder_profile_begin and nk_decoder_profile_end. */
+typedef struct nk_profile {
+    double proj_ms;          /* summed device time of projection launches   */
+    uint64_t proj_launches;  /* projection launches                          */
+    double proj_flops;       /* useful f32 flops, 2*M*N*K summed             */
+    double proj_bytes;       /* algorithmic bytes: A, W, bias, R read + C    */
+    uint64_t launches;       /* every kernel launched while profiling        */
+    int tensor_core;         /* 1 if any projection ran on tcgen05           */
+} nk_profile;
+nk_status nk_decoder_profile_begin(nk_decoder *dec);
+nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out);
+
 /* ---------------------------------------------------------------- ops */
 
 /* scan_sequential / scan_chunked (scan.rs:35-57, 98-225):

@@ -51,6 +51,11 @@ class NkSampleCfg(C.Structure):
                 ("rep_window", _u64), ("greedy", _u32)]
 
 
+class NkProfile(C.Structure):
+    _fields_ = [("proj_ms", C.c_double), ("proj_launches", _u64), ("proj_flops", C.c_double),
+                ("proj_bytes", C.c_double), ("launches", _u64), ("tensor_core", _i32)]
+
+
 SIGNATURES = {
     "nk_last_error": (C.c_char_p, []),
     "nk_device_count": (_i32, [C.POINTER(_i32)]),
@@ -81,6 +86,8 @@ SIGNATURES = {
     "nk_decoder_sync": (_i32, [_P]),
     "nk_decoder_set_engine": (_i32, [_P, _i32]),
     "nk_decoder_launch_count": (_i32, [_P, C.POINTER(_u64)]),
+    "nk_decoder_profile_begin": (_i32, [_P]),
+    "nk_decoder_profile_end": (_i32, [_P, C.POINTER(NkProfile)]),
     "nk_scan": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
     "nk_scan_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _P]),
     "nk_sample_token": (_i32, [_P, _u64, C.POINTER(NkSampleCfg), _P, _u64, _P, _P, _i32]),
@@ -400,6 +407,15 @@ class Decoder:
         n = C.c_uint64()
         _check(lib().nk_decoder_launch_count(self.h, C.byref(n)))
         return n.value
+
+    def profile_begin(self):
+        _check(lib().nk_decoder_profile_begin(self.h))
+
+    def profile_end(self) -> dict:
+        p = NkProfile()
+        _check(lib().nk_decoder_profile_end(self.h, C.byref(p)))
+        return {"proj_ms": p.proj_ms, "proj_launches": p.proj_launches, "proj_flops": p.proj_flops,
+                "proj_bytes": p.proj_bytes, "launches": p.launches, "tensor_core": bool(p.tensor_core)}
 
 
 # ---------------------------------------------------------------- ops

@@ -45,8 +45,9 @@ cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs);
 void tc_weights_free(TcWeights &w);
 void tc_scratch_free(TcScratch &s);
 
-// C = epilogue(A . W^T) with the same epilogue as gemm_nt_simt.
-cudaError_t tc_gemm(const GemmArgs &p, const TcOperand &W, TcScratch &s, cudaStream_t st,
+// C = epilogue(A . W^T) with the same epilogue as gemm_nt_simt.  A kernel
+// whose bounded waits expire writes a nonzero code to *err (device int).
+cudaError_t tc_gemm(const GemmArgs &p, const TcOperand &W, TcScratch &s, cudaStream_t st, int *err,
                     int *launches);
 
 }  // namespace nk

@@ -436,6 +436,13 @@ struct nk_decoder {
     uint32_t *p_ids = nullptr, *p_lens = nullptr;
     size_t p_ids_cap = 0;
     nk::TcScratch tcs;
+    // projection profiling (CUDA events around each projection launch)
+    bool profiling = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_used = 0;
+    double prof_flops = 0, prof_bytes = 0;
+    uint64_t prof_launch0 = 0, prof_proj = 0;
+    bool prof_tc = false;
 
     uint64_t L() const { return model->cfg.n_layer; }
     size_t layer_state_floats() const { return (size_t)S * (model->k() + 1) * model->e(); }
@@ -451,6 +458,7 @@ struct nk_decoder {
                         (void *)p_lens})
             if (p) cudaFree(p);
         nk::tc_scratch_free(tcs);
+        for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -469,16 +477,36 @@ void launch_ok(nk_decoder *dec, cudaError_t e, const char *what, int count = 1) 
 
 // One projection: tensor-core 3xTF32 GEMM when eligible, else the f32
 // CUDA-core kernels.
+cudaEvent_t prof_event(nk_decoder *dec) {
+    if (dec->ev_used == dec->ev_pool.size()) {
+        cudaEvent_t e;
+        cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+        dec->ev_pool.push_back(e);
+    }
+    return dec->ev_pool[dec->ev_used++];
+}
+
 void project(nk_decoder *dec, const float *A, int M, int K, const float *W, const nk::TcOperand *Wtc,
              int N, const float *bias, float *C, const float *R) {
     nk::GemmArgs p{A, K, W, K, C, N, M, N, K, bias, R, N};
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (dec->profiling) {
+        e0 = prof_event(dec);
+        e1 = prof_event(dec);
+        cuda_check(cudaEventRecord(e0, dec->stream), "cudaEventRecord");
+        dec->prof_flops += 2.0 * M * (double)N * K;
+        dec->prof_bytes += 4.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1) + (bias ? N : 0));
+        dec->prof_proj += 1;
+    }
     if (!(dec->engine & 1) && Wtc && nk::tc_eligible(M, N, K)) {
         int launches = 0;
-        cuda_check(nk::tc_gemm(p, *Wtc, dec->tcs, dec->stream, &launches), "tcgen05 projection");
+        cuda_check(nk::tc_gemm(p, *Wtc, dec->tcs, dec->stream, dec->err, &launches), "tcgen05 projection");
         dec->launches += (uint64_t)launches;
-        return;
+        dec->prof_tc = dec->prof_tc || dec->profiling;
+    } else {
+        launch_ok(dec, nk::gemm_nt_simt(p, dec->stream), "f32 projection");
     }
-    launch_ok(dec, nk::gemm_nt_simt(p, dec->stream), "f32 projection");
+    if (dec->profiling) cuda_check(cudaEventRecord(e1, dec->stream), "cudaEventRecord");
 }
 
 void ensure_ready(nk_decoder *dec) {
@@ -510,7 +538,8 @@ void check_err_flag(nk_decoder *dec) {
     if (h) {
         cuda_check(cudaMemsetAsync(dec->err, 0, sizeof(int), dec->stream), "clear error flag");
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
-        fail(NK_ERR_DEVICE, "a kernel reported an invalid token id or a failed bounded draw");
+        fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
+                                ": 1 invalid token, 2 bounded draw, 101-103 tensor-core pipeline wait expired)");
     }
 }
 
@@ -1133,6 +1162,40 @@ nk_status nk_decoder_launch_count(const nk_decoder *dec, uint64_t *count) {
     return guard([&] {
         if (!dec || !count) fail(NK_ERR_INVALID, "null argument");
         *count = dec->launches;
+    });
+}
+
+nk_status nk_decoder_profile_begin(nk_decoder *dec) {
+    return guard([&] {
+        if (!dec) fail(NK_ERR_INVALID, "null decoder");
+        dec->profiling = true;
+        dec->ev_used = 0;
+        dec->prof_flops = dec->prof_bytes = 0;
+        dec->prof_proj = 0;
+        dec->prof_tc = false;
+        dec->prof_launch0 = dec->launches;
+    });
+}
+
+nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out) {
+    return guard([&] {
+        if (!dec || !out) fail(NK_ERR_INVALID, "null argument");
+        cuda_check(cudaSetDevice(dec->model->device), "cudaSetDevice");
+        cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+        double ms = 0;
+        for (size_t i = 0; i + 1 < dec->ev_used; i += 2) {
+            float t = 0;
+            cuda_check(cudaEventElapsedTime(&t, dec->ev_pool[i], dec->ev_pool[i + 1]), "cudaEventElapsedTime");
+            ms += t;
+        }
+        out->proj_ms = ms;
+        out->proj_launches = dec->prof_proj;
+        out->proj_flops = dec->prof_flops;
+        out->proj_bytes = dec->prof_bytes;
+        out->launches = dec->launches - dec->prof_launch0;
+        out->tensor_core = dec->prof_tc ? 1 : 0;
+        dec->profiling = false;
+        dec->ev_used = 0;
     });
 }
 

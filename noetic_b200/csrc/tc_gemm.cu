@@ -1,15 +1,397 @@
-// tc_gemm.cu -- tcgen05 3xTF32 projection engine (sm_100a).
+// tc_gemm.cu -- tensor-core projections for sm_100a: C = epilogue(A . W^T)
+// in f32 accuracy with 3xTF32 on tcgen05.
 //
-// Not yet enabled: every projection runs on the f32 CUDA-core kernels.
+// Split: a = a_hi + a_lo with a_hi = tf32(a), a_lo = tf32(a - a_hi) (the
+// error-corrected TF32 product of Ootomo & Yokota 2022, "3xTF32" in
+// CUTLASS); A.W^T = A_hi.W_hi^T + A_hi.W_lo^T + A_lo.W_hi^T, dropping the
+// A_lo.W_lo^T term (~2^-22 relative).  Weights are split once at load; the
+// activation operand is split by a small pre-pass per projection.
+//
+// Kernel structure (one 128 x 256 output tile per CTA, 256 threads):
+//   warp 0      TMA producer: K-blocks of 32 f32 (one 128-byte swizzle row)
+//               for A_hi, A_lo, W_hi, W_lo into a 2-stage smem ring
+//               (cp.async.bulk.tensor, 128B swizzle, zero fill out of bounds);
+//   warp 1      TMEM allocator and MMA issuer: per K-block, 4 k-steps x 3
+//               tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=256, K=8) into
+//               one f32 TMEM accumulator; tcgen05.commit frees the stage;
+//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time (lane = row), bias,
+//               residual add, store.
+// Every mbarrier wait is bounded (~1 s of %globaltimer); on expiry the kernel
+// records an error code, every role leaves its loop, TMEM is freed and the
+// CTA exits -- the host reports the code instead of the GPU hanging.
+// No TMA multicast is used anywhere.
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <mutex>
+
+#include "nk_common.cuh"
 #include "nk_tc.h"
 
 namespace nk {
 
-bool tc_eligible(int, int, int) { return false; }
+namespace {
 
-cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &) {
-    w.ready = false;
+constexpr int BM = 128, BN = 256, BK = 32;
+constexpr int STAGES = 2;
+constexpr int A_BYTES = BM * BK * 4;                       // 16 KiB
+constexpr int B_BYTES = BN * BK * 4;                       // 32 KiB
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;     // 96 KiB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int THREADS = 256;
+constexpr uint32_t TMEM_COLS = BN;
+constexpr uint64_t WAIT_NS = 1000000000ull;  // bound of every mbarrier wait
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=256.
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
+
+struct TcArgs {
+    float *C;
+    int ldc;
+    int M, N, K;
+    const float *bias;
+    const float *R;
+    int ldr;
+    int *err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Bounded wait for the phase of parity `parity` to complete.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done = 0;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+    if (done) return true;
+    const uint64_t t0 = globaltimer();
+    for (;;) {
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+            : "=r"(done) : "r"(bar), "r"(parity) : "memory");
+        if (done) return true;
+        if (globaltimer() - t0 > WAIT_NS) return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(IDESC), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+          "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+          "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
+               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte aligned tile area (the 128B swizzle pattern repeats every 1 KiB).
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES);  // full[S], empty[S], accum
+    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 1);
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int kblocks = (p.K + BK - 1) / BK;
+
+    const uint32_t bar_full0 = smem_u32(&bars[0]);
+    const uint32_t bar_empty0 = smem_u32(&bars[STAGES]);
+    const uint32_t bar_accum = smem_u32(&bars[2 * STAGES]);
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(bar_full0 + 8 * s, 1);
+            mbar_init(bar_empty0 + 8 * s, 1);
+        }
+        mbar_init(bar_accum, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAh) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAl) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBh) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBl) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued = 0;
+        for (int kb = 0; kb < kblocks; ++kb) {
+            if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
+                atomicExch(p.err, 101);
+                s_abort = 1;
+                break;
+            }
+            if (*(volatile int *)&s_abort) break;
+            uint8_t *st = smem + stage * STAGE_BYTES;
+            const uint32_t full = bar_full0 + 8 * stage;
+            mbar_expect_tx(full, STAGE_BYTES);
+            const int kx = kb * BK;
+            tma_load_2d(smem_u32(st), &mapAh, full, kx, m0);
+            tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, m0);
+            tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
+            tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
+            ++issued;
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1;
+            }
+        }
+        // Drain: wait (bounded) until every issued stage has landed, so no
+        // copy is still writing this CTA's shared memory when it exits.
+        {
+            int s2 = 0;
+            uint32_t ph2 = 0;
+            for (int i = 0; i < issued; ++i) {
+                if (i >= issued - STAGES) mbar_wait(bar_full0 + 8 * s2, ph2);
+                if (++s2 == STAGES) {
+                    s2 = 0;
+                    ph2 ^= 1;
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+            if (!mbar_wait(bar_full0 + 8 * stage, phase) || *(volatile int *)&s_abort) {
+                atomicExch(p.err, 102);
+                s_abort = 1;
+                ok = false;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t base = smem_u32(smem + stage * STAGE_BYTES);
+            const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + A_BYTES);
+            const uint64_t dBh = smem_desc(base + 2 * A_BYTES), dBl = smem_desc(base + 2 * A_BYTES + B_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 8; ++kk) {
+                const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
+                mma_tf32(tmem, dAl + off, dBh + off, (kb | kk) ? 1u : 0u);
+                mma_tf32(tmem, dAh + off, dBl + off, 1u);
+                mma_tf32(tmem, dAh + off, dBh + off, 1u);
+            }
+            mma_commit(bar_empty0 + 8 * stage);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1;
+            }
+        }
+        // Arrives once every MMA issued above has completed (also on the
+        // abort path, so TMEM is never freed under a running MMA).
+        (void)ok;
+        mma_commit(bar_accum);
+    } else if (warp >= 4) {
+        // ---- epilogue: warp w reads TMEM lanes 32*(w%4) .. +31
+        const int q = warp & 3;
+        const bool ok = mbar_wait(bar_accum, 0) && !*(volatile int *)&s_abort;
+        __syncwarp();
+        if (!ok) {
+            if (lane == 0) atomicExch(p.err, 103);
+        } else {
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int row = m0 + q * 32 + lane;
+            const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
+            for (int c0 = 0; c0 < BN; c0 += 32) {
+                if (n0 + c0 >= p.N) break;  // warp-uniform
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+                if (row < p.M) {
+                    const int nb = n0 + c0;
+                    float *crow = p.C + (size_t)row * p.ldc;
+                    const float *rrow = p.R ? p.R + (size_t)row * p.ldr : nullptr;
+                    if (vec && nb + 32 <= p.N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 o;
+                            o.x = v[j + 0]; o.y = v[j + 1]; o.z = v[j + 2]; o.w = v[j + 3];
+                            if (p.bias) {
+                                const float4 b = *reinterpret_cast<const float4 *>(p.bias + nb + j);
+                                o.x = o.x + b.x; o.y = o.y + b.y; o.z = o.z + b.z; o.w = o.w + b.w;
+                            }
+                            if (rrow) {
+                                const float4 r = *reinterpret_cast<const float4 *>(rrow + nb + j);
+                                o.x = r.x + o.x; o.y = r.y + o.y; o.z = r.z + o.z; o.w = r.w + o.w;
+                            }
+                            *reinterpret_cast<float4 *>(crow + nb + j) = o;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int n = nb + j;
+                            if (n < p.N) {
+                                float o = v[j];
+                                if (p.bias) o = o + p.bias[n];
+                                if (rrow) o = rrow[n] + o;
+                                crow[n] = o;
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// hi = tf32(x), lo = tf32(x - hi), over rows x cols with a row stride.
+__global__ void split_tf32_k(const float *__restrict__ src, int ld, float *__restrict__ hi,
+                             float *__restrict__ lo, int rows, int cols) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * cols) return;
+    const int64_t r = i / cols;
+    const int c = (int)(i - r * cols);
+    const float x = src[(size_t)r * ld + c];
+    const float h = tf32_round(x);
+    hi[i] = h;
+    lo[i] = tf32_round(x - h);
+}
+
+// ---- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    });
+    return fn;
+}
+
+// 2-D f32 map over [rows, cols] (cols contiguous), box {BK, box_rows}, 128B
+// swizzle, zero fill outside the tensor.
+bool make_map(CUtensorMap *map, const float *base, int rows, int cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(float)};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+cudaError_t split(const float *src, int ld, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
+    const int64_t n = (int64_t)rows * cols;
+    if (n == 0) return cudaSuccess;
+    split_tf32_k<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, ld, hi, lo, rows, cols);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+bool tc_eligible(int M, int N, int K) {
+    return M >= BM && N >= BN && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
+}
+
+cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs) {
+    tc_weights_free(w);
+    size_t total = 0;
+    for (const TcSource &s : srcs) total += 2 * (((size_t)s.N * s.K + 63) & ~size_t(63));
+    cudaError_t e = cudaMalloc(&w.arena, total * sizeof(float));
+    if (e != cudaSuccess) return e;
+    size_t off = 0;
+    w.ops.resize(srcs.size());
+    for (size_t i = 0; i < srcs.size(); ++i) {
+        const TcSource &s = srcs[i];
+        TcOperand &op = w.ops[i];
+        const size_t n = ((size_t)s.N * s.K + 63) & ~size_t(63);
+        float *hi = w.arena + off, *lo = w.arena + off + n;
+        off += 2 * n;
+        e = split(s.w, s.K, hi, lo, s.N, s.K, nullptr);
+        if (e != cudaSuccess) return e;
+        op.hi = hi;
+        op.lo = lo;
+        op.N = s.N;
+        op.K = s.K;
+        op.N_pad = s.N;
+        op.K_pad = s.K;
+        if (s.K % 4 == 0) {
+            if (!make_map((CUtensorMap *)op.map_hi, hi, s.N, s.K, BN) ||
+                !make_map((CUtensorMap *)op.map_lo, lo, s.N, s.K, BN))
+                return cudaErrorInvalidValue;
+        }
+    }
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return e;
+    w.ready = true;
     return cudaSuccess;
 }
 
@@ -26,9 +408,41 @@ void tc_scratch_free(TcScratch &s) {
     s = TcScratch{};
 }
 
-cudaError_t tc_gemm(const GemmArgs &, const TcOperand &, TcScratch &, cudaStream_t, int *launches) {
+cudaError_t tc_gemm(const GemmArgs &p, const TcOperand &W, TcScratch &s, cudaStream_t st, int *err,
+                    int *launches) {
     if (launches) *launches = 0;
-    return cudaErrorNotSupported;
+    if (W.K != p.K || W.N != p.N) return cudaErrorInvalidValue;
+    const size_t need = (size_t)p.M * p.K;
+    if (need > s.cap) {
+        if (s.a_hi) cudaFree(s.a_hi);
+        if (s.a_lo) cudaFree(s.a_lo);
+        s.a_hi = s.a_lo = nullptr;
+        s.cap = 0;
+        cudaError_t e = cudaMalloc(&s.a_hi, need * sizeof(float));
+        if (e != cudaSuccess) return e;
+        e = cudaMalloc(&s.a_lo, need * sizeof(float));
+        if (e != cudaSuccess) return e;
+        s.cap = need;
+    }
+    cudaError_t e = split(p.A, p.lda, s.a_hi, s.a_lo, p.M, p.K, st);
+    if (e != cudaSuccess) return e;
+    alignas(64) CUtensorMap mAh, mAl;
+    if (!make_map(&mAh, s.a_hi, p.M, p.K, BM) || !make_map(&mAl, s.a_lo, p.M, p.K, BM)) return cudaErrorInvalidValue;
+    static thread_local int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+        e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_dev = dev;
+    }
+    TcArgs a{p.C, p.ldc, p.M, p.N, p.K, p.bias, p.R, p.ldr, err};
+    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+    tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(*(const CUtensorMap *)&mAh, *(const CUtensorMap *)&mAl,
+                                                     *(const CUtensorMap *)W.map_hi,
+                                                     *(const CUtensorMap *)W.map_lo, a);
+    if (launches) *launches = 2;
+    return cudaGetLastError();
 }
 
 }  // namespace nk

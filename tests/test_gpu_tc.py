@@ -1,0 +1,96 @@
+"""The tcgen05 3xTF32 projection engine against the f32 CUDA-core engine and
+the oracle.  3xTF32 keeps ~22 mantissa bits per product, so the two engines
+agree to f32 rounding (logits 1e-4, state 1e-5 relative) and both stay within
+the oracle tolerances (logits 1e-3, state 1e-4)."""
+
+import numpy as np
+import pytest
+
+from conftest import same_model, state_rel_err
+
+pytestmark = pytest.mark.gpu
+
+# Every projection of this model is tensor-core eligible at >= 128 streams:
+# N in {768, 256, 1536, 256, 512}, K in {256, 768}.
+WIDE = dict(vocab=512, d_model=256, n_layer=2, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+
+
+def _ids(S, T, V, base):
+    from noetic_b200.prompts import uniform_prompts
+
+    return uniform_prompts(S, T, V, base)
+
+
+def test_tensor_core_engine_matches_f32_engine(gpu, orc):
+    om, gm = same_model(orc, gpu, WIDE, seed=1)
+    S, T = 384, 4
+    ids = _ids(S, T, WIDE["vocab"], 10)
+    tc, f32 = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    f32.set_engine(1)
+    tc.profile_begin()
+    for t in range(T):
+        a = tc.step(ids[:, t]).copy()
+        b = f32.step(ids[:, t])
+        assert np.abs(a - b).max() <= 1e-4, t
+    prof = tc.profile_end()
+    assert prof["tensor_core"], "the tensor-core engine did not run"
+    sa, ha = tc.get_state()
+    sb, hb = f32.get_state()
+    assert np.array_equal(ha, hb)
+    assert state_rel_err(sa, sb) <= 1e-5
+    for s in [0, 191, 383]:
+        od = orc.Decoder(om)
+        for t in range(T):
+            ref = od.step(ids[s, t])
+        assert np.abs(a[s] - ref).max() <= 1e-3
+
+
+def test_tensor_core_prefill_matches_stepping(gpu, orc):
+    om, gm = same_model(orc, gpu, WIDE, seed=3)
+    S, T = 64, 40  # 2560 prompt rows per projection
+    ids = _ids(S, T, WIDE["vocab"], 77)
+    lens = np.full(S, T, np.uint32)
+    lens[5] = 17
+    dec = gpu.Decoder(gm, S)
+    dec.profile_begin()
+    last = dec.prefill(ids, lens).copy()
+    assert dec.profile_end()["tensor_core"]
+    st, heads = dec.get_state()
+    k, E = WIDE["conv_k"], WIDE["d_model"]
+    for s in [0, 5, 63]:
+        od = orc.Decoder(om)
+        for t in ids[s, : lens[s]]:
+            ref = od.step(t)
+        ost, oh = od.get_state()
+        assert heads[s] == oh
+        assert state_rel_err(st[s][:, k * E:], ost[:, k * E:]) <= 1e-4
+        assert np.abs(last[s] - ref).max() <= 1e-3
+
+
+def test_headline_model_stream_subset(gpu, orc):
+    """The d=1024 / 24-layer / vocab-32768 model (seed 2) at 512 streams:
+    scan prefill of 8 prompt tokens, then 2 greedy steps; 3 streams checked
+    against the oracle."""
+    kw = dict(vocab=32768, d_model=1024, n_layer=24, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=2)
+    om.set_threads(8)
+    S, T = 512, 8
+    ids = _ids(S, T, kw["vocab"], 5000)
+    dec = gpu.Decoder(gm, S)
+    dec.profile_begin()
+    last = dec.prefill(ids).copy()
+    tok = np.argmax(last, axis=1).astype(np.uint32)
+    lg = dec.step(tok).copy()
+    assert dec.profile_end()["tensor_core"]
+    st, _ = dec.get_state()
+    k, E = 4, 1024
+    for s in [0, 300, 511]:
+        od = orc.Decoder(om)
+        for t in ids[s]:
+            ref = od.step(t).copy()
+        assert np.abs(last[s] - ref).max() <= 1e-3, s
+        ref2 = od.step(int(tok[s]))
+        assert np.abs(lg[s] - ref2).max() <= 1e-3, s
+        ost, _ = od.get_state()
+        for layer in [0, 11, 23]:
+            assert state_rel_err(st[s, layer, k * E:], ost[layer, k * E:]) <= 1e-4, (s, layer)
