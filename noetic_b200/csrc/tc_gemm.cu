@@ -12,8 +12,13 @@
 //               for A_hi, A_lo, W_hi, W_lo into a 2-stage smem ring
 //               (cp.async.bulk.tensor, 128B swizzle, zero fill out of bounds);
 //   warp 1      TMEM allocator and MMA issuer: per K-block, 4 k-steps x 3
-//               tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=256, K=8) into
-//               one f32 TMEM accumulator; tcgen05.commit frees the stage;
+//               tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=256, K=8):
+//               hi*hi into one f32 TMEM accumulator, hi*lo and lo*hi into a
+//               second one; tcgen05.commit frees the stage.  The tensor core
+//               truncates when it adds into an accumulator, so the error of a
+//               chain grows with its length; keeping the small correction
+//               products out of the main chain makes it three times shorter,
+//               and the epilogue adds the two chains in round-to-nearest f32;
 //   warps 4-7   epilogue: tcgen05.ld 32 columns at a time (lane = row), bias,
 //               residual add, store.
 // Every mbarrier wait is bounded (~1 s of %globaltimer); on expiry the kernel
@@ -41,7 +46,9 @@ constexpr int B_BYTES = BN * BK * 4;                       // 32 KiB
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;     // 96 KiB
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int THREADS = 256;
-constexpr uint32_t TMEM_COLS = BN;
+// Two f32 accumulators of BN columns: the hi*hi products and the two small
+// correction products are summed in separate TMEM chains.
+constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint64_t WAIT_NS = 1000000000ull;  // bound of every mbarrier wait
 
 // Instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=256.
@@ -233,9 +240,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
 #pragma unroll
             for (int kk = 0; kk < BK / 8; ++kk) {
                 const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
-                mma_tf32(tmem, dAl + off, dBh + off, (kb | kk) ? 1u : 0u);
-                mma_tf32(tmem, dAh + off, dBl + off, 1u);
-                mma_tf32(tmem, dAh + off, dBh + off, 1u);
+                const uint32_t acc = (kb | kk) ? 1u : 0u;
+                mma_tf32(tmem, dAh + off, dBh + off, acc);
+                mma_tf32(tmem + BN, dAh + off, dBl + off, acc);
+                mma_tf32(tmem + BN, dAl + off, dBh + off, 1u);
             }
             mma_commit(bar_empty0 + 8 * stage);
             if (++stage == STAGES) {
@@ -260,8 +268,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 if (n0 + c0 >= p.N) break;  // warp-uniform
-                float v[32];
+                float v[32], corr[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = v[j] + corr[j];
                 if (row < p.M) {
                     const int nb = n0 + c0;
                     float *crow = p.C + (size_t)row * p.ldc;
