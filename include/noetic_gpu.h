@@ -214,6 +214,28 @@ nk_status nk_scan(const float *a, const float *b, float *h, uint64_t batch, uint
 nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t,
                          uint64_t d, int chunked, void *stream);
 
+/* Time-chunked scan that allocates nothing.  No counterpart in the
+ * reference; it exists for callers that cannot allocate device memory in the
+ * middle of their work: a host whose own pool allocator owns the whole
+ * device memory budget (a stray cudaMalloc there can fail or fragment the
+ * pool), or a latency-critical loop that cannot afford the device-wide
+ * synchronisation cudaMalloc / cudaFree may cause.  It computes what
+ * nk_scan_device(..., chunked = 1, ...) computes, on device pointers,
+ * asynchronously on `stream`, but its scratch is a fixed array of
+ * NK_SCAN_NOALLOC_SCRATCH_FLOATS floats (12 MiB) inside the library's device
+ * image, which every GPU that loads the library holds until the process
+ * exits.  Limit: batch * ceil(t / NK_SCAN_TIME_BLOCK) * d <= 1048576
+ * (three scratch floats per stream, time block and channel); larger scans
+ * return NK_ERR_INVALID with a message.  It calls no allocator at all.  The
+ * first call on each device looks up the array's device address (with that
+ * device current), so make that first call before any stream capture.  All
+ * calls share the array: calls whose GPU work overlaps (other streams or
+ * threads without ordering) race and may return wrong results; order them. */
+#define NK_SCAN_TIME_BLOCK 256u
+#define NK_SCAN_NOALLOC_SCRATCH_FLOATS (3u * 1048576u)
+nk_status nk_scan_chunked_noalloc_device(const float *a, const float *b, float *h, uint64_t batch,
+                                         uint64_t t, uint64_t d, void *stream);
+
 /* sample_token (infer.rs:228-305) on one host logit row, computed on the
  * device.  logits[vocab] is mutated like the reference (penalised, then
  * tempered and normalised when not greedy); rng_state[4] in/out. */

@@ -90,6 +90,7 @@ SIGNATURES = {
     "nk_decoder_profile_end": (_i32, [_P, C.POINTER(NkProfile)]),
     "nk_scan": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
     "nk_scan_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _P]),
+    "nk_scan_chunked_noalloc_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _P]),
     "nk_sample_token": (_i32, [_P, _u64, C.POINTER(NkSampleCfg), _P, _u64, _P, _P, _i32]),
 }
 

@@ -3,6 +3,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <string>
 #include <cuda_runtime.h>
 
 namespace nk {
@@ -108,5 +109,8 @@ cudaError_t scan_sequential(const float *a, const float *b, float *h, int64_t ba
 cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch, int64_t t,
                          int64_t d, float *scratch, cudaStream_t st);
 size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d);
+
+// Sets the thread-local message that nk_last_error() returns.
+void set_last_error(const std::string &msg);
 
 }  // namespace nk

@@ -692,6 +692,10 @@ void check_sample_cfg(const nk_model *m, const nk_sample_cfg &c) {
 
 }  // namespace
 
+namespace nk {
+void set_last_error(const std::string &msg) { g_err = msg; }
+}  // namespace nk
+
 // ================================================================ C ABI
 extern "C" {
 
