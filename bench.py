@@ -358,6 +358,10 @@ def main():
     ap.add_argument("--weak", action="store_true",
                     help="fixed streams per GPU (streams x N in total) instead of the fixed 16384")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="profiling knob: fewer layers than the headline model (for small ncu captures)")
+    ap.add_argument("--vocab", type=int, default=None,
+                    help="profiling knob: a smaller vocabulary than the headline model")
     args = ap.parse_args()
     rank = _env_int("RANK", 0)
     world = _env_int("WORLD_SIZE", 1)
@@ -366,6 +370,12 @@ def main():
         ap.error("--warmup must be at least 3")
     if args.weak:
         args.streams *= world
+    if args.layers is not None or args.vocab is not None:
+        MODEL["n_layer"] = args.layers or MODEL["n_layer"]
+        MODEL["vocab"] = args.vocab or MODEL["vocab"]
+        global WORKLOAD
+        WORKLOAD = (f"profiling case: d1024 L{MODEL['n_layer']} V{MODEL['vocab']}, {args.streams} streams x "
+                    f"64-token prompts, greedy decode (not the headline configuration)")
     if args.impl == "reference":
         run_reference(args, rank)
         return

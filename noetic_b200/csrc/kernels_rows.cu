@@ -5,6 +5,8 @@
 // recurrent state h.  One conv_head per stream, shared by every layer (all
 // layers advance their head once per token, infer.rs:157).
 
+#include <algorithm>
+
 #include "nk_common.cuh"
 #include "nk_kernels.h"
 
@@ -12,7 +14,6 @@ namespace nk {
 
 namespace {
 
-constexpr int KMAX_UNROLLED = 8;
 constexpr int KMAX = 64;
 
 inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
@@ -49,9 +50,35 @@ __global__ void embed_prompt_k(const uint32_t *__restrict__ ids, const uint32_t 
     x[i] = emb[(size_t)tok * d + j];
 }
 
+// Stores one produced activation either as f32 or as the 3xTF32 operand pair
+// (hi = tf32(v), lo = tf32(v - hi)) that the tensor-core projection reads.
+__device__ __forceinline__ void put(const RowOut &o, size_t i, float v) {
+    if (o.hi) {
+        const float h = tf32_round(v);
+        o.hi[i] = h;
+        o.lo[i] = tf32_round(v - h);
+    } else {
+        o.f32[i] = v;
+    }
+}
+
+__device__ __forceinline__ void put4(const RowOut &o, size_t i, float4 v) {
+    if (o.hi) {
+        float4 h, l;
+        h.x = tf32_round(v.x); l.x = tf32_round(v.x - h.x);
+        h.y = tf32_round(v.y); l.y = tf32_round(v.y - h.y);
+        h.z = tf32_round(v.z); l.z = tf32_round(v.z - h.z);
+        h.w = tf32_round(v.w); l.w = tf32_round(v.w - h.w);
+        *reinterpret_cast<float4 *>(o.hi + i) = h;
+        *reinterpret_cast<float4 *>(o.lo + i) = l;
+    } else {
+        *reinterpret_cast<float4 *>(o.f32 + i) = v;
+    }
+}
+
 // One warp per row.
-__global__ void rmsnorm_k(const float *__restrict__ x, const float *__restrict__ gain, float eps,
-                          float *__restrict__ out, int M, int d) {
+__global__ void rmsnorm_k(const float *__restrict__ x, const float *__restrict__ gain, float eps, RowOut out,
+                          int M, int d) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= M) return;
@@ -60,8 +87,8 @@ __global__ void rmsnorm_k(const float *__restrict__ x, const float *__restrict__
     for (int j = lane; j < d; j += 32) ms = fmaf(xr[j], xr[j], ms);
     ms = warp_sum(ms);
     const float r = 1.0f / sqrtf(ms / (float)d + eps);
-    float *orow = out + (size_t)warp * d;
-    for (int j = lane; j < d; j += 32) orow[j] = xr[j] * r * gain[j];
+    const size_t base = (size_t)warp * d;
+    for (int j = lane; j < d; j += 32) put(out, base + j, xr[j] * r * gain[j]);
 }
 
 __global__ void advance_heads_k(uint32_t *heads, const uint32_t *adv, int S, int k) {
@@ -81,41 +108,84 @@ __global__ void advance_heads_prompt_k(uint32_t *heads, const uint32_t *lens, in
     heads[s] = (uint32_t)((heads[s] + (uint64_t)nv) % (uint32_t)k);
 }
 
-// infer.rs:155-176 for one (stream, channel).
-template <int K>
+// infer.rs:155-176 for VW consecutive channels of one stream (VW = 4 uses
+// 16-byte loads; rows of u, the ring, h and g are 16-byte aligned when E % 4 == 0).
+template <int K, int VW>
 __global__ void ssm_decode_k(const float *__restrict__ u, float *__restrict__ state,
                              const uint32_t *__restrict__ heads, const float *__restrict__ conv_w,
-                             const float *__restrict__ conv_b, float *__restrict__ g, int S, int E,
-                             int k_dyn) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (int64_t)S * E) return;
-    const int s = (int)(i / E), j = (int)(i - (int64_t)s * E);
+                             const float *__restrict__ conv_b, RowOut g, int S, int E, int k_dyn) {
     const int k = K > 0 ? K : k_dyn;
-    const float *ur = u + (size_t)s * 3 * E;
-    float *ring = state + (size_t)s * (k + 1) * E;
-    const uint32_t head = heads[s];
-    const float v = ur[j];
-    ring[(size_t)head * E + j] = v;
-    float sum = conv_b[j];
-    sum = sum + conv_w[j] * v;
-    if (K > 0) {
+    const int j0 = (blockIdx.x * blockDim.x + threadIdx.x) * VW;
+    if (j0 >= E) return;
+    for (int s = blockIdx.y; s < S; s += gridDim.y) {
+        const float *ur = u + (size_t)s * 3 * E;
+        float *ring = state + (size_t)s * (k + 1) * E;
+        const uint32_t head = heads[s];
+        float v[VW], sum[VW], z[VW], o[VW], h[VW];
+        if (VW == 4) {
+            const float4 a = *reinterpret_cast<const float4 *>(ur + j0);
+            const float4 b = *reinterpret_cast<const float4 *>(ur + E + j0);
+            const float4 c = *reinterpret_cast<const float4 *>(ur + 2 * E + j0);
+            const float4 hh = *reinterpret_cast<const float4 *>(ring + (size_t)k * E + j0);
+            const float4 cb = *reinterpret_cast<const float4 *>(conv_b + j0);
+            const float4 w0 = *reinterpret_cast<const float4 *>(conv_w + j0);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+            z[0] = b.x; z[1] = b.y; z[2] = b.z; z[3] = b.w;
+            o[0] = c.x; o[1] = c.y; o[2] = c.z; o[3] = c.w;
+            h[0] = hh.x; h[1] = hh.y; h[2] = hh.z; h[3] = hh.w;
+            sum[0] = cb.x + w0.x * v[0]; sum[1] = cb.y + w0.y * v[1];
+            sum[2] = cb.z + w0.z * v[2]; sum[3] = cb.w + w0.w * v[3];
+            *reinterpret_cast<float4 *>(ring + (size_t)head * E + j0) = a;
+        } else {
 #pragma unroll
-        for (int q = 1; q < (K > 0 ? K : 1); ++q) {
-            const uint32_t slot = (head + K - q) % K;
-            sum = sum + conv_w[(size_t)q * E + j] * ring[(size_t)slot * E + j];
+            for (int c = 0; c < VW; ++c) {
+                const int j = j0 + c;
+                v[c] = ur[j];
+                z[c] = ur[E + j];
+                o[c] = ur[2 * E + j];
+                h[c] = ring[(size_t)k * E + j];
+                sum[c] = conv_b[j] + conv_w[j] * v[c];
+                ring[(size_t)head * E + j] = v[c];
+            }
         }
-    } else {
+        // Older taps q = 1..k-1 (q = 0 is the value just written), q ascending
+        // as in the reference's sum.
         for (int q = 1; q < k; ++q) {
-            const uint32_t slot = (head + k - q) % k;
-            sum = sum + conv_w[(size_t)q * E + j] * ring[(size_t)slot * E + j];
+            const uint32_t slot = (head + (uint32_t)k - (uint32_t)q) % (uint32_t)k;
+            if (VW == 4) {
+                const float4 r = *reinterpret_cast<const float4 *>(ring + (size_t)slot * E + j0);
+                const float4 w = *reinterpret_cast<const float4 *>(conv_w + (size_t)q * E + j0);
+                sum[0] = sum[0] + w.x * r.x; sum[1] = sum[1] + w.y * r.y;
+                sum[2] = sum[2] + w.z * r.z; sum[3] = sum[3] + w.w * r.w;
+            } else {
+#pragma unroll
+                for (int c = 0; c < VW; ++c)
+                    sum[c] = sum[c] + conv_w[(size_t)q * E + j0 + c] * ring[(size_t)slot * E + j0 + c];
+            }
+        }
+        float gv[VW];
+#pragma unroll
+        for (int c = 0; c < VW; ++c) {
+            const float value = silu(sum[c]);
+            const float decay = sigmoid(z[c]);
+            h[c] = decay * h[c] + (1.0f - decay) * value;
+            gv[c] = h[c] * silu(o[c]);
+        }
+        const size_t gi = (size_t)s * E + j0;
+        if (VW == 4) {
+            float4 hh, gg;
+            hh.x = h[0]; hh.y = h[1]; hh.z = h[2]; hh.w = h[3];
+            gg.x = gv[0]; gg.y = gv[1]; gg.z = gv[2]; gg.w = gv[3];
+            *reinterpret_cast<float4 *>(ring + (size_t)k * E + j0) = hh;
+            put4(g, gi, gg);
+        } else {
+#pragma unroll
+            for (int c = 0; c < VW; ++c) {
+                ring[(size_t)k * E + j0 + c] = h[c];
+                put(g, gi + c, gv[c]);
+            }
         }
     }
-    const float value = silu(sum);
-    const float decay = sigmoid(ur[E + j]);
-    float *hp = ring + (size_t)k * E + j;
-    const float h = decay * (*hp) + (1.0f - decay) * value;
-    *hp = h;
-    g[(size_t)s * E + j] = h * silu(ur[2 * E + j]);
 }
 
 // Sequential-in-time prefill of one prompt chunk for one (stream, channel):
@@ -125,7 +195,7 @@ template <int K>
 __global__ void ssm_prefill_seq_k(const float *__restrict__ u, float *__restrict__ state,
                                   const uint32_t *__restrict__ heads, const uint32_t *__restrict__ lens,
                                   int t0, int tc, const float *__restrict__ conv_w,
-                                  const float *__restrict__ conv_b, float *__restrict__ y, int S,
+                                  const float *__restrict__ conv_b, RowOut y, int S,
                                   int E, int k_dyn) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)S * E) return;
@@ -155,7 +225,7 @@ __global__ void ssm_prefill_seq_k(const float *__restrict__ u, float *__restrict
     const float bias = conv_b[j];
     float h = ring[(size_t)k * E + j];
     const float *ur = u + (size_t)s * tc * 3 * E;
-    float *yr = y + (size_t)s * tc * E;
+    const size_t ybase = (size_t)s * tc * E + j;
     for (int t = 0; t < nv; ++t) {
         const float *row = ur + (size_t)t * 3 * E;
         const float v = row[j];
@@ -169,9 +239,9 @@ __global__ void ssm_prefill_seq_k(const float *__restrict__ u, float *__restrict
         const float value = silu(sum);
         const float decay = sigmoid(row[E + j]);
         h = decay * h + (1.0f - decay) * value;
-        yr[(size_t)t * E + j] = h * silu(row[2 * E + j]);
+        put(y, ybase + (size_t)t * E, h * silu(row[2 * E + j]));
     }
-    for (int t = nv; t < tc; ++t) yr[(size_t)t * E + j] = 0.0f;
+    for (int t = nv; t < tc; ++t) put(y, ybase + (size_t)t * E, 0.0f);
     if (nv > 0) {
         const uint32_t head1 = (uint32_t)((head0 + (uint64_t)nv) % (uint32_t)k);
 #pragma unroll
@@ -255,8 +325,8 @@ __global__ void ssm_chunk_carry_k(const float *__restrict__ state, const uint32_
 // block of each stream also writes h and the conv ring back to the state.
 __global__ void ssm_chunk_fix_k(const float *__restrict__ u, float *__restrict__ state,
                                 const uint32_t *__restrict__ heads, const uint32_t *__restrict__ lens,
-                                int t0, int tc, float *__restrict__ y, const float *__restrict__ carry,
-                                int S, int E, int k, int nblk) {
+                                int t0, int tc, const float *y, RowOut yout,
+                                const float *__restrict__ carry, int S, int E, int k, int nblk) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)S * nblk * E) return;
     const int j = (int)(i % E);
@@ -265,9 +335,10 @@ __global__ void ssm_chunk_fix_k(const float *__restrict__ u, float *__restrict__
     int nv = (int)lens[s] - t0;
     nv = nv < 0 ? 0 : (nv > tc ? tc : nv);
     const int p0 = c * TB, p1 = min(nv, p0 + TB);
-    float *yr = y + (size_t)s * tc * E;
+    const float *yr = y + (size_t)s * tc * E;
+    const size_t ybase = (size_t)s * tc * E + j;
     if (p0 >= p1) {
-        for (int p = max(p0, nv); p < min(tc, p0 + TB); ++p) yr[(size_t)p * E + j] = 0.0f;
+        for (int p = max(p0, nv); p < min(tc, p0 + TB); ++p) put(yout, ybase + (size_t)p * E, 0.0f);
         return;
     }
     const float *ur = u + (size_t)s * tc * 3 * E;
@@ -277,9 +348,9 @@ __global__ void ssm_chunk_fix_k(const float *__restrict__ u, float *__restrict__
         const float decay = sigmoid(ur[(size_t)p * 3 * E + E + j]);
         P = P * decay;
         h = yr[(size_t)p * E + j] + P * cin;
-        yr[(size_t)p * E + j] = h * silu(ur[(size_t)p * 3 * E + 2 * E + j]);
+        put(yout, ybase + (size_t)p * E, h * silu(ur[(size_t)p * 3 * E + 2 * E + j]));
     }
-    for (int p = p1; p < min(tc, p0 + TB); ++p) yr[(size_t)p * E + j] = 0.0f;
+    for (int p = p1; p < min(tc, p0 + TB); ++p) put(yout, ybase + (size_t)p * E, 0.0f);
     if (p1 == nv) {
         // Last block holding valid positions: write the state back.
         float *ring = state + (size_t)s * (k + 1) * E;
@@ -295,13 +366,41 @@ __global__ void ssm_chunk_fix_k(const float *__restrict__ u, float *__restrict__
     }
 }
 
-__global__ void swiglu_k(const float *__restrict__ up, float *__restrict__ s, int M, int H) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (int64_t)M * H) return;
-    const int64_t m = i / H;
-    const int j = (int)(i - m * H);
-    const float *r = up + (size_t)m * 2 * H;
-    s[i] = silu(r[j]) * r[H + j];
+template <int VW>
+__global__ void swiglu_k(const float *__restrict__ up, RowOut out, int M, int H) {
+    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * VW;
+    if (j >= H) return;
+    for (int m = blockIdx.y; m < M; m += gridDim.y) {
+        const float *r = up + (size_t)m * 2 * H;
+        const size_t o = (size_t)m * H + j;
+        if (VW == 4) {
+            const float4 a = *reinterpret_cast<const float4 *>(r + j);
+            const float4 b = *reinterpret_cast<const float4 *>(r + H + j);
+            float4 v;
+            v.x = silu(a.x) * b.x; v.y = silu(a.y) * b.y; v.z = silu(a.z) * b.z; v.w = silu(a.w) * b.w;
+            put4(out, o, v);
+        } else {
+            put(out, o, silu(r[j]) * r[H + j]);
+        }
+    }
+}
+
+// Per row: the best (value, index) over the column tiles' partial maxima,
+// earliest tile first on ties (argmax, tensor.rs:354-365).
+__global__ void argmax_partials_k(const float *__restrict__ val, const uint32_t *__restrict__ idx, int n_tiles,
+                                  int M, uint32_t *__restrict__ out) {
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= M) return;
+    float bv = -INFINITY;
+    uint32_t bi = 0;
+    for (int t = 0; t < n_tiles; ++t) {
+        const float v = val[(size_t)m * n_tiles + t];
+        if (v > bv) {
+            bv = v;
+            bi = idx[(size_t)m * n_tiles + t];
+        }
+    }
+    out[m] = bv == -INFINITY ? 0u : bi;
 }
 
 // Block per row: first index of the maximum over non-NaN entries; 0 when
@@ -411,7 +510,7 @@ cudaError_t embed_prompt_chunk(const uint32_t *ids, const uint32_t *lens, int ma
     return cudaGetLastError();
 }
 
-cudaError_t rmsnorm_rows(const float *x, const float *gain, float eps, float *out, int M, int d,
+cudaError_t rmsnorm_rows(const float *x, const float *gain, float eps, RowOut out, int M, int d,
                          cudaStream_t st) {
     if (M == 0) return cudaSuccess;
     rmsnorm_k<<<blocks_for((int64_t)M * 32, 256), 256, 0, st>>>(x, gain, eps, out, M, d);
@@ -432,23 +531,27 @@ cudaError_t advance_heads_prompt(uint32_t *heads, const uint32_t *lens, int t0, 
 }
 
 cudaError_t ssm_decode(const float *u, float *state, const uint32_t *heads, const float *conv_w,
-                       const float *conv_b, float *g, int S, int E, int k, cudaStream_t st) {
-    const int64_t n = (int64_t)S * E;
-    if (n == 0) return cudaSuccess;
-    const unsigned grid = blocks_for(n, 256);
-    switch (k) {
-#define NK_CASE(KK) \
-    case KK: ssm_decode_k<KK><<<grid, 256, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k); break;
+                       const float *conv_b, RowOut g, int S, int E, int k, cudaStream_t st) {
+    if ((int64_t)S * E == 0) return cudaSuccess;
+    const bool vec = (E % 4 == 0);
+    const int per = vec ? 4 : 1;
+    dim3 grid((unsigned)((E / per + 127) / 128), (unsigned)std::min(S, 65535));
+    switch (vec ? k : -k) {
+#define NK_CASE(KK)                                                                                             \
+    case KK: ssm_decode_k<KK, 4><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k); break;     \
+    case -KK: ssm_decode_k<KK, 1><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k); break;
         NK_CASE(1) NK_CASE(2) NK_CASE(3) NK_CASE(4) NK_CASE(5) NK_CASE(6) NK_CASE(7) NK_CASE(8)
 #undef NK_CASE
-        default: ssm_decode_k<0><<<grid, 256, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k);
+        default:
+            if (vec) ssm_decode_k<0, 4><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k);
+            else ssm_decode_k<0, 1><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k);
     }
     return cudaGetLastError();
 }
 
 cudaError_t ssm_prefill_seq(const float *u, float *state, const uint32_t *heads,
                             const uint32_t *lens, int t0, int tc, const float *conv_w,
-                            const float *conv_b, float *y, int S, int E, int k, cudaStream_t st) {
+                            const float *conv_b, RowOut y, int S, int E, int k, cudaStream_t st) {
     const int64_t n = (int64_t)S * E;
     if (n == 0) return cudaSuccess;
     if (k > KMAX) return cudaErrorInvalidValue;
@@ -475,8 +578,8 @@ size_t ssm_prefill_chunked_scratch_floats(int S, int E, int tc) {
 
 cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *heads,
                                 const uint32_t *lens, int t0, int tc, const float *conv_w,
-                                const float *conv_b, float *y, float *scratch, int S, int E, int k,
-                                cudaStream_t st) {
+                                const float *conv_b, float *y, RowOut yout, float *scratch, int S, int E,
+                                int k, cudaStream_t st) {
     if ((int64_t)S * E == 0 || tc == 0) return cudaSuccess;
     if (k > KMAX) return cudaErrorInvalidValue;
     const int nblk = (tc + TB - 1) / TB;
@@ -487,15 +590,25 @@ cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *he
                                                           conv_b, y, blkA, blkH, S, E, k, nblk);
     ssm_chunk_carry_k<<<blocks_for((int64_t)S * E, 128), 128, 0, st>>>(state, lens, t0, tc, blkA,
                                                                        blkH, carry, S, E, k, nblk);
-    ssm_chunk_fix_k<<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, y, carry, S,
-                                                        E, k, nblk);
+    ssm_chunk_fix_k<<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, y, yout, carry,
+                                                        S, E, k, nblk);
     return cudaGetLastError();
 }
 
-cudaError_t swiglu_rows(const float *up, float *s, int M, int H, cudaStream_t st) {
-    const int64_t n = (int64_t)M * H;
-    if (n == 0) return cudaSuccess;
-    swiglu_k<<<blocks_for(n, 256), 256, 0, st>>>(up, s, M, H);
+cudaError_t swiglu_rows(const float *up, RowOut s, int M, int H, cudaStream_t st) {
+    if ((int64_t)M * H == 0) return cudaSuccess;
+    const bool vec = (H % 4 == 0);
+    const int per = vec ? 4 : 1;
+    dim3 grid((unsigned)((H / per + 127) / 128), (unsigned)std::min(M, 65535));
+    if (vec) swiglu_k<4><<<grid, 128, 0, st>>>(up, s, M, H);
+    else swiglu_k<1><<<grid, 128, 0, st>>>(up, s, M, H);
+    return cudaGetLastError();
+}
+
+cudaError_t argmax_partials(const float *val, const uint32_t *idx, int n_tiles, int M, uint32_t *out,
+                            cudaStream_t st) {
+    if (M == 0) return cudaSuccess;
+    argmax_partials_k<<<blocks_for(M, 128), 128, 0, st>>>(val, idx, n_tiles, M, out);
     return cudaGetLastError();
 }
 

@@ -24,6 +24,16 @@ struct GemmArgs {
 
 constexpr int GEMV_MAX_ROWS = 8;
 
+// Where a producer kernel writes its activations: f32 (f32 != nullptr), or
+// the 3xTF32 operand pair hi = tf32(v), lo = tf32(v - hi) (hi, lo != nullptr)
+// that the tensor-core projection consumes directly.
+struct RowOut {
+    float *f32;
+    float *hi;
+    float *lo;
+};
+inline RowOut f32_out(float *p) { return RowOut{p, nullptr, nullptr}; }
+
 cudaError_t gemm_nt_simt(const GemmArgs &p, cudaStream_t st);
 
 // ---- elementwise / row kernels (kernels_rows.cu)
@@ -39,7 +49,7 @@ cudaError_t embed_prompt_chunk(const uint32_t *ids, const uint32_t *lens, int ma
                                cudaStream_t st);
 
 // out = x * (1 / sqrt(mean(x^2) + eps)) * gain, per row (tensor.rs:298-312).
-cudaError_t rmsnorm_rows(const float *x, const float *gain, float eps, float *out, int M, int d,
+cudaError_t rmsnorm_rows(const float *x, const float *gain, float eps, RowOut out, int M, int d,
                          cudaStream_t st);
 
 // heads[s] = (heads[s] + adv[s]) % k, adv == nullptr means +1.
@@ -52,24 +62,29 @@ cudaError_t advance_heads_prompt(uint32_t *heads, const uint32_t *lens, int t0, 
 // ring write, causal conv, SiLU, sigmoid decay, h update, output gate
 // (infer.rs:155-176).  heads[] are the already-advanced slots.
 cudaError_t ssm_decode(const float *u, float *state, const uint32_t *heads, const float *conv_w,
-                       const float *conv_b, float *g, int S, int E, int k, cudaStream_t st);
+                       const float *conv_b, RowOut g, int S, int E, int k, cudaStream_t st);
 
 // Prefill of one prompt chunk for layer state [S][k+1][E] (sequential in time
 // per (stream, channel)); y[S*tc, E]; heads[] are the slots at chunk start.
 cudaError_t ssm_prefill_seq(const float *u, float *state, const uint32_t *heads,
                             const uint32_t *lens, int t0, int tc, const float *conv_w,
-                            const float *conv_b, float *y, int S, int E, int k, cudaStream_t st);
+                            const float *conv_b, RowOut y, int S, int E, int k, cudaStream_t st);
 
 // Same result, time-parallel: local scans over time blocks, carry composition,
 // fix-up (the chunked associative scan of scan.rs:98-225 fused with the conv).
+// y [S*tc, E] f32 holds the local scans; the gated output goes to yout.
 cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *heads,
                                 const uint32_t *lens, int t0, int tc, const float *conv_w,
-                                const float *conv_b, float *y, float *scratch, int S, int E, int k,
-                                cudaStream_t st);
+                                const float *conv_b, float *y, RowOut yout, float *scratch, int S, int E,
+                                int k, cudaStream_t st);
 size_t ssm_prefill_chunked_scratch_floats(int S, int E, int tc);
 
 // s[m,j] = SiLU(up[m,j]) * up[m,H+j] (infer.rs:188-190).
-cudaError_t swiglu_rows(const float *up, float *s, int M, int H, cudaStream_t st);
+cudaError_t swiglu_rows(const float *up, RowOut s, int M, int H, cudaStream_t st);
+
+// out[m] = argmax over per-tile partial maxima (val/idx [M, n_tiles]).
+cudaError_t argmax_partials(const float *val, const uint32_t *idx, int n_tiles, int M, uint32_t *out,
+                            cudaStream_t st);
 
 // out[m] = argmax(x[m,:]) (tensor.rs:354-365), first strict maximum, NaN skipped.
 cudaError_t argmax_rows(const float *x, uint32_t *out, int M, int V, cudaStream_t st);

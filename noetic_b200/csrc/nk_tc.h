@@ -32,22 +32,34 @@ struct TcSource {
     int N, K;
 };
 
-// Activation operand staging (hi/lo split of A) reused across calls.
-struct TcScratch {
-    float *a_hi = nullptr, *a_lo = nullptr;
-    size_t cap = 0;  // floats per buffer
+// Epilogue of one projection: either store C = acc (+ bias) (R + ...), or
+// (best_val != nullptr) write each row's first maximum over every 256-column
+// tile into best_val / best_idx [M, tc_tiles_n(N)] without storing C.
+struct TcEpilogue {
+    float *C = nullptr;
+    int ldc = 0;
+    const float *bias = nullptr;
+    const float *R = nullptr;
+    int ldr = 0;
+    float *best_val = nullptr;
+    uint32_t *best_idx = nullptr;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.
 bool tc_eligible(int M, int N, int K);
 
+// Number of 256-column tiles of an N-wide projection.
+int tc_tiles_n(int N);
+
 cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs);
 void tc_weights_free(TcWeights &w);
-void tc_scratch_free(TcScratch &s);
 
-// C = epilogue(A . W^T) with the same epilogue as gemm_nt_simt.  A kernel
-// whose bounded waits expire writes a nonzero code to *err (device int).
-cudaError_t tc_gemm(const GemmArgs &p, const TcOperand &W, TcScratch &s, cudaStream_t st, int *err,
-                    int *launches);
+// hi = tf32(A), lo = tf32(A - hi) for an f32 operand [rows, cols] (row stride lda).
+cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st);
+
+// epilogue(A . W^T) with A given as its hi/lo operand pair [M, K] (dense).
+// A kernel whose bounded waits expire writes a nonzero code to *err.
+cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
+                    cudaStream_t st, int *err);
 
 }  // namespace nk

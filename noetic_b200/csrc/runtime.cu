@@ -435,7 +435,12 @@ struct nk_decoder {
     size_t p_rows = 0, p_scan_floats = 0;
     uint32_t *p_ids = nullptr, *p_lens = nullptr;
     size_t p_ids_cap = 0;
-    nk::TcScratch tcs;
+    // 3xTF32 activation operand pair (decode) and the fused argmax partials
+    float *ahi = nullptr, *alo = nullptr;
+    float *best_val = nullptr;
+    uint32_t *best_idx = nullptr;
+    // prefill operand pair
+    float *p_ahi = nullptr, *p_alo = nullptr;
     // projection profiling (CUDA events around each projection launch)
     bool profiling = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -457,7 +462,8 @@ struct nk_decoder {
                         (void *)p_y, (void *)p_last, (void *)p_scan, (void *)p_logits, (void *)p_ids,
                         (void *)p_lens})
             if (p) cudaFree(p);
-        nk::tc_scratch_free(tcs);
+        for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo})
+            if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -486,27 +492,77 @@ cudaEvent_t prof_event(nk_decoder *dec) {
     return dec->ev_pool[dec->ev_used++];
 }
 
-void project(nk_decoder *dec, const float *A, int M, int K, const float *W, const nk::TcOperand *Wtc,
-             int N, const float *bias, float *C, const float *R) {
-    nk::GemmArgs p{A, K, W, K, C, N, M, N, K, bias, R, N};
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
-    if (dec->profiling) {
-        e0 = prof_event(dec);
+// Which engine runs a projection of this shape: the tcgen05 3xTF32 kernel
+// when eligible, else the f32 CUDA-core kernels.  The producer of the
+// projection's input writes the operand form the chosen engine reads.
+bool use_tc(const nk_decoder *dec, int M, int N, int K, const nk::TcOperand *Wtc) {
+    return !(dec->engine & 1) && Wtc && nk::tc_eligible(M, N, K);
+}
+
+// An activation buffer in both forms: f32 for the CUDA-core engine, the hi/lo
+// pair for the tensor-core engine.
+struct Act {
+    float *f32, *hi, *lo;
+    nk::RowOut out(bool tc) const { return tc ? nk::RowOut{nullptr, hi, lo} : nk::RowOut{f32, nullptr, nullptr}; }
+};
+
+struct ProfScope {
+    nk_decoder *dec;
+    cudaEvent_t e1 = nullptr;
+    ProfScope(nk_decoder *d, int M, int N, int K, bool residual, bool bias) : dec(d) {
+        if (!dec->profiling) return;
+        cudaEvent_t e0 = prof_event(dec);
         e1 = prof_event(dec);
         cuda_check(cudaEventRecord(e0, dec->stream), "cudaEventRecord");
         dec->prof_flops += 2.0 * M * (double)N * K;
-        dec->prof_bytes += 4.0 * ((double)M * K + (double)N * K + (double)M * N * (R ? 2 : 1) + (bias ? N : 0));
+        dec->prof_bytes += 4.0 * ((double)M * K + (double)N * K + (double)M * N * (residual ? 2 : 1) + (bias ? N : 0));
         dec->prof_proj += 1;
     }
-    if (!(dec->engine & 1) && Wtc && nk::tc_eligible(M, N, K)) {
-        int launches = 0;
-        cuda_check(nk::tc_gemm(p, *Wtc, dec->tcs, dec->stream, dec->err, &launches), "tcgen05 projection");
-        dec->launches += (uint64_t)launches;
+    ~ProfScope() {
+        if (e1) cudaEventRecord(e1, dec->stream);
+    }
+};
+
+// C = A.W^T (+bias) (R + ...), A read from `a` in the form `tc` selects.
+void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W, const nk::TcOperand *Wtc,
+             int N, const float *bias, float *C, const float *R) {
+    ProfScope prof(dec, M, N, K, R != nullptr, bias != nullptr);
+    if (tc) {
+        nk::TcEpilogue ep;
+        ep.C = C;
+        ep.ldc = N;
+        ep.bias = bias;
+        ep.R = R;
+        ep.ldr = N;
+        cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, dec->stream, dec->err), "tcgen05 projection");
+        dec->launches += 1;
         dec->prof_tc = dec->prof_tc || dec->profiling;
     } else {
+        nk::GemmArgs p{a.f32, K, W, K, C, N, M, N, K, bias, R, N};
         launch_ok(dec, nk::gemm_nt_simt(p, dec->stream), "f32 projection");
     }
-    if (dec->profiling) cuda_check(cudaEventRecord(e1, dec->stream), "cudaEventRecord");
+}
+
+// tokens[m] = argmax_n (A.W^T)[m, n] without storing the product when the
+// tensor-core engine runs it (first strict maximum, tensor.rs:354-365).
+void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W,
+                    const nk::TcOperand *Wtc, int N, uint32_t *tokens) {
+    if (tc) {
+        {
+            ProfScope prof(dec, M, N, K, false, false);
+            nk::TcEpilogue ep;
+            ep.best_val = dec->best_val;
+            ep.best_idx = dec->best_idx;
+            cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, dec->stream, dec->err), "tcgen05 projection");
+            dec->launches += 1;
+            dec->prof_tc = dec->prof_tc || dec->profiling;
+        }
+        launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, nk::tc_tiles_n(N), M, tokens, dec->stream),
+                  "argmax partials");
+    } else {
+        project(dec, false, a, M, K, W, Wtc, N, nullptr, dec->logits, nullptr);
+        launch_ok(dec, nk::argmax_rows(dec->logits, tokens, M, N, dec->stream), "argmax");
+    }
 }
 
 void ensure_ready(nk_decoder *dec) {
@@ -544,27 +600,41 @@ void check_err_flag(nk_decoder *dec) {
 }
 
 // Decoder::step over every stream (infer.rs:106-200), tokens on the device.
-void step_device(nk_decoder *dec, const uint32_t *tokens) {
+// With tokens_out, the step ends in the greedy choice (sample_token with
+// greedy and no penalty); the logits are then stored only if want_logits.
+void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
     nk_model *m = dec->model;
     const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(),
               k = (int)m->k(), V = (int)m->cfg.vocab;
     cudaStream_t st = dec->stream;
+    const Act nrm{dec->nrm, dec->ahi, dec->alo}, gated{dec->g, dec->ahi, dec->alo};
     launch_ok(dec, nk::embed_rows(tokens, m->dp(m->emb), dec->x, S, d, V, dec->err, st), "embed");
     launch_ok(dec, nk::advance_heads(dec->heads, nullptr, S, k, st), "advance heads");
     for (uint64_t l = 0; l < m->cfg.n_layer; ++l) {
         const LayerIx &L = m->layers[l];
-        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n1), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
-        project(dec, dec->nrm, S, d, m->dp(L.in_w), tc_op(m, 4 * l + 0), 3 * E, m->dp(L.in_b), dec->u, nullptr);
-        launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w),
-                                      m->dp(L.conv_b), dec->g, S, E, k, st), "ssm step");
-        project(dec, dec->g, S, E, m->dp(L.out_w), tc_op(m, 4 * l + 1), d, m->dp(L.out_b), dec->x, dec->x);
-        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n2), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
-        project(dec, dec->nrm, S, d, m->dp(L.up_w), tc_op(m, 4 * l + 2), 2 * H, m->dp(L.up_b), dec->u, nullptr);
-        launch_ok(dec, nk::swiglu_rows(dec->u, dec->g, S, H, st), "swiglu");
-        project(dec, dec->g, S, H, m->dp(L.down_w), tc_op(m, 4 * l + 3), d, m->dp(L.down_b), dec->x, dec->x);
+        const nk::TcOperand *w_in = tc_op(m, 4 * l + 0), *w_out = tc_op(m, 4 * l + 1), *w_up = tc_op(m, 4 * l + 2),
+                            *w_dn = tc_op(m, 4 * l + 3);
+        const bool t_in = use_tc(dec, S, 3 * E, d, w_in), t_out = use_tc(dec, S, d, E, w_out),
+                   t_up = use_tc(dec, S, 2 * H, d, w_up), t_dn = use_tc(dec, S, d, H, w_dn);
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n1), m->cfg.eps, nrm.out(t_in), S, d, st), "rmsnorm");
+        project(dec, t_in, nrm, S, d, m->dp(L.in_w), w_in, 3 * E, m->dp(L.in_b), dec->u, nullptr);
+        launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w), m->dp(L.conv_b),
+                                      gated.out(t_out), S, E, k, st), "ssm step");
+        project(dec, t_out, gated, S, E, m->dp(L.out_w), w_out, d, m->dp(L.out_b), dec->x, dec->x);
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n2), m->cfg.eps, nrm.out(t_up), S, d, st), "rmsnorm");
+        project(dec, t_up, nrm, S, d, m->dp(L.up_w), w_up, 2 * H, m->dp(L.up_b), dec->u, nullptr);
+        launch_ok(dec, nk::swiglu_rows(dec->u, gated.out(t_dn), S, H, st), "swiglu");
+        project(dec, t_dn, gated, S, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->x, dec->x);
     }
-    launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
-    project(dec, dec->nrm, S, d, m->dp(m->emb), tc_op(m, 4 * m->cfg.n_layer), V, nullptr, dec->logits, nullptr);
+    const nk::TcOperand *w_lg = tc_op(m, 4 * m->cfg.n_layer);
+    const bool t_lg = use_tc(dec, S, V, d, w_lg);
+    launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, nrm.out(t_lg), S, d, st), "rmsnorm");
+    if (want_logits || !tokens_out) {
+        project(dec, t_lg, nrm, S, d, m->dp(m->emb), w_lg, V, nullptr, dec->logits, nullptr);
+        if (tokens_out) launch_ok(dec, nk::argmax_rows(dec->logits, tokens_out, S, V, st), "argmax");
+    } else {
+        project_argmax(dec, t_lg, nrm, S, d, m->dp(m->emb), w_lg, V, tokens_out);
+    }
 }
 
 void validate_tokens(const nk_model *m, const uint32_t *t, size_t n) {
@@ -582,18 +652,22 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
     cudaStream_t st = dec->stream;
     if (max_t == 0) return;
     // Rows per chunk: bounded scratch (about 3 GiB at most).
-    const size_t row_bytes = 4 * (2 * (size_t)d + std::max(3 * (size_t)E, 2 * (size_t)H) + std::max((size_t)E, (size_t)H));
+    const size_t row_bytes = 4 * (2 * (size_t)d + std::max(3 * (size_t)E, 2 * (size_t)H) + std::max((size_t)E, (size_t)H) +
+                                  2 * std::max({(size_t)d, (size_t)E, (size_t)H}));
     size_t rows_budget = std::max<size_t>((size_t)3 << 30, 0) / row_bytes;
     rows_budget = std::min<size_t>(std::max<size_t>(rows_budget, (size_t)S), (size_t)1 << 20);
     int tc = (int)std::max<size_t>(1, std::min<size_t>(max_t, rows_budget / (size_t)S));
     const size_t rows = (size_t)S * tc;
+    const size_t act_w = std::max({(size_t)d, (size_t)E, (size_t)H});
     if (rows > dec->p_rows) {
-        for (float **p : {&dec->p_x, &dec->p_n, &dec->p_u, &dec->p_y})
+        for (float **p : {&dec->p_x, &dec->p_n, &dec->p_u, &dec->p_y, &dec->p_ahi, &dec->p_alo})
             if (*p) cudaFree(*p), *p = nullptr;
         dalloc(&dec->p_x, rows * d, "prefill x");
         dalloc(&dec->p_n, rows * d, "prefill norm");
         dalloc(&dec->p_u, rows * std::max(3 * E, 2 * H), "prefill projection");
         dalloc(&dec->p_y, rows * std::max(E, H), "prefill gated");
+        dalloc(&dec->p_ahi, rows * act_w, "prefill operand hi");
+        dalloc(&dec->p_alo, rows * act_w, "prefill operand lo");
         dec->p_rows = rows;
     }
     if (!dec->p_last) dalloc(&dec->p_last, (size_t)S * d, "prefill last rows");
@@ -614,25 +688,29 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
         const int R = S * tcc;
         launch_ok(dec, nk::embed_prompt_chunk(d_ids, d_lens, (int)max_t, (int)t0, tcc, m->dp(m->emb),
                                               dec->p_x, S, d, V, dec->err, st), "prompt embed");
+        const Act nrm{dec->p_n, dec->p_ahi, dec->p_alo}, gated{dec->p_y, dec->p_ahi, dec->p_alo};
         for (uint64_t l = 0; l < m->cfg.n_layer; ++l) {
             const LayerIx &L = m->layers[l];
-            launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n1), m->cfg.eps, dec->p_n, R, d, st), "rmsnorm");
-            project(dec, dec->p_n, R, d, m->dp(L.in_w), tc_op(m, 4 * l + 0), 3 * E, m->dp(L.in_b), dec->p_u, nullptr);
+            const nk::TcOperand *w_in = tc_op(m, 4 * l + 0), *w_out = tc_op(m, 4 * l + 1),
+                                *w_up = tc_op(m, 4 * l + 2), *w_dn = tc_op(m, 4 * l + 3);
+            const bool t_in = use_tc(dec, R, 3 * E, d, w_in), t_out = use_tc(dec, R, d, E, w_out),
+                       t_up = use_tc(dec, R, 2 * H, d, w_up), t_dn = use_tc(dec, R, d, H, w_dn);
+            launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n1), m->cfg.eps, nrm.out(t_in), R, d, st), "rmsnorm");
+            project(dec, t_in, nrm, R, d, m->dp(L.in_w), w_in, 3 * E, m->dp(L.in_b), dec->p_u, nullptr);
             if (chunked)
-                launch_ok(dec, nk::ssm_prefill_chunked(dec->p_u, dec->layer_state(l), dec->heads, d_lens,
-                                                       (int)t0, tcc, m->dp(L.conv_w), m->dp(L.conv_b),
-                                                       dec->p_y, dec->p_scan, S, E, k, st),
+                launch_ok(dec, nk::ssm_prefill_chunked(dec->p_u, dec->layer_state(l), dec->heads, d_lens, (int)t0, tcc,
+                                                       m->dp(L.conv_w), m->dp(L.conv_b), dec->p_y, gated.out(t_out),
+                                                       dec->p_scan, S, E, k, st),
                           "prefill scan", 3);
             else
-                launch_ok(dec, nk::ssm_prefill_seq(dec->p_u, dec->layer_state(l), dec->heads, d_lens,
-                                                   (int)t0, tcc, m->dp(L.conv_w), m->dp(L.conv_b),
-                                                   dec->p_y, S, E, k, st),
+                launch_ok(dec, nk::ssm_prefill_seq(dec->p_u, dec->layer_state(l), dec->heads, d_lens, (int)t0, tcc,
+                                                   m->dp(L.conv_w), m->dp(L.conv_b), gated.out(t_out), S, E, k, st),
                           "prefill scan");
-            project(dec, dec->p_y, R, E, m->dp(L.out_w), tc_op(m, 4 * l + 1), d, m->dp(L.out_b), dec->p_x, dec->p_x);
-            launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n2), m->cfg.eps, dec->p_n, R, d, st), "rmsnorm");
-            project(dec, dec->p_n, R, d, m->dp(L.up_w), tc_op(m, 4 * l + 2), 2 * H, m->dp(L.up_b), dec->p_u, nullptr);
-            launch_ok(dec, nk::swiglu_rows(dec->p_u, dec->p_y, R, H, st), "swiglu");
-            project(dec, dec->p_y, R, H, m->dp(L.down_w), tc_op(m, 4 * l + 3), d, m->dp(L.down_b), dec->p_x, dec->p_x);
+            project(dec, t_out, gated, R, E, m->dp(L.out_w), w_out, d, m->dp(L.out_b), dec->p_x, dec->p_x);
+            launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n2), m->cfg.eps, nrm.out(t_up), R, d, st), "rmsnorm");
+            project(dec, t_up, nrm, R, d, m->dp(L.up_w), w_up, 2 * H, m->dp(L.up_b), dec->p_u, nullptr);
+            launch_ok(dec, nk::swiglu_rows(dec->p_u, gated.out(t_dn), R, H, st), "swiglu");
+            project(dec, t_dn, gated, R, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->p_x, dec->p_x);
         }
         launch_ok(dec, nk::gather_last_rows(dec->p_x, d_lens, (int)t0, tcc, dec->p_last, S, d, st), "gather last");
         launch_ok(dec, nk::advance_heads_prompt(dec->heads, d_lens, (int)t0, tcc, S, k, st), "advance heads");
@@ -642,17 +720,21 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
     for (int s = 0; s < S; ++s)
         if (lens[s] > 0) live.push_back((uint32_t)s);
     if (live.empty()) return;
+    const nk::TcOperand *w_lg = tc_op(m, 4 * m->cfg.n_layer);
+    const Act nrm{dec->nrm, dec->ahi, dec->alo};
     if ((int)live.size() == S) {
-        launch_ok(dec, nk::rmsnorm_rows(dec->p_last, m->dp(m->norm_f), m->cfg.eps, dec->nrm, S, d, st), "rmsnorm");
-        project(dec, dec->nrm, S, d, m->dp(m->emb), tc_op(m, 4 * m->cfg.n_layer), V, nullptr, dec->logits, nullptr);
+        const bool t_lg = use_tc(dec, S, V, d, w_lg);
+        launch_ok(dec, nk::rmsnorm_rows(dec->p_last, m->dp(m->norm_f), m->cfg.eps, nrm.out(t_lg), S, d, st), "rmsnorm");
+        project(dec, t_lg, nrm, S, d, m->dp(m->emb), w_lg, V, nullptr, dec->logits, nullptr);
     } else {
         const int n = (int)live.size();
+        const bool t_lg = use_tc(dec, n, V, d, w_lg);
         uint32_t *d_idx = dec->tok_b;  // S u32 of scratch
         cuda_check(cudaMemcpyAsync(d_idx, live.data(), n * sizeof(uint32_t), cudaMemcpyHostToDevice, st), "upload index");
         launch_ok(dec, nk::gather_rows(dec->p_last, d_idx, dec->x, n, d, st), "gather");
-        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, dec->nrm, n, d, st), "rmsnorm");
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, nrm.out(t_lg), n, d, st), "rmsnorm");
         if (!dec->p_logits) dalloc(&dec->p_logits, (size_t)S * V, "compacted logits");
-        project(dec, dec->nrm, n, d, m->dp(m->emb), tc_op(m, 4 * m->cfg.n_layer), V, nullptr, dec->p_logits, nullptr);
+        project(dec, t_lg, nrm, n, d, m->dp(m->emb), w_lg, V, nullptr, dec->p_logits, nullptr);
         launch_ok(dec, nk::scatter_rows(dec->p_logits, d_idx, dec->logits, n, V, st), "scatter");
         cuda_check(cudaStreamSynchronize(st), "cudaStreamSynchronize");
     }
@@ -903,6 +985,11 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         dalloc(&dec->u, S * std::max(3 * E, 2 * H), "projection");
         dalloc(&dec->g, S * std::max(E, H), "gated");
         dalloc(&dec->logits, S * V, "logits");
+        const size_t act_w = std::max({d, E, H});
+        dalloc(&dec->ahi, S * act_w, "operand hi");
+        dalloc(&dec->alo, S * act_w, "operand lo");
+        dalloc(&dec->best_val, S * (size_t)nk::tc_tiles_n((int)V), "argmax partials");
+        dalloc(&dec->best_idx, S * (size_t)nk::tc_tiles_n((int)V), "argmax partials");
         dalloc(&dec->tok_a, S, "tokens");
         dalloc(&dec->tok_b, S, "tokens");
         dalloc(&dec->err, 1, "error flag");
@@ -953,7 +1040,7 @@ nk_status nk_decoder_step(nk_decoder *dec, const uint32_t *tokens, float *logits
         ensure_ready(dec);
         cuda_check(cudaMemcpyAsync(dec->tok_a, tokens, dec->S * sizeof(uint32_t), cudaMemcpyHostToDevice,
                                    dec->stream), "upload tokens");
-        step_device(dec, dec->tok_a);
+        step_device(dec, dec->tok_a, true, nullptr);
         if (logits_out)
             cuda_check(cudaMemcpyAsync(logits_out, dec->logits, (size_t)dec->S * dec->model->cfg.vocab * sizeof(float),
                                        cudaMemcpyDeviceToHost, dec->stream), "download logits");
@@ -965,9 +1052,7 @@ nk_status nk_decoder_step_greedy_device(nk_decoder *dec, const uint32_t *tokens_
     return guard([&] {
         if (!dec || !tokens_in || !tokens_out) fail(NK_ERR_INVALID, "null argument");
         ensure_ready(dec);
-        step_device(dec, tokens_in);
-        launch_ok(dec, nk::argmax_rows(dec->logits, tokens_out, (int)dec->S, (int)dec->model->cfg.vocab, dec->stream),
-                  "argmax");
+        step_device(dec, tokens_in, false, tokens_out);
     });
 }
 
@@ -978,9 +1063,7 @@ nk_status nk_decoder_step_greedy(nk_decoder *dec, const uint32_t *tokens_in, uin
         ensure_ready(dec);
         cuda_check(cudaMemcpyAsync(dec->tok_a, tokens_in, dec->S * sizeof(uint32_t), cudaMemcpyHostToDevice,
                                    dec->stream), "upload tokens");
-        step_device(dec, dec->tok_a);
-        launch_ok(dec, nk::argmax_rows(dec->logits, dec->tok_b, (int)dec->S, (int)dec->model->cfg.vocab, dec->stream),
-                  "argmax");
+        step_device(dec, dec->tok_a, false, dec->tok_b);
         cuda_check(cudaMemcpyAsync(tokens_out, dec->tok_b, dec->S * sizeof(uint32_t), cudaMemcpyDeviceToHost,
                                    dec->stream), "download tokens");
         check_err_flag(dec);
@@ -1088,7 +1171,7 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
             cuda_check(cudaMemcpy2DAsync(d_out + gi, (size_t)n_new * sizeof(uint32_t), dec->tok_b, sizeof(uint32_t),
                                          sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, dec->stream), "collect tokens");
             if (W > 0) launch_ok(dec, nk::history_push(dec->hist, dec->hist_len, dec->tok_b, (int)S, (int)W, dec->stream), "history");
-            if (gi + 1 < n_new) step_device(dec, dec->tok_b);
+            if (gi + 1 < n_new) step_device(dec, dec->tok_b, true, nullptr);
         }
         if (n_new)
             cuda_check(cudaMemcpyAsync(out_tokens, d_out, (size_t)S * n_new * sizeof(uint32_t), cudaMemcpyDeviceToHost,

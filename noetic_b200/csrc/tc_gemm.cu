@@ -8,9 +8,9 @@
 // activation operand is split by a small pre-pass per projection.
 //
 // Kernel structure (one 128 x 256 output tile per CTA, 256 threads):
-//   warp 0      TMA producer: K-blocks of 32 f32 (one 128-byte swizzle row)
-//               for A_hi, A_lo, W_hi, W_lo into a 2-stage smem ring
-//               (cp.async.bulk.tensor, 128B swizzle, zero fill out of bounds);
+//   warp 0      TMA producer: K-blocks of 16 f32 (one 64-byte swizzle row)
+//               for A_hi, A_lo, W_hi, W_lo into a 4-stage smem ring
+//               (cp.async.bulk.tensor, 64B swizzle, zero fill out of bounds);
 //   warp 1      TMEM allocator and MMA issuer: per K-block, 4 k-steps x 3
 //               tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=256, K=8):
 //               hi*hi into one f32 TMEM accumulator, hi*lo and lo*hi into a
@@ -39,11 +39,15 @@ namespace nk {
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 32;
-constexpr int STAGES = 2;
-constexpr int A_BYTES = BM * BK * 4;                       // 16 KiB
-constexpr int B_BYTES = BN * BK * 4;                       // 32 KiB
-constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;     // 96 KiB
+// BK = 16 f32 = one 64-byte swizzle row; four stages keep three K-blocks of
+// loads in flight ahead of the MMAs.
+constexpr int BM = 128, BN = 256, BK = 16;
+constexpr int STAGES = 4;
+constexpr int SWIZZLE_BYTES = BK * 4;                       // 64
+constexpr int ATOM_BYTES = 8 * SWIZZLE_BYTES;               // 8 rows: 512
+constexpr int A_BYTES = BM * BK * 4;                       // 8 KiB
+constexpr int B_BYTES = BN * BK * 4;                       // 16 KiB
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;     // 48 KiB
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int THREADS = 256;
 // Two f32 accumulators of BN columns: the hi*hi products and the two small
@@ -62,6 +66,9 @@ struct TcArgs {
     const float *bias;
     const float *R;
     int ldr;
+    float *best_val;     // argmax mode when non-null: per-row best of this tile
+    uint32_t *best_idx;
+    int n_tiles;
     int *err;
 };
 
@@ -107,10 +114,11 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
-// K-major operand, 128-byte swizzle, 8-row groups 1024 bytes apart.
+// K-major operand with the 64-byte swizzle (layout type 4): rows of 64 bytes,
+// 8-row groups ATOM_BYTES apart.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) |
-           (2ull << 61);
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(ATOM_BYTES >> 4) << 32) | (1ull << 46) |
+           (4ull << 61);
 }
 
 __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
@@ -144,7 +152,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-byte aligned tile area (the 128B swizzle pattern repeats every 1 KiB).
+    // 1024-byte aligned tile area (swizzle atoms must not straddle their period).
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES);  // full[S], empty[S], accum
     uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 1);
@@ -266,6 +274,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int row = m0 + q * 32 + lane;
             const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
+            const bool argmax_mode = p.best_val != nullptr;
+            float best = -INFINITY;
+            uint32_t best_n = 0xFFFFFFFFu;
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 if (n0 + c0 >= p.N) break;  // warp-uniform
                 float v[32], corr[32];
@@ -273,8 +284,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = v[j] + corr[j];
+                const int nb = n0 + c0;
+                if (argmax_mode) {
+                    // First strict maximum over this tile's columns, NaN skipped.
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        float o = v[j];
+                        if (p.bias && nb + j < p.N) o = o + p.bias[nb + j];
+                        if (nb + j < p.N && !isnan(o) && o > best) {
+                            best = o;
+                            best_n = (uint32_t)(nb + j);
+                        }
+                    }
+                    continue;
+                }
                 if (row < p.M) {
-                    const int nb = n0 + c0;
                     float *crow = p.C + (size_t)row * p.ldc;
                     const float *rrow = p.R ? p.R + (size_t)row * p.ldr : nullptr;
                     if (vec && nb + 32 <= p.N) {
@@ -305,6 +329,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                         }
                     }
                 }
+            }
+            if (argmax_mode && row < p.M) {
+                p.best_val[(size_t)row * p.n_tiles + blockIdx.x] = best;
+                p.best_idx[(size_t)row * p.n_tiles + blockIdx.x] = best_n;
             }
         }
     }
@@ -344,7 +372,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D f32 map over [rows, cols] (cols contiguous), box {BK, box_rows}, 128B
+// 2-D f32 map over [rows, cols] (cols contiguous), box {BK, box_rows}, 64B
 // swizzle, zero fill outside the tensor.
 bool make_map(CUtensorMap *map, const float *base, int rows, int cols, int box_rows) {
     auto fn = encode_fn();
@@ -354,7 +382,7 @@ bool make_map(CUtensorMap *map, const float *base, int rows, int cols, int box_r
     cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -370,6 +398,12 @@ cudaError_t split(const float *src, int ld, float *hi, float *lo, int rows, int 
 
 bool tc_eligible(int M, int N, int K) {
     return M >= BM && N >= BN && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
+}
+
+int tc_tiles_n(int N) { return (N + BN - 1) / BN; }
+
+cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
+    return split(A, lda, hi, lo, rows, cols, st);
 }
 
 cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs) {
@@ -413,46 +447,24 @@ void tc_weights_free(TcWeights &w) {
     w.ready = false;
 }
 
-void tc_scratch_free(TcScratch &s) {
-    if (s.a_hi) cudaFree(s.a_hi);
-    if (s.a_lo) cudaFree(s.a_lo);
-    s = TcScratch{};
-}
-
-cudaError_t tc_gemm(const GemmArgs &p, const TcOperand &W, TcScratch &s, cudaStream_t st, int *err,
-                    int *launches) {
-    if (launches) *launches = 0;
-    if (W.K != p.K || W.N != p.N) return cudaErrorInvalidValue;
-    const size_t need = (size_t)p.M * p.K;
-    if (need > s.cap) {
-        if (s.a_hi) cudaFree(s.a_hi);
-        if (s.a_lo) cudaFree(s.a_lo);
-        s.a_hi = s.a_lo = nullptr;
-        s.cap = 0;
-        cudaError_t e = cudaMalloc(&s.a_hi, need * sizeof(float));
-        if (e != cudaSuccess) return e;
-        e = cudaMalloc(&s.a_lo, need * sizeof(float));
-        if (e != cudaSuccess) return e;
-        s.cap = need;
-    }
-    cudaError_t e = split(p.A, p.lda, s.a_hi, s.a_lo, p.M, p.K, st);
-    if (e != cudaSuccess) return e;
+cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
+                    cudaStream_t st, int *err) {
+    if (W.K != K || M <= 0) return cudaErrorInvalidValue;
     alignas(64) CUtensorMap mAh, mAl;
-    if (!make_map(&mAh, s.a_hi, p.M, p.K, BM) || !make_map(&mAl, s.a_lo, p.M, p.K, BM)) return cudaErrorInvalidValue;
+    if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
     static thread_local int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_dev != dev) {
-        e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr_dev = dev;
     }
-    TcArgs a{p.C, p.ldc, p.M, p.N, p.K, p.bias, p.R, p.ldr, err};
-    dim3 grid((p.N + BN - 1) / BN, (p.M + BM - 1) / BM);
+    TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_tiles_n(W.N), err};
+    dim3 grid((unsigned)tc_tiles_n(W.N), (unsigned)((M + BM - 1) / BM));
     tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(*(const CUtensorMap *)&mAh, *(const CUtensorMap *)&mAl,
                                                      *(const CUtensorMap *)W.map_hi,
                                                      *(const CUtensorMap *)W.map_lo, a);
-    if (launches) *launches = 2;
     return cudaGetLastError();
 }
 

@@ -94,3 +94,24 @@ def test_headline_model_stream_subset(gpu, orc):
         ost, _ = od.get_state()
         for layer in [0, 11, 23]:
             assert state_rel_err(st[s, layer, k * E:], ost[layer, k * E:]) <= 1e-4, (s, layer)
+
+
+def test_fused_argmax_epilogue_matches_materialised_logits(gpu, orc):
+    """Greedy steps through the logits projection's argmax epilogue (no
+    logits stored) pick the same tokens as argmax over stored logits, except
+    where the two best logits are within 1e-4."""
+    _, gm = same_model(orc, gpu, WIDE, seed=5)
+    S = 256
+    ids = _ids(S, 3, WIDE["vocab"], 31)
+    fused, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    for t in range(3):
+        tok = fused.step_greedy(ids[:, t])
+        lg = plain.step(ids[:, t])
+        ref = np.argmax(lg, axis=1)
+        top2 = np.sort(lg, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 1e-4
+        assert np.array_equal(tok[clear], ref[clear]), t
+        assert clear.mean() > 0.9
+    st_a, _ = fused.get_state()
+    st_b, _ = plain.get_state()
+    assert state_rel_err(st_a, st_b) <= 1e-6
