@@ -287,6 +287,43 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
     barrier()
 
+    # ---- one stream: the HBM-bound regime (every weight streams once per token)
+    batch1 = None
+    if rank == 0 and not args.no_batch1:
+        d1 = nb.Decoder(gm, 1)
+        s1 = torch.cuda.ExternalStream(d1.cuda_stream())
+        d1.prefill(ids[:1], want_logits=False)
+        t1 = torch.from_numpy(d1.sample(greedy, np.zeros((1, 4), np.uint64)).astype(np.int32)).cuda()
+        t2 = torch.empty_like(t1)
+        for _ in range(3):
+            d1.step_greedy_device(t1.data_ptr(), t2.data_ptr())
+            t1, t2 = t2, t1
+        torch.cuda.synchronize()
+        n1 = max(20, args.steps)
+        e0.record(s1)
+        for _ in range(n1):
+            d1.step_greedy_device(t1.data_ptr(), t2.data_ptr())
+            t1, t2 = t2, t1
+        e1.record(s1)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / n1
+        c = cfg
+        E, H = c.d_model * c.expand, c.d_model * c.mlp_mult
+        weight_bytes = 4.0 * (c.n_layer * (3 * E * c.d_model + c.d_model * E + 2 * H * c.d_model + c.d_model * H +
+                                           c.conv_k * E + 3 * E + E + 2 * c.d_model + 2 * H + 2 * c.d_model) +
+                              c.vocab * c.d_model + c.d_model)
+        state_bytes = 4.0 * c.n_layer * ((c.conv_k + 1) * E + 2 * E)  # ring + h read, slot + h written
+        gbs = (weight_bytes + state_bytes) / (us * 1e-6) / 1e9
+        peaks, basis = load_peaks()
+        batch1 = {"us_per_token": us, "tokens_per_s": 1e6 / us, "bytes_per_token": weight_bytes + state_bytes,
+                  "achieved_gbs": gbs, "peak_gbs": peaks["hbm_gbs"], "frac": gbs / peaks["hbm_gbs"],
+                  "peak_basis": f"{basis} hbm_gbs", "launches_per_token": None}
+        l0 = d1.launch_count()
+        d1.step_greedy_device(t1.data_ptr(), t2.data_ptr())
+        torch.cuda.synchronize()
+        batch1["launches_per_token"] = d1.launch_count() - l0
+        d1.close()
+
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_decode_rate(steps=8, warmup=1)
@@ -300,10 +337,12 @@ def run_ours(args, rank, world, local_rank):
         # 3xTF32 rate: TF32 issues at half the dense bf16 rate, and every f32
         # product takes three TF32 passes.
         peak = peaks["bf16_tflops_sustained"] / 2.0 / 3.0
-        traffic = None
+        traffic, traffic_launch = None, None
         try:
             with open(TRAFFIC_PATH) as f:
-                traffic = json.load(f).get("projection_dram_bytes_per_launch")
+                tj = json.load(f)
+            traffic = tj.get("projection_dram_bytes_per_launch")
+            traffic_launch = tj.get("launch")
         except (OSError, ValueError):
             pass
         total_tokens = n_streams
@@ -331,12 +370,13 @@ def run_ours(args, rank, world, local_rank):
                     "h2d_bytes_per_step": 4 * n_streams, "d2h_bytes_per_step": 4 * n_streams},
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "achieved": achieved_tflops, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved_tflops / peak, "traffic": traffic,
+                         "frac": achieved_tflops / peak, "traffic": traffic, "traffic_launch": traffic_launch,
                          "kernel": "projection GEMMs (in/out/up/down/logits)",
                          "peak_basis": f"{basis} bf16_tflops_sustained / 2 (TF32) / 3 (3xTF32 passes)",
                          "proj_ms_per_step": prof["proj_ms"] / args.steps,
                          "proj_launches_per_step": prof["proj_launches"] / args.steps},
             "clocks": clocks,
+            "batch1": batch1,
             "cpu_baseline": cpu_baseline,
             "setup": {"init_s": round(init_s, 2)},
         }
@@ -358,6 +398,7 @@ def main():
     ap.add_argument("--weak", action="store_true",
                     help="fixed streams per GPU (streams x N in total) instead of the fixed 16384")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch1", action="store_true", help="skip the one-stream HBM measurement")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling knob: fewer layers than the headline model (for small ncu captures)")
     ap.add_argument("--vocab", type=int, default=None,

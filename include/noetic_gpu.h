@@ -179,8 +179,10 @@ nk_status nk_decoder_step_greedy(nk_decoder *dec, const uint32_t *tokens_in,
 nk_status nk_decoder_cuda_stream(nk_decoder *dec, void **stream);
 nk_status nk_decoder_sync(nk_decoder *dec);
 
-/* Which projection engine the decoder uses: 0 = automatic (tensor-core
- * 3xTF32 GEMM where the shape allows it), 1 = f32 CUDA-core kernels only. */
+/* Engine flags: 0 = automatic (tensor-core 3xTF32 projections where the
+ * shape allows it; the fused small-batch step for <= 8 streams).  Bit 0: f32
+ * CUDA-core projections only.  Bit 1 / bit 2: force the time-chunked /
+ * sequential prefill scan.  Bit 3: no fused small-batch step. */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

@@ -387,20 +387,52 @@ __global__ void swiglu_k(const float *__restrict__ up, RowOut out, int M, int H)
 
 // Per row: the best (value, index) over the column tiles' partial maxima,
 // earliest tile first on ties (argmax, tensor.rs:354-365).
+// One CTA per row; (value, tile) pairs reduce with "larger value, then
+// earlier tile" so ties resolve to the earliest tile as in a serial scan.
 __global__ void argmax_partials_k(const float *__restrict__ val, const uint32_t *__restrict__ idx, int n_tiles,
                                   int M, uint32_t *__restrict__ out) {
-    const int m = blockIdx.x * blockDim.x + threadIdx.x;
-    if (m >= M) return;
+    const int m = blockIdx.x;
     float bv = -INFINITY;
-    uint32_t bi = 0;
-    for (int t = 0; t < n_tiles; ++t) {
+    int bt = n_tiles;
+    for (int t = threadIdx.x; t < n_tiles; t += blockDim.x) {
         const float v = val[(size_t)m * n_tiles + t];
-        if (v > bv) {
+        if (v > bv) {  // strided by thread: the first t with a larger value wins
             bv = v;
-            bi = idx[(size_t)m * n_tiles + t];
+            bt = t;
         }
     }
-    out[m] = bv == -INFINITY ? 0u : bi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int ot = __shfl_xor_sync(0xffffffffu, bt, o);
+        if (ov > bv || (ov == bv && ot < bt)) {
+            bv = ov;
+            bt = ot;
+        }
+    }
+    __shared__ float sv[32];
+    __shared__ int st[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        st[warp] = bt;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bt = lane < nw ? st[lane] : n_tiles;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int ot = __shfl_xor_sync(0xffffffffu, bt, o);
+            if (ov > bv || (ov == bv && ot < bt)) {
+                bv = ov;
+                bt = ot;
+            }
+        }
+        if (lane == 0) out[m] = (bv == -INFINITY || bt >= n_tiles) ? 0u : idx[(size_t)m * n_tiles + bt];
+    }
 }
 
 // Block per row: first index of the maximum over non-NaN entries; 0 when
@@ -608,7 +640,7 @@ cudaError_t swiglu_rows(const float *up, RowOut s, int M, int H, cudaStream_t st
 cudaError_t argmax_partials(const float *val, const uint32_t *idx, int n_tiles, int M, uint32_t *out,
                             cudaStream_t st) {
     if (M == 0) return cudaSuccess;
-    argmax_partials_k<<<blocks_for(M, 128), 128, 0, st>>>(val, idx, n_tiles, M, out);
+    argmax_partials_k<<<M, 256, 0, st>>>(val, idx, n_tiles, M, out);
     return cudaGetLastError();
 }
 

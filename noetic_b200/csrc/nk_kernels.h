@@ -100,6 +100,30 @@ cudaError_t gather_rows(const float *src, const uint32_t *idx, float *dst, int n
 cudaError_t scatter_rows(const float *src, const uint32_t *idx, float *dst, int n, int d,
                          cudaStream_t st);
 
+// ---- small-batch decode step (small_batch.cu): M <= GEMV_MAX_ROWS streams,
+// four fused kernels per layer with L2 weight prefetch ahead of the
+// programmatic-dependent-launch wait.
+struct SmallLayer {
+    const float *n1, *in_w, *in_b, *conv_w, *conv_b, *out_w, *out_b, *n2, *up_w, *up_b, *down_w, *down_b;
+};
+struct SmallStepArgs {
+    const uint32_t *tokens;  // device [M]
+    uint32_t *tokens_out;    // device [M] greedy choice, nullable
+    const float *emb, *norm_f;
+    float eps;
+    float *x, *g, *state;    // x [M,d], g [M,max(E,H)], state [L][M][k+1][E]
+    uint32_t *heads;
+    float *logits;           // [M,V] nullable
+    float *best_val;         // [M, small_logit_tiles(V)]
+    uint32_t *best_idx;
+    int *err;
+    int M, d, E, H, k, V, n_layer;
+    const SmallLayer *layers;  // host array [n_layer]
+};
+bool small_step_supported(int M, int d, int E, int H, int k);
+int small_logit_tiles(int V);
+cudaError_t small_step(const SmallStepArgs &a, cudaStream_t st, int *launches);
+
 // ---- sampler (sampler.cu): sample_token for every row.
 struct SampleParams {
     float temperature;

@@ -441,6 +441,16 @@ struct nk_decoder {
     uint32_t *best_idx = nullptr;
     // prefill operand pair
     float *p_ahi = nullptr, *p_alo = nullptr;
+    // small-batch engine: layer pointers and CUDA graphs of the greedy step,
+    // one per (tokens in, tokens out) device buffer pair
+    std::vector<nk::SmallLayer> small_layers;
+    struct StepGraph {
+        const uint32_t *in;
+        uint32_t *out;
+        cudaGraphExec_t exec;
+    };
+    std::vector<StepGraph> graphs;
+    bool small_warm = false;
     // projection profiling (CUDA events around each projection launch)
     bool profiling = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -465,6 +475,7 @@ struct nk_decoder {
         for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo})
             if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+        for (auto &gph : graphs) cudaGraphExecDestroy(gph.exec);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -599,10 +610,90 @@ void check_err_flag(nk_decoder *dec) {
     }
 }
 
+bool use_small(const nk_decoder *dec) {
+    const nk_model *m = dec->model;
+    return !(dec->engine & 8) &&
+           nk::small_step_supported((int)dec->S, (int)m->d(), (int)m->e(), (int)m->hidden(), (int)m->k());
+}
+
+nk::SmallStepArgs small_args(nk_decoder *dec, const uint32_t *tokens, uint32_t *tokens_out, bool want_logits) {
+    nk_model *m = dec->model;
+    if (dec->small_layers.size() != m->cfg.n_layer) {
+        dec->small_layers.clear();
+        for (const LayerIx &L : m->layers)
+            dec->small_layers.push_back({m->dp(L.n1), m->dp(L.in_w), m->dp(L.in_b), m->dp(L.conv_w), m->dp(L.conv_b),
+                                         m->dp(L.out_w), m->dp(L.out_b), m->dp(L.n2), m->dp(L.up_w), m->dp(L.up_b),
+                                         m->dp(L.down_w), m->dp(L.down_b)});
+    }
+    nk::SmallStepArgs a{};
+    a.tokens = tokens;
+    a.tokens_out = tokens_out;
+    a.emb = m->dp(m->emb);
+    a.norm_f = m->dp(m->norm_f);
+    a.eps = m->cfg.eps;
+    a.x = dec->x;
+    a.g = dec->g;
+    a.state = dec->state;
+    a.heads = dec->heads;
+    a.logits = want_logits ? dec->logits : nullptr;
+    a.best_val = dec->best_val;
+    a.best_idx = dec->best_idx;
+    a.err = dec->err;
+    a.M = (int)dec->S;
+    a.d = (int)m->d();
+    a.E = (int)m->e();
+    a.H = (int)m->hidden();
+    a.k = (int)m->k();
+    a.V = (int)m->cfg.vocab;
+    a.n_layer = (int)m->cfg.n_layer;
+    a.layers = dec->small_layers.data();
+    return a;
+}
+
+// The small-batch step; the greedy form replays a captured CUDA graph once
+// the eager form has run (kernel attributes set, buffers touched).
+void small_step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
+    const nk::SmallStepArgs a = small_args(dec, tokens, tokens_out, want_logits);
+    const bool graphable = tokens_out && !want_logits && !dec->profiling && dec->small_warm;
+    if (graphable) {
+        for (auto &gph : dec->graphs)
+            if (gph.in == tokens && gph.out == tokens_out) {
+                cuda_check(cudaGraphLaunch(gph.exec, dec->stream), "cudaGraphLaunch");
+                dec->launches += 2 + 4 * dec->model->cfg.n_layer;
+                return;
+            }
+        if (dec->graphs.size() < 4) {
+            cudaGraph_t graph = nullptr;
+            cuda_check(cudaStreamBeginCapture(dec->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
+            int n = 0;
+            cudaError_t e = nk::small_step(a, dec->stream, &n);
+            cudaError_t e2 = cudaStreamEndCapture(dec->stream, &graph);
+            cuda_check(e, "small-batch step capture");
+            cuda_check(e2, "cudaStreamEndCapture");
+            cudaGraphExec_t exec = nullptr;
+            e = cudaGraphInstantiate(&exec, graph, 0);
+            cudaGraphDestroy(graph);
+            cuda_check(e, "cudaGraphInstantiate");
+            dec->graphs.push_back({tokens, tokens_out, exec});
+            cuda_check(cudaGraphLaunch(exec, dec->stream), "cudaGraphLaunch");
+            dec->launches += (uint64_t)n;
+            return;
+        }
+    }
+    int n = 0;
+    cuda_check(nk::small_step(a, dec->stream, &n), "small-batch step");
+    dec->launches += (uint64_t)n;
+    dec->small_warm = true;
+}
+
 // Decoder::step over every stream (infer.rs:106-200), tokens on the device.
 // With tokens_out, the step ends in the greedy choice (sample_token with
 // greedy and no penalty); the logits are then stored only if want_logits.
 void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
+    if (use_small(dec)) {
+        small_step_device(dec, tokens, want_logits || !tokens_out, tokens_out);
+        return;
+    }
     nk_model *m = dec->model;
     const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(),
               k = (int)m->k(), V = (int)m->cfg.vocab;
@@ -988,8 +1079,9 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         const size_t act_w = std::max({d, E, H});
         dalloc(&dec->ahi, S * act_w, "operand hi");
         dalloc(&dec->alo, S * act_w, "operand lo");
-        dalloc(&dec->best_val, S * (size_t)nk::tc_tiles_n((int)V), "argmax partials");
-        dalloc(&dec->best_idx, S * (size_t)nk::tc_tiles_n((int)V), "argmax partials");
+        const size_t tiles = std::max<size_t>(nk::tc_tiles_n((int)V), nk::small_logit_tiles((int)V));
+        dalloc(&dec->best_val, S * tiles, "argmax partials");
+        dalloc(&dec->best_idx, S * tiles, "argmax partials");
         dalloc(&dec->tok_a, S, "tokens");
         dalloc(&dec->tok_b, S, "tokens");
         dalloc(&dec->err, 1, "error flag");
@@ -1240,8 +1332,11 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 7) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 15) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
+        cudaSetDevice(dec->model->device);
+        for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);
+        dec->graphs.clear();
     });
 }
 
