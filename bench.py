@@ -214,6 +214,8 @@ def run_ours(args, rank, world, local_rank):
     init_s = time.perf_counter() - t0
     ids = uniform_prompts(count, PROMPT_LEN, cfg.vocab, PROMPT_SEED_BASE, first=first)
     dec = nb.Decoder(gm, count)
+    if args.engine:
+        dec.set_engine(args.engine)
     stream = torch.cuda.ExternalStream(dec.cuda_stream())
     greedy = nb.SampleCfg(temperature=1.0, top_k=0, top_p=1.0, rep_penalty=1.0, rep_window=0, greedy=True)
 
@@ -399,6 +401,7 @@ def main():
                     help="fixed streams per GPU (streams x N in total) instead of the fixed 16384")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true", help="skip the one-stream HBM measurement")
+    ap.add_argument("--engine", type=int, default=0, help="decoder engine flags (0 = automatic)")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling knob: fewer layers than the headline model (for small ncu captures)")
     ap.add_argument("--vocab", type=int, default=None,

@@ -182,7 +182,9 @@ nk_status nk_decoder_sync(nk_decoder *dec);
 /* Engine flags: 0 = automatic (tensor-core 3xTF32 projections where the
  * shape allows it; the fused small-batch step for <= 8 streams).  Bit 0: f32
  * CUDA-core projections only.  Bit 1 / bit 2: force the time-chunked /
- * sequential prefill scan.  Bit 3: no fused small-batch step. */
+ * sequential prefill scan.  Bit 3: no fused small-batch step.  Bits 4 / 5:
+ * tensor-core tiles 128 / 256 columns wide (default: 256 while the grid
+ * covers every SM twice, else 128). */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

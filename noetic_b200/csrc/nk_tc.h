@@ -16,8 +16,10 @@ namespace nk {
 struct TcOperand {
     const float *hi = nullptr, *lo = nullptr;
     int N = 0, K = 0, N_pad = 0, K_pad = 0;
-    alignas(64) unsigned char map_hi[128];
+    alignas(64) unsigned char map_hi[128];     // 256-row boxes
     alignas(64) unsigned char map_lo[128];
+    alignas(64) unsigned char map_hi128[128];  // 128-row boxes
+    alignas(64) unsigned char map_lo128[128];
 };
 
 struct TcWeights {
@@ -33,8 +35,8 @@ struct TcSource {
 };
 
 // Epilogue of one projection: either store C = acc (+ bias) (R + ...), or
-// (best_val != nullptr) write each row's first maximum over every 256-column
-// tile into best_val / best_idx [M, tc_tiles_n(N)] without storing C.
+// (best_val != nullptr) write each row's first maximum over every column
+// tile into best_val / best_idx [M, tc_tiles_n(N, bn)] without storing C.
 struct TcEpilogue {
     float *C = nullptr;
     int ldc = 0;
@@ -48,8 +50,10 @@ struct TcEpilogue {
 // Whether the tcgen05 engine takes a projection of this shape.
 bool tc_eligible(int M, int N, int K);
 
-// Number of 256-column tiles of an N-wide projection.
-int tc_tiles_n(int N);
+// Tile width for an M x N projection (256 while the grid covers every SM
+// twice, else 128) and the number of column tiles at that width.
+int tc_pick_bn(int M, int N);
+int tc_tiles_n(int N, int bn);
 
 cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs);
 void tc_weights_free(TcWeights &w);
@@ -60,6 +64,6 @@ cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, in
 // epilogue(A . W^T) with A given as its hi/lo operand pair [M, K] (dense).
 // A kernel whose bounded waits expire writes a nonzero code to *err.
 cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
-                    cudaStream_t st, int *err);
+                    int bn, cudaStream_t st, int *err);
 
 }  // namespace nk

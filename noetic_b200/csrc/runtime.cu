@@ -534,6 +534,13 @@ struct ProfScope {
     }
 };
 
+// Tile width of a tensor-core projection; engine bits 4 / 5 force 128 / 256.
+int pick_bn(const nk_decoder *dec, int M, int N) {
+    if (dec->engine & 16) return 128;
+    if ((dec->engine & 32) && N >= 256) return 256;
+    return nk::tc_pick_bn(M, N);
+}
+
 // C = A.W^T (+bias) (R + ...), A read from `a` in the form `tc` selects.
 void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W, const nk::TcOperand *Wtc,
              int N, const float *bias, float *C, const float *R) {
@@ -545,7 +552,8 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         ep.bias = bias;
         ep.R = R;
         ep.ldr = N;
-        cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, dec->stream, dec->err), "tcgen05 projection");
+        cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, N), dec->stream, dec->err),
+                   "tcgen05 projection");
         dec->launches += 1;
         dec->prof_tc = dec->prof_tc || dec->profiling;
     } else {
@@ -559,16 +567,17 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
 void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W,
                     const nk::TcOperand *Wtc, int N, uint32_t *tokens) {
     if (tc) {
+        const int bn = pick_bn(dec, M, N);
         {
             ProfScope prof(dec, M, N, K, false, false);
             nk::TcEpilogue ep;
             ep.best_val = dec->best_val;
             ep.best_idx = dec->best_idx;
-            cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, dec->stream, dec->err), "tcgen05 projection");
+            cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, bn, dec->stream, dec->err), "tcgen05 projection");
             dec->launches += 1;
             dec->prof_tc = dec->prof_tc || dec->profiling;
         }
-        launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, nk::tc_tiles_n(N), M, tokens, dec->stream),
+        launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, nk::tc_tiles_n(N, bn), M, tokens, dec->stream),
                   "argmax partials");
     } else {
         project(dec, false, a, M, K, W, Wtc, N, nullptr, dec->logits, nullptr);
@@ -1079,7 +1088,7 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         const size_t act_w = std::max({d, E, H});
         dalloc(&dec->ahi, S * act_w, "operand hi");
         dalloc(&dec->alo, S * act_w, "operand lo");
-        const size_t tiles = std::max<size_t>(nk::tc_tiles_n((int)V), nk::small_logit_tiles((int)V));
+        const size_t tiles = std::max<size_t>(nk::tc_tiles_n((int)V, 128), nk::small_logit_tiles((int)V));
         dalloc(&dec->best_val, S * tiles, "argmax partials");
         dalloc(&dec->best_idx, S * tiles, "argmax partials");
         dalloc(&dec->tok_a, S, "tokens");
@@ -1332,7 +1341,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 15) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 63) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

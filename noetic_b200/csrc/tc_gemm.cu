@@ -39,25 +39,31 @@ namespace nk {
 
 namespace {
 
-// BK = 16 f32 = one 64-byte swizzle row; four stages keep three K-blocks of
-// loads in flight ahead of the MMAs.
-constexpr int BM = 128, BN = 256, BK = 16;
-constexpr int STAGES = 4;
+// BK = 16 f32 = one 64-byte swizzle row.  Tile width BN is 256 (one CTA per
+// SM, 4 stages of 48 KiB, 512 TMEM columns) or 128 (two CTAs per SM, 3
+// stages of 32 KiB, 256 TMEM columns each, so one CTA's epilogue overlaps the
+// other's main loop and small grids still cover every SM).
+constexpr int BM = 128, BK = 16;
 constexpr int SWIZZLE_BYTES = BK * 4;                       // 64
 constexpr int ATOM_BYTES = 8 * SWIZZLE_BYTES;               // 8 rows: 512
 constexpr int A_BYTES = BM * BK * 4;                       // 8 KiB
-constexpr int B_BYTES = BN * BK * 4;                       // 16 KiB
-constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;     // 48 KiB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 constexpr int THREADS = 256;
-// Two f32 accumulators of BN columns: the hi*hi products and the two small
-// correction products are summed in separate TMEM chains.
-constexpr uint32_t TMEM_COLS = 2 * BN;
 constexpr uint64_t WAIT_NS = 1000000000ull;  // bound of every mbarrier wait
 
-// Instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=256.
-constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+template <int BN>
+struct Tile {
+    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int STAGES = BN == 256 ? 4 : 3;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    static constexpr int CTAS_PER_SM = BN == 256 ? 1 : 2;
+    // Two f32 accumulators of BN columns: the hi*hi products and the two
+    // small correction products are summed in separate TMEM chains.
+    static constexpr uint32_t TMEM_COLS = 2 * BN;
+    // Instruction descriptor: D f32, A/B tf32, both K-major, M=128, N=BN.
+    static constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                      ((uint32_t)(BM >> 4) << 24);
+};
 
 struct TcArgs {
     float *C;
@@ -121,10 +127,11 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
            (4ull << 61);
 }
 
-__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
     asm volatile(
         "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p; }"
-        ::"r"(d_tmem), "l"(a), "l"(b), "r"(IDESC), "r"(accumulate));
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -148,9 +155,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+template <int BN>
+__global__ void __launch_bounds__(THREADS, Tile<BN>::CTAS_PER_SM)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
+    using T = Tile<BN>;
+    constexpr int STAGES = T::STAGES, STAGE_BYTES = T::STAGE_BYTES, B_BYTES = T::B_BYTES;
+    constexpr uint32_t TMEM_COLS = T::TMEM_COLS, IDESC = T::IDESC;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned tile area (swizzle atoms must not straddle their period).
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -249,9 +260,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             for (int kk = 0; kk < BK / 8; ++kk) {
                 const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
                 const uint32_t acc = (kb | kk) ? 1u : 0u;
-                mma_tf32(tmem, dAh + off, dBh + off, acc);
-                mma_tf32(tmem + BN, dAh + off, dBl + off, acc);
-                mma_tf32(tmem + BN, dAl + off, dBh + off, 1u);
+                mma_tf32(tmem, dAh + off, dBh + off, IDESC, acc);
+                mma_tf32(tmem + BN, dAh + off, dBl + off, IDESC, acc);
+                mma_tf32(tmem + BN, dAl + off, dBh + off, IDESC, 1u);
             }
             mma_commit(bar_empty0 + 8 * stage);
             if (++stage == STAGES) {
@@ -397,10 +408,23 @@ cudaError_t split(const float *src, int ld, float *hi, float *lo, int rows, int 
 }  // namespace
 
 bool tc_eligible(int M, int N, int K) {
-    return M >= BM && N >= BN && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
+    return M >= BM && N >= 128 && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
 }
 
-int tc_tiles_n(int N) { return (N + BN - 1) / BN; }
+// BN = 256 while the grid still fills every SM twice over, else 128.
+int tc_pick_bn(int M, int N) {
+    static int num_sms = 0;
+    if (!num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (num_sms <= 0) num_sms = 148;
+    }
+    const long tiles256 = (long)((N + 255) / 256) * ((M + BM - 1) / BM);
+    return (N >= 256 && tiles256 >= 2L * num_sms) ? 256 : 128;
+}
+
+int tc_tiles_n(int N, int bn) { return (N + bn - 1) / bn; }
 
 cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
     return split(A, lda, hi, lo, rows, cols, st);
@@ -429,8 +453,10 @@ cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs) {
         op.N_pad = s.N;
         op.K_pad = s.K;
         if (s.K % 4 == 0) {
-            if (!make_map((CUtensorMap *)op.map_hi, hi, s.N, s.K, BN) ||
-                !make_map((CUtensorMap *)op.map_lo, lo, s.N, s.K, BN))
+            if (!make_map((CUtensorMap *)op.map_hi, hi, s.N, s.K, 256) ||
+                !make_map((CUtensorMap *)op.map_lo, lo, s.N, s.K, 256) ||
+                !make_map((CUtensorMap *)op.map_hi128, hi, s.N, s.K, 128) ||
+                !make_map((CUtensorMap *)op.map_lo128, lo, s.N, s.K, 128))
                 return cudaErrorInvalidValue;
         }
     }
@@ -447,25 +473,33 @@ void tc_weights_free(TcWeights &w) {
     w.ready = false;
 }
 
-cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
-                    cudaStream_t st, int *err) {
-    if (W.K != K || M <= 0) return cudaErrorInvalidValue;
-    alignas(64) CUtensorMap mAh, mAl;
-    if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
+template <int BN>
+cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, const TcArgs &a, int M,
+                      cudaStream_t st) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Tile<BN>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr_dev = dev;
     }
-    TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_tiles_n(W.N), err};
-    dim3 grid((unsigned)tc_tiles_n(W.N), (unsigned)((M + BM - 1) / BM));
-    tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(*(const CUtensorMap *)&mAh, *(const CUtensorMap *)&mAl,
-                                                     *(const CUtensorMap *)W.map_hi,
-                                                     *(const CUtensorMap *)W.map_lo, a);
+    const unsigned char *mh = BN == 256 ? W.map_hi : W.map_hi128;
+    const unsigned char *ml = BN == 256 ? W.map_lo : W.map_lo128;
+    dim3 grid((unsigned)tc_tiles_n(W.N, BN), (unsigned)((M + BM - 1) / BM));
+    tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(mAh, mAl, *(const CUtensorMap *)mh,
+                                                                    *(const CUtensorMap *)ml, a);
     return cudaGetLastError();
+}
+
+cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
+                    int bn, cudaStream_t st, int *err) {
+    if (W.K != K || M <= 0 || (bn != 128 && bn != 256)) return cudaErrorInvalidValue;
+    alignas(64) CUtensorMap mAh, mAl;
+    if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
+    TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_tiles_n(W.N, bn), err};
+    return bn == 256 ? launch_tc<256>(mAh, mAl, W, a, M, st) : launch_tc<128>(mAh, mAl, W, a, M, st);
 }
 
 }  // namespace nk

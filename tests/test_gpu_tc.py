@@ -21,11 +21,13 @@ def _ids(S, T, V, base):
     return uniform_prompts(S, T, V, base)
 
 
-def test_tensor_core_engine_matches_f32_engine(gpu, orc):
+@pytest.mark.parametrize("tile_bits", [16, 32])  # tensor-core tiles 128 / 256 columns wide
+def test_tensor_core_engine_matches_f32_engine(gpu, orc, tile_bits):
     om, gm = same_model(orc, gpu, WIDE, seed=1)
     S, T = 384, 4
     ids = _ids(S, T, WIDE["vocab"], 10)
     tc, f32 = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    tc.set_engine(tile_bits)
     f32.set_engine(1)
     tc.profile_begin()
     for t in range(T):
