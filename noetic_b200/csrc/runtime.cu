@@ -448,9 +448,10 @@ struct nk_decoder {
         const uint32_t *in;
         uint32_t *out;
         cudaGraphExec_t exec;
+        uint64_t launches;
     };
     std::vector<StepGraph> graphs;
-    bool small_warm = false;
+    bool warm = false;  // an eager greedy step has run (buffers sized, attributes set)
     // projection profiling (CUDA events around each projection launch)
     bool profiling = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -659,46 +660,58 @@ nk::SmallStepArgs small_args(nk_decoder *dec, const uint32_t *tokens, uint32_t *
     return a;
 }
 
-// The small-batch step; the greedy form replays a captured CUDA graph once
-// the eager form has run (kernel attributes set, buffers touched).
 void small_step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
     const nk::SmallStepArgs a = small_args(dec, tokens, tokens_out, want_logits);
-    const bool graphable = tokens_out && !want_logits && !dec->profiling && dec->small_warm;
+    int n = 0;
+    cuda_check(nk::small_step(a, dec->stream, &n), "small-batch step");
+    dec->launches += (uint64_t)n;
+}
+
+void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out);
+
+// Greedy steps replay a CUDA graph captured from the eager step (one per
+// pair of token buffers, at most four) once an eager step has sized every
+// buffer: the host cost of ~200 launches, tensor-map encodes included, is
+// paid once.  Profiling and logit-producing steps run eagerly.
+void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
+    const bool graphable = tokens_out && !want_logits && !dec->profiling && dec->warm;
     if (graphable) {
         for (auto &gph : dec->graphs)
             if (gph.in == tokens && gph.out == tokens_out) {
                 cuda_check(cudaGraphLaunch(gph.exec, dec->stream), "cudaGraphLaunch");
-                dec->launches += 2 + 4 * dec->model->cfg.n_layer;
+                dec->launches += gph.launches;
                 return;
             }
         if (dec->graphs.size() < 4) {
             cudaGraph_t graph = nullptr;
+            const uint64_t before = dec->launches;
             cuda_check(cudaStreamBeginCapture(dec->stream, cudaStreamCaptureModeThreadLocal), "cudaStreamBeginCapture");
-            int n = 0;
-            cudaError_t e = nk::small_step(a, dec->stream, &n);
-            cudaError_t e2 = cudaStreamEndCapture(dec->stream, &graph);
-            cuda_check(e, "small-batch step capture");
-            cuda_check(e2, "cudaStreamEndCapture");
+            try {
+                eager_step(dec, tokens, false, tokens_out);
+            } catch (...) {
+                cudaStreamEndCapture(dec->stream, &graph);
+                if (graph) cudaGraphDestroy(graph);
+                cudaGetLastError();
+                throw;
+            }
+            cuda_check(cudaStreamEndCapture(dec->stream, &graph), "cudaStreamEndCapture");
             cudaGraphExec_t exec = nullptr;
-            e = cudaGraphInstantiate(&exec, graph, 0);
+            cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
             cudaGraphDestroy(graph);
             cuda_check(e, "cudaGraphInstantiate");
-            dec->graphs.push_back({tokens, tokens_out, exec});
+            dec->graphs.push_back({tokens, tokens_out, exec, dec->launches - before});
             cuda_check(cudaGraphLaunch(exec, dec->stream), "cudaGraphLaunch");
-            dec->launches += (uint64_t)n;
             return;
         }
     }
-    int n = 0;
-    cuda_check(nk::small_step(a, dec->stream, &n), "small-batch step");
-    dec->launches += (uint64_t)n;
-    dec->small_warm = true;
+    eager_step(dec, tokens, want_logits, tokens_out);
+    if (tokens_out && !want_logits) dec->warm = true;
 }
 
 // Decoder::step over every stream (infer.rs:106-200), tokens on the device.
 // With tokens_out, the step ends in the greedy choice (sample_token with
 // greedy and no penalty); the logits are then stored only if want_logits.
-void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
+void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
     if (use_small(dec)) {
         small_step_device(dec, tokens, want_logits || !tokens_out, tokens_out);
         return;
