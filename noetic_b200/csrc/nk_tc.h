@@ -36,7 +36,7 @@ struct TcSource {
 
 // Epilogue of one projection: either store C = acc (+ bias) (R + ...), or
 // (best_val != nullptr) write each row's first maximum over every column
-// tile into best_val / best_idx [M, tc_tiles_n(N, bn)] without storing C.
+// half tile into best_val / best_idx [M, tc_argmax_parts(N, bn)] without storing C.
 struct TcEpilogue {
     float *C = nullptr;
     int ldc = 0;
@@ -54,6 +54,8 @@ bool tc_eligible(int M, int N, int K);
 // twice, else 128) and the number of column tiles at that width.
 int tc_pick_bn(int M, int N);
 int tc_tiles_n(int N, int bn);
+// Argmax partials per row: one per half tile (each epilogue warpgroup owns half the columns).
+int tc_argmax_parts(int N, int bn);
 
 cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs);
 void tc_weights_free(TcWeights &w);

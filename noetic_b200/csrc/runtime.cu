@@ -578,7 +578,7 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
             dec->launches += 1;
             dec->prof_tc = dec->prof_tc || dec->profiling;
         }
-        launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, nk::tc_tiles_n(N, bn), M, tokens, dec->stream),
+        launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, nk::tc_argmax_parts(N, bn), M, tokens, dec->stream),
                   "argmax partials");
     } else {
         project(dec, false, a, M, K, W, Wtc, N, nullptr, dec->logits, nullptr);
@@ -616,7 +616,7 @@ void check_err_flag(nk_decoder *dec) {
         cuda_check(cudaMemsetAsync(dec->err, 0, sizeof(int), dec->stream), "clear error flag");
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
-                                ": 1 invalid token, 2 bounded draw, 101-103 tensor-core pipeline wait expired)");
+                                ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired)");
     }
 }
 
@@ -1101,7 +1101,7 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         const size_t act_w = std::max({d, E, H});
         dalloc(&dec->ahi, S * act_w, "operand hi");
         dalloc(&dec->alo, S * act_w, "operand lo");
-        const size_t tiles = std::max<size_t>(nk::tc_tiles_n((int)V, 128), nk::small_logit_tiles((int)V));
+        const size_t tiles = std::max<size_t>(nk::tc_argmax_parts((int)V, 128), nk::small_logit_tiles((int)V));
         dalloc(&dec->best_val, S * tiles, "argmax partials");
         dalloc(&dec->best_idx, S * tiles, "argmax partials");
         dalloc(&dec->tok_a, S, "tokens");

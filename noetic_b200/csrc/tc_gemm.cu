@@ -7,20 +7,27 @@
 // A_lo.W_lo^T term (~2^-22 relative).  Weights are split once at load; the
 // activation operand is split by a small pre-pass per projection.
 //
-// Kernel structure (one 128 x 256 output tile per CTA, 256 threads):
+// Kernel structure: persistent, at most one CTA per SM slot (BN = 256: one
+// per SM; BN = 128: two), each walking 128 x BN output tiles in steps of the
+// grid size, n fastest; 384 threads:
 //   warp 0      TMA producer: K-blocks of 16 f32 (one 64-byte swizzle row)
-//               for A_hi, A_lo, W_hi, W_lo into a 4-stage smem ring
-//               (cp.async.bulk.tensor, 64B swizzle, zero fill out of bounds);
-//   warp 1      TMEM allocator and MMA issuer: per K-block, 4 k-steps x 3
-//               tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=256, K=8):
+//               for A_hi, A_lo, W_hi, W_lo into a 4-stage (BN 256) or
+//               3-stage (BN 128) smem ring (cp.async.bulk.tensor, 64B
+//               swizzle, zero fill out of bounds).  It runs on into the next
+//               tile's K-blocks while the epilogue drains the current one;
+//   warp 1      TMEM allocator and MMA issuer: per K-block, 2 k-steps x 3
+//               tcgen05.mma.cta_group::1.kind::tf32 (M=128, N=BN, K=8):
 //               hi*hi into one f32 TMEM accumulator, hi*lo and lo*hi into a
-//               second one; tcgen05.commit frees the stage.  The tensor core
+//               second one; tcgen05.commit frees the stage, and after the
+//               last K-block signals the epilogue.  The tensor core
 //               truncates when it adds into an accumulator, so the error of a
 //               chain grows with its length; keeping the small correction
 //               products out of the main chain makes it three times shorter,
 //               and the epilogue adds the two chains in round-to-nearest f32;
-//   warps 4-7   epilogue: tcgen05.ld 32 columns at a time (lane = row), bias,
-//               residual add, store.
+//   warps 4-11  epilogue, two warpgroups each draining half of the tile's
+//               columns: tcgen05.ld 32 columns at a time (lane = row), bias,
+//               residual add, store (or the first maximum of its columns);
+//               then they hand the accumulators back to the MMA warp.
 // Every mbarrier wait is bounded (~1 s of %globaltimer); on expiry the kernel
 // records an error code, every role leaves its loop, TMEM is freed and the
 // CTA exits -- the host reports the code instead of the GPU hanging.
@@ -29,6 +36,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 
@@ -47,7 +55,10 @@ constexpr int BM = 128, BK = 16;
 constexpr int SWIZZLE_BYTES = BK * 4;                       // 64
 constexpr int ATOM_BYTES = 8 * SWIZZLE_BYTES;               // 8 rows: 512
 constexpr int A_BYTES = BM * BK * 4;                       // 8 KiB
-constexpr int THREADS = 256;
+// Warp roles: 0 TMA producer, 1 TMEM allocator + MMA issuer, 2-3 idle,
+// 4..11 epilogue (two warpgroups, each draining half the tile's columns).
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = (4 + EPI_WARPS) * 32;
 constexpr uint64_t WAIT_NS = 1000000000ull;  // bound of every mbarrier wait
 
 template <int BN>
@@ -165,17 +176,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned tile area (swizzle atoms must not straddle their period).
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES);  // full[S], empty[S], accum
-    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 1);
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES);  // full[S], empty[S], acc_full, acc_empty
+    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 2);
     __shared__ int s_abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int n_tiles_n = (p.N + BN - 1) / BN;
+    const int n_tiles = n_tiles_n * ((p.M + BM - 1) / BM);
     const int kblocks = (p.K + BK - 1) / BK;
 
     const uint32_t bar_full0 = smem_u32(&bars[0]);
     const uint32_t bar_empty0 = smem_u32(&bars[STAGES]);
-    const uint32_t bar_accum = smem_u32(&bars[2 * STAGES]);
+    const uint32_t bar_acc_full = smem_u32(&bars[2 * STAGES]);
+    const uint32_t bar_acc_empty = smem_u32(&bars[2 * STAGES + 1]);
 
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -183,7 +196,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             mbar_init(bar_full0 + 8 * s, 1);
             mbar_init(bar_empty0 + 8 * s, 1);
         }
-        mbar_init(bar_accum, 1);
+        mbar_init(bar_acc_full, 1);
+        mbar_init(bar_acc_empty, EPI_WARPS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAh) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAl) : "memory");
@@ -202,33 +216,37 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        // ---- TMA producer
+        // ---- TMA producer: runs ahead into the next tile's K-blocks while
+        // the epilogue drains the current one.
         int stage = 0;
         uint32_t phase = 0;
         int issued = 0;
-        for (int kb = 0; kb < kblocks; ++kb) {
-            if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
-                atomicExch(p.err, 101);
-                s_abort = 1;
-                break;
-            }
-            if (*(volatile int *)&s_abort) break;
-            uint8_t *st = smem + stage * STAGE_BYTES;
-            const uint32_t full = bar_full0 + 8 * stage;
-            mbar_expect_tx(full, STAGE_BYTES);
-            const int kx = kb * BK;
-            tma_load_2d(smem_u32(st), &mapAh, full, kx, m0);
-            tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, m0);
-            tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
-            tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
-            ++issued;
-            if (++stage == STAGES) {
-                stage = 0;
-                phase ^= 1;
+        for (int t = blockIdx.x; t < n_tiles && !*(volatile int *)&s_abort; t += gridDim.x) {
+            const int m0 = (t / n_tiles_n) * BM, n0 = (t % n_tiles_n) * BN;
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
+                    atomicExch(p.err, 101);
+                    s_abort = 1;
+                    break;
+                }
+                if (*(volatile int *)&s_abort) break;
+                uint8_t *st = smem + stage * STAGE_BYTES;
+                const uint32_t full = bar_full0 + 8 * stage;
+                mbar_expect_tx(full, STAGE_BYTES);
+                const int kx = kb * BK;
+                tma_load_2d(smem_u32(st), &mapAh, full, kx, m0);
+                tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, m0);
+                tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
+                tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
+                ++issued;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
             }
         }
-        // Drain: wait (bounded) until every issued stage has landed, so no
-        // copy is still writing this CTA's shared memory when it exits.
+        // Drain: wait (bounded) until the last issued stages have landed, so
+        // no copy is still writing this CTA's shared memory when it exits.
         {
             int s2 = 0;
             uint32_t ph2 = 0;
@@ -244,51 +262,68 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         // ---- MMA issuer
         int stage = 0;
         uint32_t phase = 0;
-        bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
-            if (!mbar_wait(bar_full0 + 8 * stage, phase) || *(volatile int *)&s_abort) {
-                atomicExch(p.err, 102);
+        int i = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+            // The accumulators are free once the epilogue drained tile i - 1.
+            if (!mbar_wait(bar_acc_empty, (uint32_t)((i & 1) ^ 1)) || *(volatile int *)&s_abort) {
+                atomicExch(p.err, 104);
                 s_abort = 1;
-                ok = false;
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t base = smem_u32(smem + stage * STAGE_BYTES);
-            const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + A_BYTES);
-            const uint64_t dBh = smem_desc(base + 2 * A_BYTES), dBl = smem_desc(base + 2 * A_BYTES + B_BYTES);
+            bool ok = true;
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(bar_full0 + 8 * stage, phase) || *(volatile int *)&s_abort) {
+                    atomicExch(p.err, 102);
+                    s_abort = 1;
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t base = smem_u32(smem + stage * STAGE_BYTES);
+                const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + A_BYTES);
+                const uint64_t dBh = smem_desc(base + 2 * A_BYTES), dBl = smem_desc(base + 2 * A_BYTES + B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < BK / 8; ++kk) {
-                const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
-                const uint32_t acc = (kb | kk) ? 1u : 0u;
-                mma_tf32(tmem, dAh + off, dBh + off, IDESC, acc);
-                mma_tf32(tmem + BN, dAh + off, dBl + off, IDESC, acc);
-                mma_tf32(tmem + BN, dAl + off, dBh + off, IDESC, 1u);
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
+                    const uint32_t acc = (kb | kk) ? 1u : 0u;
+                    mma_tf32(tmem, dAh + off, dBh + off, IDESC, acc);
+                    mma_tf32(tmem + BN, dAh + off, dBl + off, IDESC, acc);
+                    mma_tf32(tmem + BN, dAl + off, dBh + off, IDESC, 1u);
+                }
+                mma_commit(bar_empty0 + 8 * stage);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
             }
-            mma_commit(bar_empty0 + 8 * stage);
-            if (++stage == STAGES) {
-                stage = 0;
-                phase ^= 1;
-            }
+            // Arrives once every MMA issued above has completed (also on the
+            // abort path, so TMEM is never freed under a running MMA).
+            mma_commit(bar_acc_full);
+            if (!ok) break;
         }
-        // Arrives once every MMA issued above has completed (also on the
-        // abort path, so TMEM is never freed under a running MMA).
-        (void)ok;
-        mma_commit(bar_accum);
     } else if (warp >= 4) {
-        // ---- epilogue: warp w reads TMEM lanes 32*(w%4) .. +31
+        // ---- epilogue: warps 4..3+EPI_WARPS; warp w reads TMEM lanes
+        // 32*(w%4) .. +31 and half of the columns (warpgroup (w-4)/4).
         const int q = warp & 3;
-        const bool ok = mbar_wait(bar_accum, 0) && !*(volatile int *)&s_abort;
-        __syncwarp();
-        if (!ok) {
-            if (lane == 0) atomicExch(p.err, 103);
-        } else {
+        const int half = (warp - 4) >> 2;
+        constexpr int COLS = BN / 2;
+        const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
+        const bool argmax_mode = p.best_val != nullptr;
+        int i = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+            const int m0 = (t / n_tiles_n) * BM, n0 = (t % n_tiles_n) * BN;
+            const bool ok = mbar_wait(bar_acc_full, (uint32_t)(i & 1)) && !*(volatile int *)&s_abort;
+            __syncwarp();
+            if (!ok) {
+                if (lane == 0) atomicExch(p.err, 103);
+                break;
+            }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const int row = m0 + q * 32 + lane;
-            const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
-            const bool argmax_mode = p.best_val != nullptr;
             float best = -INFINITY;
             uint32_t best_n = 0xFFFFFFFFu;
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 32) {
                 if (n0 + c0 >= p.N) break;  // warp-uniform
                 float v[32], corr[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
@@ -341,9 +376,18 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                     }
                 }
             }
+            // TMEM of this tile fully read: hand the accumulators back.
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_acc_empty) : "memory");
             if (argmax_mode && row < p.M) {
-                p.best_val[(size_t)row * p.n_tiles + blockIdx.x] = best;
-                p.best_idx[(size_t)row * p.n_tiles + blockIdx.x] = best_n;
+                // Each warpgroup holds the first maximum of its half of the
+                // tile's columns: partial 2*tile_n + half, so partial order is
+                // column order and the reduction's earliest-partial tie rule
+                // keeps the first maximum.
+                const size_t slot = (size_t)row * p.n_tiles + 2 * (t % n_tiles_n) + half;
+                p.best_val[slot] = best;
+                p.best_idx[slot] = best_n;
             }
         }
     }
@@ -425,6 +469,7 @@ int tc_pick_bn(int M, int N) {
 }
 
 int tc_tiles_n(int N, int bn) { return (N + bn - 1) / bn; }
+int tc_argmax_parts(int N, int bn) { return 2 * tc_tiles_n(N, bn); }
 
 cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
     return split(A, lda, hi, lo, rows, cols, st);
@@ -487,7 +532,15 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
     }
     const unsigned char *mh = BN == 256 ? W.map_hi : W.map_hi128;
     const unsigned char *ml = BN == 256 ? W.map_lo : W.map_lo128;
-    dim3 grid((unsigned)tc_tiles_n(W.N, BN), (unsigned)((M + BM - 1) / BM));
+    // Persistent: at most one CTA per SM slot, each walking tiles in steps
+    // of the grid size (n fastest, so neighbouring CTAs share the A rows).
+    static int num_sms = 0;
+    if (!num_sms) {
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (num_sms <= 0) num_sms = 148;
+    }
+    const long tiles = (long)tc_tiles_n(W.N, BN) * ((M + BM - 1) / BM);
+    const unsigned grid = (unsigned)std::min<long>(tiles, (long)num_sms * Tile<BN>::CTAS_PER_SM);
     tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(mAh, mAl, *(const CUtensorMap *)mh,
                                                                     *(const CUtensorMap *)ml, a);
     return cudaGetLastError();
@@ -498,7 +551,7 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     if (W.K != K || M <= 0 || (bn != 128 && bn != 256)) return cudaErrorInvalidValue;
     alignas(64) CUtensorMap mAh, mAl;
     if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
-    TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_tiles_n(W.N, bn), err};
+    TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err};
     return bn == 256 ? launch_tc<256>(mAh, mAl, W, a, M, st) : launch_tc<128>(mAh, mAl, W, a, M, st);
 }
 
