@@ -184,7 +184,9 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * CUDA-core projections only.  Bit 1 / bit 2: force the time-chunked /
  * sequential prefill scan.  Bit 3: no fused small-batch step.  Bits 4 / 5:
  * tensor-core tiles 128 / 256 columns wide (default: 256 while the grid
- * covers every SM twice, else 128). */
+ * covers every SM twice, else 128).  Bit 6: for 1-4 streams, the whole step
+ * as one persistent cooperative kernel instead of the fused small-batch
+ * kernels. */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

@@ -124,6 +124,14 @@ bool small_step_supported(int M, int d, int E, int H, int k);
 int small_logit_tiles(int V);
 cudaError_t small_step(const SmallStepArgs &a, cudaStream_t st, int *launches);
 
+// ---- the whole decode step for 1..4 streams as one persistent cooperative
+// kernel (decode_persistent.cu).  layers_dev: device copy of a.layers;
+// sync: two device words, zeroed by the launch; a.best_val / best_idx hold
+// persistent_partials() entries per stream.
+bool persistent_step_supported(int M, int d, int E, int H, int k, int V, int n_layer);
+int persistent_partials();
+cudaError_t persistent_step(const SmallStepArgs &a, const SmallLayer *layers_dev, uint32_t *sync, cudaStream_t st);
+
 // ---- sampler (sampler.cu): sample_token for every row.
 struct SampleParams {
     float temperature;

@@ -16,6 +16,10 @@ namespace nk {
 struct TcOperand {
     const float *hi = nullptr, *lo = nullptr;
     int N = 0, K = 0, N_pad = 0, K_pad = 0;
+    // > 0: rows [0, H) and [H, 2H) (gate and value of a SwiGLU) are stored
+    // interleaved in blocks of 32: gate rows 32b..32b+31, then value rows
+    // 32b..32b+31, so a tile holds both halves of its channels.
+    int pair_half = 0;
     alignas(64) unsigned char map_hi[128];     // 256-row boxes
     alignas(64) unsigned char map_lo[128];
     alignas(64) unsigned char map_hi128[128];  // 128-row boxes
@@ -32,6 +36,7 @@ struct TcWeights {
 struct TcSource {
     const float *w;
     int N, K;
+    int pair_half = 0;  // H: interleave gate / value rows (needs N == 2H, H % 32 == 0)
 };
 
 // Epilogue of one projection: either store C = acc (+ bias) (R + ...), or
@@ -45,6 +50,12 @@ struct TcEpilogue {
     int ldr = 0;
     float *best_val = nullptr;
     uint32_t *best_idx = nullptr;
+    // SwiGLU mode (operand with pair_half = H): instead of C, write
+    // s[m, j] = SiLU(acc_gate + bias[j]) * (acc_value + bias[H + j]) for
+    // j < H, row stride ldc, as f32 into C (C_lo == nullptr) or as the 3xTF32
+    // operand pair hi = tf32(s) into C, lo = tf32(s - hi) into C_lo.
+    bool swiglu = false;
+    float *C_lo = nullptr;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.

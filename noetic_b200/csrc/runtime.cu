@@ -444,6 +444,10 @@ struct nk_decoder {
     // small-batch engine: layer pointers and CUDA graphs of the greedy step,
     // one per (tokens in, tokens out) device buffer pair
     std::vector<nk::SmallLayer> small_layers;
+    // persistent step kernel: device copy of the layer pointers, barrier words
+    nk::SmallLayer *layers_dev = nullptr;
+    const float *layers_arena = nullptr;  // model arena the layer tables point into
+    uint32_t *sync = nullptr;
     struct StepGraph {
         const uint32_t *in;
         uint32_t *out;
@@ -473,7 +477,8 @@ struct nk_decoder {
                         (void *)p_y, (void *)p_last, (void *)p_scan, (void *)p_logits, (void *)p_ids,
                         (void *)p_lens})
             if (p) cudaFree(p);
-        for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo})
+        for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo,
+                        (void *)layers_dev, (void *)sync})
             if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         for (auto &gph : graphs) cudaGraphExecDestroy(gph.exec);
@@ -563,6 +568,41 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
     }
 }
 
+// s = SiLU(a) * b of up_proj (infer.rs:185-190) in the form the down
+// projection reads (tensor-core operand pair when t_dn, else f32); returns
+// where it is.  With the tensor-core operand stored gate/value-interleaved
+// the SwiGLU runs in the projection's epilogue and the [M, 2H] product never
+// reaches memory; the pair then goes to `scratch` ([M, 2H] floats), never to
+// `gated`'s pair, which may be the A operand this projection is reading.
+// Otherwise the product goes to `scratch` and a row kernel applies SwiGLU.
+Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W, const nk::TcOperand *Wtc,
+                   int H, const float *bias, float *scratch, const Act &gated, bool t_dn) {
+    if (tc && Wtc->pair_half == H) {
+        ProfScope prof(dec, M, 2 * H, K, false, true);
+        nk::TcEpilogue ep;
+        ep.swiglu = true;
+        ep.bias = bias;
+        ep.ldc = H;
+        Act out = gated;
+        if (t_dn) {
+            out = Act{nullptr, scratch, scratch + (size_t)M * H};
+            ep.C = out.hi;
+            ep.C_lo = out.lo;
+        } else {
+            ep.C = gated.f32;
+        }
+        cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, 2 * H), dec->stream, dec->err),
+                   "tcgen05 projection + SwiGLU");
+        dec->launches += 1;
+        dec->prof_tc = dec->prof_tc || dec->profiling;
+        return out;
+    }
+    if (tc && Wtc->pair_half) fail(NK_ERR_INVALID, "interleaved up_proj operand with a different hidden width");
+    project(dec, tc, a, M, K, W, Wtc, 2 * H, bias, scratch, nullptr);
+    launch_ok(dec, nk::swiglu_rows(scratch, gated.out(t_dn), M, H, dec->stream), "swiglu");
+    return gated;
+}
+
 // tokens[m] = argmax_n (A.W^T)[m, n] without storing the product when the
 // tensor-core engine runs it (first strict maximum, tensor.rs:354-365).
 void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W,
@@ -598,11 +638,26 @@ void ensure_ready(nk_decoder *dec) {
         for (const LayerIx &L : m->layers) {
             srcs.push_back({m->dp(L.in_w), (int)(3 * m->e()), (int)m->d()});
             srcs.push_back({m->dp(L.out_w), (int)m->d(), (int)m->e()});
-            srcs.push_back({m->dp(L.up_w), (int)(2 * m->hidden()), (int)m->d()});
+            srcs.push_back({m->dp(L.up_w), (int)(2 * m->hidden()), (int)m->d(), (int)m->hidden()});
             srcs.push_back({m->dp(L.down_w), (int)m->d(), (int)m->hidden()});
         }
         srcs.push_back({m->dp(m->emb), (int)m->cfg.vocab, (int)m->d()});
         cuda_check(nk::tc_weights_build(m->tc, srcs), "tensor-core weight split");
+    }
+    if (dec->layers_arena != m->arena) {
+        // Per-layer weight pointers for the few-stream engines, host and
+        // device copies; the arena exists only after the first upload.
+        dec->small_layers.clear();
+        for (const LayerIx &L : m->layers)
+            dec->small_layers.push_back({m->dp(L.n1), m->dp(L.in_w), m->dp(L.in_b), m->dp(L.conv_w), m->dp(L.conv_b),
+                                         m->dp(L.out_w), m->dp(L.out_b), m->dp(L.n2), m->dp(L.up_w), m->dp(L.up_b),
+                                         m->dp(L.down_w), m->dp(L.down_b)});
+        cuda_check(cudaMemcpyAsync(dec->layers_dev, dec->small_layers.data(),
+                                   dec->small_layers.size() * sizeof(nk::SmallLayer), cudaMemcpyHostToDevice,
+                                   dec->stream),
+                   "upload layer table");
+        cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+        dec->layers_arena = m->arena;
     }
 }
 
@@ -616,7 +671,8 @@ void check_err_flag(nk_decoder *dec) {
         cuda_check(cudaMemsetAsync(dec->err, 0, sizeof(int), dec->stream), "clear error flag");
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
-                                ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired)");
+                                ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 111-113 persistent "
+                                "step wait expired)");
     }
 }
 
@@ -628,13 +684,6 @@ bool use_small(const nk_decoder *dec) {
 
 nk::SmallStepArgs small_args(nk_decoder *dec, const uint32_t *tokens, uint32_t *tokens_out, bool want_logits) {
     nk_model *m = dec->model;
-    if (dec->small_layers.size() != m->cfg.n_layer) {
-        dec->small_layers.clear();
-        for (const LayerIx &L : m->layers)
-            dec->small_layers.push_back({m->dp(L.n1), m->dp(L.in_w), m->dp(L.in_b), m->dp(L.conv_w), m->dp(L.conv_b),
-                                         m->dp(L.out_w), m->dp(L.out_b), m->dp(L.n2), m->dp(L.up_w), m->dp(L.up_b),
-                                         m->dp(L.down_w), m->dp(L.down_b)});
-    }
     nk::SmallStepArgs a{};
     a.tokens = tokens;
     a.tokens_out = tokens_out;
@@ -660,8 +709,20 @@ nk::SmallStepArgs small_args(nk_decoder *dec, const uint32_t *tokens, uint32_t *
     return a;
 }
 
+bool use_persistent(const nk_decoder *dec) {
+    const nk_model *m = dec->model;
+    return (dec->engine & 64) && !(dec->engine & 8) &&
+           nk::persistent_step_supported((int)dec->S, (int)m->d(), (int)m->e(), (int)m->hidden(), (int)m->k(),
+                                         (int)m->cfg.vocab, (int)m->cfg.n_layer);
+}
+
 void small_step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
     const nk::SmallStepArgs a = small_args(dec, tokens, tokens_out, want_logits);
+    if (use_persistent(dec)) {
+        cuda_check(nk::persistent_step(a, dec->layers_dev, dec->sync, dec->stream), "persistent decode step");
+        dec->launches += 1;
+        return;
+    }
     int n = 0;
     cuda_check(nk::small_step(a, dec->stream, &n), "small-batch step");
     dec->launches += (uint64_t)n;
@@ -735,9 +796,9 @@ void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint3
                                       gated.out(t_out), S, E, k, st), "ssm step");
         project(dec, t_out, gated, S, E, m->dp(L.out_w), w_out, d, m->dp(L.out_b), dec->x, dec->x);
         launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n2), m->cfg.eps, nrm.out(t_up), S, d, st), "rmsnorm");
-        project(dec, t_up, nrm, S, d, m->dp(L.up_w), w_up, 2 * H, m->dp(L.up_b), dec->u, nullptr);
-        launch_ok(dec, nk::swiglu_rows(dec->u, gated.out(t_dn), S, H, st), "swiglu");
-        project(dec, t_dn, gated, S, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->x, dec->x);
+        const Act s_act = project_swiglu(dec, t_up, nrm, S, d, m->dp(L.up_w), w_up, H, m->dp(L.up_b), dec->u, gated,
+                                         t_dn);
+        project(dec, t_dn, s_act, S, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->x, dec->x);
     }
     const nk::TcOperand *w_lg = tc_op(m, 4 * m->cfg.n_layer);
     const bool t_lg = use_tc(dec, S, V, d, w_lg);
@@ -821,9 +882,9 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
                           "prefill scan");
             project(dec, t_out, gated, R, E, m->dp(L.out_w), w_out, d, m->dp(L.out_b), dec->p_x, dec->p_x);
             launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n2), m->cfg.eps, nrm.out(t_up), R, d, st), "rmsnorm");
-            project(dec, t_up, nrm, R, d, m->dp(L.up_w), w_up, 2 * H, m->dp(L.up_b), dec->p_u, nullptr);
-            launch_ok(dec, nk::swiglu_rows(dec->p_u, gated.out(t_dn), R, H, st), "swiglu");
-            project(dec, t_dn, gated, R, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->p_x, dec->p_x);
+            const Act s_act = project_swiglu(dec, t_up, nrm, R, d, m->dp(L.up_w), w_up, H, m->dp(L.up_b), dec->p_u,
+                                             gated, t_dn);
+            project(dec, t_dn, s_act, R, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->p_x, dec->p_x);
         }
         launch_ok(dec, nk::gather_last_rows(dec->p_x, d_lens, (int)t0, tcc, dec->p_last, S, d, st), "gather last");
         launch_ok(dec, nk::advance_heads_prompt(dec->heads, d_lens, (int)t0, tcc, S, k, st), "advance heads");
@@ -1101,12 +1162,16 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         const size_t act_w = std::max({d, E, H});
         dalloc(&dec->ahi, S * act_w, "operand hi");
         dalloc(&dec->alo, S * act_w, "operand lo");
-        const size_t tiles = std::max<size_t>(nk::tc_argmax_parts((int)V, 128), nk::small_logit_tiles((int)V));
+        const size_t tiles = std::max<size_t>({(size_t)nk::tc_argmax_parts((int)V, 128),
+                                               (size_t)nk::small_logit_tiles((int)V),
+                                               (size_t)nk::persistent_partials()});
         dalloc(&dec->best_val, S * tiles, "argmax partials");
         dalloc(&dec->best_idx, S * tiles, "argmax partials");
         dalloc(&dec->tok_a, S, "tokens");
         dalloc(&dec->tok_b, S, "tokens");
         dalloc(&dec->err, 1, "error flag");
+        dalloc(&dec->sync, 2, "barrier words");
+        dalloc(&dec->layers_dev, model->cfg.n_layer, "layer table");
         dalloc(&dec->rng, S * 4, "rng");
         cuda_check(cudaMemset(dec->err, 0, sizeof(int)), "memset");
         cuda_check(cudaMemset(dec->logits, 0, S * V * sizeof(float)), "memset");
@@ -1354,7 +1419,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 63) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 127) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

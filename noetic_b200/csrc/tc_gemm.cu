@@ -87,7 +87,33 @@ struct TcArgs {
     uint32_t *best_idx;
     int n_tiles;
     int *err;
+    int swiglu_H;        // SwiGLU mode when > 0 (interleaved operand)
+    float *C_lo;         // SwiGLU mode: lo half of the operand pair, or null for f32
+    // Tiles [0, full_units) run at width BN; each later tile (the last,
+    // partial wave of the grid) runs as two units of width BN / 2, so that
+    // wave takes half as long.
+    int full_units;
 };
+
+// Work unit u of the tile loop: output rows m0.., columns n0.. of `width`.
+struct Unit {
+    int m0, n0, tn, width;
+};
+
+template <int BN>
+__device__ __forceinline__ Unit unit_of(int u, int full_units, int n_tiles_n) {
+    int t = u, hs = -1;
+    if (BN == 256 && u >= full_units) {
+        t = full_units + ((u - full_units) >> 1);
+        hs = (u - full_units) & 1;
+    }
+    Unit x;
+    x.m0 = (t / n_tiles_n) * BM;
+    x.tn = t % n_tiles_n;
+    x.n0 = x.tn * BN + (hs > 0 ? BN / 2 : 0);
+    x.width = hs < 0 ? BN : BN / 2;
+    return x;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -166,13 +192,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+          "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(THREADS, Tile<BN>::CTAS_PER_SM)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
-               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
+               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
+               const __grid_constant__ CUtensorMap mapBh2, const __grid_constant__ CUtensorMap mapBl2, TcArgs p) {
     using T = Tile<BN>;
     constexpr int STAGES = T::STAGES, STAGE_BYTES = T::STAGE_BYTES, B_BYTES = T::B_BYTES;
     constexpr uint32_t TMEM_COLS = T::TMEM_COLS, IDESC = T::IDESC;
+    // Half-width units: N = BN / 2 in the instruction descriptor.
+    constexpr uint32_t IDESC_HALF = (IDESC & ~(0x3Fu << 17)) | ((uint32_t)(BN >> 4) << 17);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned tile area (swizzle atoms must not straddle their period).
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -183,6 +225,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles_n = (p.N + BN - 1) / BN;
     const int n_tiles = n_tiles_n * ((p.M + BM - 1) / BM);
+    const int n_units = p.full_units + 2 * (n_tiles - p.full_units);
     const int kblocks = (p.K + BK - 1) / BK;
 
     const uint32_t bar_full0 = smem_u32(&bars[0]);
@@ -203,6 +246,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAl) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBh) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBl) : "memory");
+        if (p.full_units < n_tiles) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBh2) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBl2) : "memory");
+        }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -221,8 +268,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         int stage = 0;
         uint32_t phase = 0;
         int issued = 0;
-        for (int t = blockIdx.x; t < n_tiles && !*(volatile int *)&s_abort; t += gridDim.x) {
-            const int m0 = (t / n_tiles_n) * BM, n0 = (t % n_tiles_n) * BN;
+        for (int u = blockIdx.x; u < n_units && !*(volatile int *)&s_abort; u += gridDim.x) {
+            const Unit un = unit_of<BN>(u, p.full_units, n_tiles_n);
+            const bool wide = un.width == BN;
+            const CUtensorMap *mBh = wide ? &mapBh : &mapBh2, *mBl = wide ? &mapBl : &mapBl2;
+            const uint32_t bytes = wide ? STAGE_BYTES : 2 * A_BYTES + B_BYTES;
             for (int kb = 0; kb < kblocks; ++kb) {
                 if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
                     atomicExch(p.err, 101);
@@ -232,12 +282,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 if (*(volatile int *)&s_abort) break;
                 uint8_t *st = smem + stage * STAGE_BYTES;
                 const uint32_t full = bar_full0 + 8 * stage;
-                mbar_expect_tx(full, STAGE_BYTES);
+                mbar_expect_tx(full, bytes);
                 const int kx = kb * BK;
-                tma_load_2d(smem_u32(st), &mapAh, full, kx, m0);
-                tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, m0);
-                tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
-                tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
+                tma_load_2d(smem_u32(st), &mapAh, full, kx, un.m0);
+                tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, un.m0);
+                tma_load_2d(smem_u32(st + 2 * A_BYTES), mBh, full, kx, un.n0);
+                tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), mBl, full, kx, un.n0);
                 ++issued;
                 if (++stage == STAGES) {
                     stage = 0;
@@ -263,7 +313,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         int stage = 0;
         uint32_t phase = 0;
         int i = 0;
-        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
+            const uint32_t idesc = (BN != 256 || u < p.full_units) ? IDESC : IDESC_HALF;
             // The accumulators are free once the epilogue drained tile i - 1.
             if (!mbar_wait(bar_acc_empty, (uint32_t)((i & 1) ^ 1)) || *(volatile int *)&s_abort) {
                 atomicExch(p.err, 104);
@@ -287,9 +338,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 for (int kk = 0; kk < BK / 8; ++kk) {
                     const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
                     const uint32_t acc = (kb | kk) ? 1u : 0u;
-                    mma_tf32(tmem, dAh + off, dBh + off, IDESC, acc);
-                    mma_tf32(tmem + BN, dAh + off, dBl + off, IDESC, acc);
-                    mma_tf32(tmem + BN, dAl + off, dBh + off, IDESC, 1u);
+                    mma_tf32(tmem, dAh + off, dBh + off, idesc, acc);
+                    mma_tf32(tmem + BN, dAh + off, dBl + off, idesc, acc);
+                    mma_tf32(tmem + BN, dAl + off, dBh + off, idesc, 1u);
                 }
                 mma_commit(bar_empty0 + 8 * stage);
                 if (++stage == STAGES) {
@@ -307,12 +358,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         // 32*(w%4) .. +31 and half of the columns (warpgroup (w-4)/4).
         const int q = warp & 3;
         const int half = (warp - 4) >> 2;
-        constexpr int COLS = BN / 2;
         const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
         const bool argmax_mode = p.best_val != nullptr;
         int i = 0;
-        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
-            const int m0 = (t / n_tiles_n) * BM, n0 = (t % n_tiles_n) * BN;
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
+            const Unit un = unit_of<BN>(u, p.full_units, n_tiles_n);
+            const int m0 = un.m0, n0 = un.n0;
+            const int COLS = un.width / 2;  // columns of this warpgroup
             const bool ok = mbar_wait(bar_acc_full, (uint32_t)(i & 1)) && !*(volatile int *)&s_abort;
             __syncwarp();
             if (!ok) {
@@ -323,7 +375,49 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             const int row = m0 + q * 32 + lane;
             float best = -INFINITY;
             uint32_t best_n = 0xFFFFFFFFu;
-            for (int c0 = half * COLS; c0 < (half + 1) * COLS; c0 += 32) {
+            // SwiGLU: 64-column blocks of (32 gate, 32 value) columns of the
+            // same 32 channels; both accumulator chains summed first.
+            for (int c0 = half * COLS; p.swiglu_H && c0 < (half + 1) * COLS; c0 += 64) {
+                if (n0 + c0 >= p.N) break;  // warp-uniform
+                const int j0 = (n0 + c0) >> 1;
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+#pragma unroll
+                for (int sub = 0; sub < 32; sub += 16) {
+                    float a[16], b[16], t[16];
+                    tmem_ld16(ta + sub, a);
+                    tmem_ld16(ta + BN + sub, t);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) a[jj] = a[jj] + t[jj];
+                    tmem_ld16(ta + 32 + sub, b);
+                    tmem_ld16(ta + BN + 32 + sub, t);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) b[jj] = b[jj] + t[jj];
+                    if (row < p.M) {
+                        const int j = j0 + sub;
+                        float *out = p.C + (size_t)row * p.ldc + j;
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj += 4) {
+                            float4 sv;
+                            sv.x = silu(a[jj + 0] + p.bias[j + jj + 0]) * (b[jj + 0] + p.bias[p.swiglu_H + j + jj + 0]);
+                            sv.y = silu(a[jj + 1] + p.bias[j + jj + 1]) * (b[jj + 1] + p.bias[p.swiglu_H + j + jj + 1]);
+                            sv.z = silu(a[jj + 2] + p.bias[j + jj + 2]) * (b[jj + 2] + p.bias[p.swiglu_H + j + jj + 2]);
+                            sv.w = silu(a[jj + 3] + p.bias[j + jj + 3]) * (b[jj + 3] + p.bias[p.swiglu_H + j + jj + 3]);
+                            if (p.C_lo) {
+                                float4 h, l;
+                                h.x = tf32_round(sv.x); l.x = tf32_round(sv.x - h.x);
+                                h.y = tf32_round(sv.y); l.y = tf32_round(sv.y - h.y);
+                                h.z = tf32_round(sv.z); l.z = tf32_round(sv.z - h.z);
+                                h.w = tf32_round(sv.w); l.w = tf32_round(sv.w - h.w);
+                                *reinterpret_cast<float4 *>(out + jj) = h;
+                                *reinterpret_cast<float4 *>(p.C_lo + (size_t)row * p.ldc + j + jj) = l;
+                            } else {
+                                *reinterpret_cast<float4 *>(out + jj) = sv;
+                            }
+                        }
+                    }
+                }
+            }
+            for (int c0 = half * COLS; !p.swiglu_H && c0 < (half + 1) * COLS; c0 += 32) {
                 if (n0 + c0 >= p.N) break;  // warp-uniform
                 float v[32], corr[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
@@ -385,7 +479,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 // tile's columns: partial 2*tile_n + half, so partial order is
                 // column order and the reduction's earliest-partial tie rule
                 // keeps the first maximum.
-                const size_t slot = (size_t)row * p.n_tiles + 2 * (t % n_tiles_n) + half;
+                const size_t slot = (size_t)row * p.n_tiles + 2 * un.tn + half;
                 p.best_val[slot] = best;
                 p.best_idx[slot] = best_n;
             }
@@ -401,16 +495,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
 }
 
 // hi = tf32(x), lo = tf32(x - hi), over rows x cols with a row stride.
+// pair_half = H > 0: source row r lands at the interleaved position (gate
+// rows r < H and value rows H + r in alternating blocks of 32).
 __global__ void split_tf32_k(const float *__restrict__ src, int ld, float *__restrict__ hi,
-                             float *__restrict__ lo, int rows, int cols) {
+                             float *__restrict__ lo, int rows, int cols, int pair_half) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)rows * cols) return;
     const int64_t r = i / cols;
     const int c = (int)(i - r * cols);
+    int64_t rd = r;
+    if (pair_half > 0) {
+        const int64_t v = r < pair_half ? r : r - pair_half;
+        rd = (v >> 5) * 64 + (r < pair_half ? 0 : 32) + (v & 31);
+    }
     const float x = src[(size_t)r * ld + c];
     const float h = tf32_round(x);
-    hi[i] = h;
-    lo[i] = tf32_round(x - h);
+    hi[(size_t)rd * cols + c] = h;
+    lo[(size_t)rd * cols + c] = tf32_round(x - h);
 }
 
 // ---- host side
@@ -442,10 +543,11 @@ bool make_map(CUtensorMap *map, const float *base, int rows, int cols, int box_r
     return r == CUDA_SUCCESS;
 }
 
-cudaError_t split(const float *src, int ld, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
+cudaError_t split(const float *src, int ld, float *hi, float *lo, int rows, int cols, cudaStream_t st,
+                  int pair_half = 0) {
     const int64_t n = (int64_t)rows * cols;
     if (n == 0) return cudaSuccess;
-    split_tf32_k<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, ld, hi, lo, rows, cols);
+    split_tf32_k<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(src, ld, hi, lo, rows, cols, pair_half);
     return cudaGetLastError();
 }
 
@@ -489,8 +591,10 @@ cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs) {
         const size_t n = ((size_t)s.N * s.K + 63) & ~size_t(63);
         float *hi = w.arena + off, *lo = w.arena + off + n;
         off += 2 * n;
-        e = split(s.w, s.K, hi, lo, s.N, s.K, nullptr);
+        const bool pair = s.pair_half > 0 && s.pair_half % 32 == 0 && s.N == 2 * s.pair_half;
+        e = split(s.w, s.K, hi, lo, s.N, s.K, nullptr, pair ? s.pair_half : 0);
         if (e != cudaSuccess) return e;
+        op.pair_half = pair ? s.pair_half : 0;
         op.hi = hi;
         op.lo = lo;
         op.N = s.N;
@@ -519,7 +623,7 @@ void tc_weights_free(TcWeights &w) {
 }
 
 template <int BN>
-cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, const TcArgs &a, int M,
+cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, TcArgs a, int M,
                       cudaStream_t st) {
     static thread_local int attr_dev = -1;
     int dev = 0;
@@ -540,18 +644,37 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
         if (num_sms <= 0) num_sms = 148;
     }
     const long tiles = (long)tc_tiles_n(W.N, BN) * ((M + BM - 1) / BM);
-    const unsigned grid = (unsigned)std::min<long>(tiles, (long)num_sms * Tile<BN>::CTAS_PER_SM);
-    tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(mAh, mAl, *(const CUtensorMap *)mh,
-                                                                    *(const CUtensorMap *)ml, a);
+    const long slots = (long)num_sms * Tile<BN>::CTAS_PER_SM;
+    const unsigned grid = (unsigned)std::min<long>(tiles, slots);
+    // A last wave that covers at most half the grid runs as half-width units
+    // (full-width tiles only for the argmax epilogue's partial layout).
+    const long rem = tiles % (long)grid;
+    a.full_units = (int)((BN == 256 && !a.best_val && rem > 0 && 2 * rem <= (long)grid) ? tiles - rem : tiles);
+    tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(
+        mAh, mAl, *(const CUtensorMap *)mh, *(const CUtensorMap *)ml, *(const CUtensorMap *)W.map_hi128,
+        *(const CUtensorMap *)W.map_lo128, a);
     return cudaGetLastError();
 }
 
 cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
                     int bn, cudaStream_t st, int *err) {
     if (W.K != K || M <= 0 || (bn != 128 && bn != 256)) return cudaErrorInvalidValue;
+    // SwiGLU mode and the interleaved operand go together; argmax never with it.
+    if (ep.swiglu != (W.pair_half > 0) || (ep.swiglu && (ep.best_val || !ep.bias))) return cudaErrorInvalidValue;
+    // Tiles read A rows while other tiles' epilogues write: no output may
+    // overlap the A operand.
+    {
+        auto overlap = [](const float *a, size_t na, const float *b, size_t nb) {
+            return a && b && a < b + nb && b < a + na;
+        };
+        const size_t na = (size_t)M * K, nc = (size_t)M * (size_t)std::max(ep.ldc, 1);
+        for (const float *o : {(const float *)ep.C, (const float *)ep.C_lo})
+            if (overlap(o, nc, A_hi, na) || overlap(o, nc, A_lo, na)) return cudaErrorInvalidValue;
+    }
     alignas(64) CUtensorMap mAh, mAl;
     if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
-    TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err};
+    TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err,
+              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0};
     return bn == 256 ? launch_tc<256>(mAh, mAl, W, a, M, st) : launch_tc<128>(mAh, mAl, W, a, M, st);
 }
 

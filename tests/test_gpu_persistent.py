@@ -1,0 +1,110 @@
+"""The single persistent decode-step kernel (engine bit 6, 1..4 streams:
+weights streamed through a shared-memory ring, grid barriers between
+phases) against the oracle and against the multi-kernel small-batch step."""
+
+import numpy as np
+import pytest
+
+from conftest import c1_cfg, same_model, state_rel_err, tiny_cfg
+
+pytestmark = pytest.mark.gpu
+
+PERSISTENT = 64  # engine bit: the whole step as one persistent kernel
+
+
+def _run_both(gpu, orc, kw, S, T, seed, base):
+    from noetic_b200.prompts import uniform_prompts
+
+    om, gm = same_model(orc, gpu, kw, seed=seed)
+    ids = uniform_prompts(S, T, kw["vocab"], base)
+    pers, multi = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    pers.set_engine(PERSISTENT)
+    ods = [orc.Decoder(om) for _ in range(S)]
+    worst_o = worst_m = 0.0
+    for t in range(T):
+        a = pers.step(ids[:, t]).copy()
+        b = multi.step(ids[:, t])
+        worst_m = max(worst_m, float(np.abs(a - b).max()))
+        for s in range(S):
+            worst_o = max(worst_o, float(np.abs(a[s] - ods[s].step(ids[s, t])).max()))
+    return pers, multi, ods, worst_o, worst_m
+
+
+@pytest.mark.parametrize("S", [1, 2, 3, 4])
+def test_persistent_step_matches_oracle_and_multi_kernel(gpu, orc, S):
+    kw = c1_cfg(dict)
+    pers, multi, ods, worst_o, worst_m = _run_both(gpu, orc, kw, S, 6, 0, 90)
+    assert worst_o <= 1e-3, worst_o
+    assert worst_m <= 1e-5, worst_m
+    sa, ha = pers.get_state()
+    sb, hb = multi.get_state()
+    assert np.array_equal(ha, hb) and state_rel_err(sa, sb) <= 1e-5
+    for s in range(S):
+        ost, oh = ods[s].get_state()
+        assert ha[s] == oh and state_rel_err(sa[s], ost) <= 1e-4
+
+
+def test_persistent_step_headline_widths(gpu, orc):
+    """d = E = 1024, H = 3072, vocab 32768 (the benchmark model's widths) on
+    two layers: 6-row and 2-row stages, uneven row splits over the SMs."""
+    kw = dict(vocab=32768, d_model=1024, n_layer=2, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    pers, _, ods, worst_o, worst_m = _run_both(gpu, orc, kw, 2, 3, 2, 5000)
+    assert worst_o <= 1e-3, worst_o
+    assert worst_m <= 1e-5, worst_m
+    st, hd = pers.get_state()
+    for s in range(2):
+        ost, oh = ods[s].get_state()
+        assert hd[s] == oh and state_rel_err(st[s], ost) <= 1e-4
+
+
+def test_persistent_step_tiny_models(gpu, orc):
+    # Fewer rows than SMs in every phase (most CTAs own nothing), conv widths 1 and 7.
+    for kw in [tiny_cfg(dict, 17, conv_k=1, n_layer=1), tiny_cfg(dict, 17, conv_k=7, n_layer=3),
+               tiny_cfg(dict, 300, conv_k=3, n_layer=2)]:
+        pers, _, ods, worst_o, worst_m = _run_both(gpu, orc, kw, 3, 5, 3, 11)
+        assert worst_o <= 1e-3 and worst_m <= 1e-5, (kw, worst_o, worst_m)
+        st, hd = pers.get_state()
+        for s in range(3):
+            ost, oh = ods[s].get_state()
+            assert hd[s] == oh and state_rel_err(st[s], ost) <= 1e-4
+
+
+def test_persistent_greedy_replay_follows_the_oracle(gpu, orc):
+    """Greedy steps (graph-replayed after the first) teacher-forced with the
+    oracle's tokens; one kernel launch per step."""
+    kw = c1_cfg(dict)
+    om, gm = same_model(orc, gpu, kw, seed=0)
+    S = 3
+    dec = gpu.Decoder(gm, S)
+    dec.set_engine(PERSISTENT)
+    ods = [orc.Decoder(om) for _ in range(S)]
+    toks = np.array([5, 600, 1023], dtype=np.uint32)
+    checked = 0
+    n0 = dec.launch_count()
+    steps = 20
+    for step in range(steps):
+        nxt = dec.step_greedy(toks)
+        for s in range(S):
+            lg = ods[s].step(int(toks[s])).copy()
+            top2 = np.sort(lg)[-2:]
+            if top2[1] - top2[0] > 1e-3:
+                assert int(nxt[s]) == orc.argmax(lg), (step, s)
+                checked += 1
+        toks = np.array([orc.argmax(ods[s].logits) for s in range(S)], dtype=np.uint32)
+    assert checked >= 40
+    assert dec.launch_count() - n0 == steps
+
+
+def test_persistent_matches_fused_greedy_tokens(gpu, orc):
+    # The same greedy rollout through both engines, logits never stored.
+    kw = c1_cfg(dict)
+    _, gm = same_model(orc, gpu, kw, seed=1)
+    a, b = gpu.Decoder(gm, 4), gpu.Decoder(gm, 4)
+    a.set_engine(PERSISTENT)
+    ta = tb = np.array([1, 2, 3, 4], dtype=np.uint32)
+    agree = 0
+    for _ in range(16):
+        ta, tb = a.step_greedy(ta).copy(), b.step_greedy(tb).copy()
+        agree += int((ta == tb).sum())
+        tb = ta  # keep both on the same trajectory
+    assert agree >= 62

@@ -117,3 +117,52 @@ def test_fused_argmax_epilogue_matches_materialised_logits(gpu, orc):
     st_a, _ = fused.get_state()
     st_b, _ = plain.get_state()
     assert state_rel_err(st_a, st_b) <= 1e-6
+
+
+def test_hidden_width_off_the_interleave_grid(gpu, orc):
+    """H = 600 is not a multiple of 32: the up projection keeps its row order
+    and SwiGLU runs as a row kernel instead of in the projection epilogue."""
+    kw = dict(vocab=512, d_model=200, n_layer=2, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=6)
+    S, T = 256, 3
+    ids = _ids(S, T, kw["vocab"], 31)
+    tc, f32 = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    f32.set_engine(1)
+    tc.profile_begin()
+    for t in range(T):
+        a = tc.step(ids[:, t]).copy()
+        b = f32.step(ids[:, t])
+        assert np.abs(a - b).max() <= 1e-4, t
+    assert tc.profile_end()["tensor_core"]
+    sa, _ = tc.get_state()
+    sb, _ = f32.get_state()
+    assert state_rel_err(sa, sb) <= 1e-5
+    od = orc.Decoder(om)
+    for t in range(T):
+        ref = od.step(ids[7, t])
+    assert np.abs(a[7] - ref).max() <= 1e-3
+
+
+def test_last_wave_half_width_units(gpu, orc):
+    """16384 streams of a d=1024 model: out_proj and down_proj have 512
+    tiles of 128 x 256 on 148 SMs, so the last 68 tiles run as 136
+    half-width units (in_proj: 56 -> 112); every stream, the last rows and
+    columns included, equals the f32 engine."""
+    kw = dict(vocab=2048, d_model=1024, n_layer=1, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=8)
+    S = 16384
+    ids = _ids(S, 2, kw["vocab"], 900)
+    tc, f32 = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    f32.set_engine(1)
+    for t in range(2):
+        a = tc.step(ids[:, t]).copy()
+        b = f32.step(ids[:, t])
+        assert np.abs(a - b).max() <= 1e-4, t
+    sa, _ = tc.get_state()
+    sb, _ = f32.get_state()
+    assert state_rel_err(sa, sb) <= 1e-5
+    for s in [0, 16383]:
+        od = orc.Decoder(om)
+        for t in range(2):
+            ref = od.step(ids[s, t])
+        assert np.abs(a[s] - ref).max() <= 1e-3, s
