@@ -15,7 +15,7 @@
 //                   activations, so the stream runs ahead across phases and
 //                   layers, limited only by free stages; HBM stays busy
 //                   while the consumers wait at grid barriers.
-//   8 consumer      per phase: read the phase's input vector (RMSNorm of x,
+//   16 consumer     per phase: read the phase's input vector (RMSNorm of x,
 //   warps           g, or SwiGLU output) from L2 into shared memory, take
 //                   the streamed rows round-robin (one warp per row, f32
 //                   FMA dot products), apply the phase's epilogue, then a
@@ -47,12 +47,13 @@ namespace nk {
 
 namespace {
 
-constexpr int CWARPS = 8;                    // consumer warps
+constexpr int CWARPS = 16;                   // consumer warps
 constexpr int CTHREADS = CWARPS * 32;        // consumer threads (named barrier 1)
 constexpr int PTHREADS = CTHREADS + 32;      // + one producer warp
 constexpr int STAGE_BYTES = 24 * 1024;       // 6 rows of 1024 f32, 2 rows of 3072
 constexpr int SMEM_LIMIT = 227 * 1024;
 constexpr uint64_t WAIT_NS = 1000000000ull;  // bound of every wait
+constexpr int KCONV = 8;                     // largest conv width this kernel takes
 
 struct PersistParams {
     const uint32_t *tokens;
@@ -357,6 +358,40 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
             const int K = ph.K;
             float *state = kind == 0 ? p.state + (size_t)layer * M * (p.k + 1) * p.E : nullptr;
 
+            // ---- operands of the phase epilogue, fetched before anything
+            // waits: thread t < n * MR owns row i = t / MR for stream r = t % MR.
+            const bool mine = kind != 4 && tid < ph.n * MR && (tid % MR) < M;
+            const int ei = tid / MR, er = tid % MR, ej = ph.u0 + ei;
+            float pb0 = 0.f, pb1 = 0.f, pb2 = 0.f, pcb = 0.f, ph_old = 0.f, pbase = 0.f;
+            float pcw[KCONV], prv[KCONV];
+#pragma unroll
+            for (int qq = 0; qq < KCONV; ++qq) pcw[qq] = prv[qq] = 0.f;
+            if (mine) {
+                if (kind == 0) {
+                    const int E = p.E, kk = p.k;
+                    pb0 = L->in_b[ej];
+                    pb1 = L->in_b[E + ej];
+                    pb2 = L->in_b[2 * E + ej];
+                    pcb = L->conv_b[ej];
+                    const float *ring_s = state + (size_t)er * (kk + 1) * E;
+                    const uint32_t head = s_head[er];
+#pragma unroll
+                    for (int qq = 0; qq < KCONV; ++qq)
+                        if (qq < kk) {
+                            pcw[qq] = L->conv_w[(size_t)qq * E + ej];
+                            if (qq > 0) prv[qq] = ring_s[(size_t)((head + (uint32_t)kk - (uint32_t)qq) % (uint32_t)kk) * E + ej];
+                        }
+                    ph_old = ring_s[(size_t)kk * E + ej];
+                } else if (kind == 2) {
+                    pb0 = L->up_b[ej];
+                    pb1 = L->up_b[p.H + ej];
+                } else {
+                    pb0 = kind == 1 ? L->out_b[ej] : L->down_b[ej];
+                    pbase = (kind == 1 && layer == 0) ? __ldg(p.emb + (size_t)s_tok[er] * p.d + ej)
+                                                      : p.x[(size_t)er * p.d + ej];
+                }
+            }
+
             // ---- input vector of the phase
             if (kind == 0 || kind == 2 || kind == 4) {
                 // Layer 0 normalises the tokens' embedding rows directly.
@@ -390,25 +425,13 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                         dot_row<MR>(chunk + (size_t)j * K, act, K, acc);
                         const int i = r0 + j;  // row within the region
                         const int u = ph.u0 + i;
-                        if (kind == 0 || kind == 2) {
+                        if (kind != 4) {
                             if (lane < MR) {
                                 float v = acc[0];
 #pragma unroll
                                 for (int r = 1; r < MR; ++r)
                                     if (lane == r) v = acc[r];
                                 res[(rg * ph.n + i) * MR + lane] = v;
-                            }
-                        } else if (kind == 1 || kind == 3) {
-                            const float *b = kind == 1 ? L->out_b : L->down_b;
-#pragma unroll
-                            for (int r = 0; r < MR; ++r) {
-                                if (lane == r && r < M) {
-                                    float *xp = p.x + (size_t)r * p.d + u;
-                                    const float base = (kind == 1 && layer == 0)
-                                                           ? __ldg(p.emb + (size_t)s_tok[r] * p.d + u)
-                                                           : *xp;
-                                    *xp = base + (acc[r] + b[u]);
-                                }
                             }
                         } else {
 #pragma unroll
@@ -433,38 +456,35 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                 }
             }
 
-            // ---- phase epilogue
-            if (kind == 0 || kind == 2) {
+            // ---- phase epilogue: thread t < n * MR owns (row i, stream r)
+            // and applies it with the operands it fetched at phase start.
+            if (kind != 4) {
                 consumer_sync();
                 const bool live = !*(volatile int *)&s_dead && !*(volatile int *)&s_abort;
-                for (int t = tid; live && t < ph.n * MR; t += CTHREADS) {
-                    const int i = t / MR, r = t - i * MR;
-                    if (r >= M) continue;
-                    const int j = ph.u0 + i;
+                if (live && mine) {
                     if (kind == 0) {
                         const int E = p.E, kk = p.k;
-                        const float v = res[(0 * ph.n + i) * MR + r] + L->in_b[j];
-                        const float zz = res[(1 * ph.n + i) * MR + r] + L->in_b[E + j];
-                        const float oo = res[(2 * ph.n + i) * MR + r] + L->in_b[2 * E + j];
-                        float *ring_s = state + (size_t)r * (kk + 1) * E;
-                        const uint32_t head = s_head[r];
-                        ring_s[(size_t)head * E + j] = v;
-                        float sum = L->conv_b[j];
-                        for (int qq = 0; qq < kk; ++qq) {
-                            const uint32_t slot = (head + (uint32_t)kk - (uint32_t)qq) % (uint32_t)kk;
-                            sum = sum + L->conv_w[(size_t)qq * E + j] * (qq == 0 ? v : ring_s[(size_t)slot * E + j]);
-                        }
+                        const float v = res[(0 * ph.n + ei) * MR + er] + pb0;
+                        const float zz = res[(1 * ph.n + ei) * MR + er] + pb1;
+                        const float oo = res[(2 * ph.n + ei) * MR + er] + pb2;
+                        float *ring_s = state + (size_t)er * (kk + 1) * E;
+                        const uint32_t head = s_head[er];
+                        ring_s[(size_t)head * E + ej] = v;
+                        float sum = pcb;
+#pragma unroll
+                        for (int qq = 0; qq < KCONV; ++qq)
+                            if (qq < kk) sum = sum + pcw[qq] * (qq == 0 ? v : prv[qq]);
                         const float value = silu(sum);
                         const float decay = sigmoid(zz);
-                        float *hp = ring_s + (size_t)kk * E + j;
-                        const float h = decay * (*hp) + (1.0f - decay) * value;
-                        *hp = h;
-                        p.g[(size_t)r * E + j] = h * silu(oo);
+                        const float h = decay * ph_old + (1.0f - decay) * value;
+                        ring_s[(size_t)kk * E + ej] = h;
+                        p.g[(size_t)er * E + ej] = h * silu(oo);
+                    } else if (kind == 2) {
+                        const float a = res[(0 * ph.n + ei) * MR + er];
+                        const float b = res[(1 * ph.n + ei) * MR + er];
+                        p.g[(size_t)er * p.H + ej] = silu(a + pb0) * (b + pb1);
                     } else {
-                        const int H = p.H;
-                        const float a = res[(0 * ph.n + i) * MR + r];
-                        const float b = res[(1 * ph.n + i) * MR + r];
-                        p.g[(size_t)r * H + j] = silu(a + L->up_b[j]) * (b + L->up_b[H + j]);
+                        p.x[(size_t)er * p.d + ej] = pbase + (res[ei * MR + er] + pb0);
                     }
                 }
             }
@@ -473,7 +493,9 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                 barrier_target += G;
                 consumer_sync();
                 if (tid == 0) {
-                    __threadfence();
+                    // The CTA barrier above orders every consumer's writes
+                    // before this release; the acquire below orders the
+                    // other CTAs' writes before the barrier after it.
                     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p.sync), "r"(1u) : "memory");
                     if (!*(volatile int *)&s_abort) {
                         const uint64_t t0 = gtimer();
@@ -488,7 +510,6 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                             }
                         }
                     }
-                    __threadfence();
                 }
                 consumer_sync();
             }
@@ -569,9 +590,9 @@ int sm_count() {
     return n;
 }
 
-int res_cap_for(int E, int H, int G) {
-    const int ce = (E + G - 1) / G, ch = (H + G - 1) / G;
-    return std::max(3 * ce, 2 * ch);
+int res_cap_for(int d, int E, int H, int G) {
+    const int cd = (d + G - 1) / G, ce = (E + G - 1) / G, ch = (H + G - 1) / G;
+    return std::max(cd, std::max(3 * ce, 2 * ch));
 }
 
 template <int MR>
@@ -600,7 +621,7 @@ cudaError_t launch_mr(const SmallStepArgs &a, const SmallLayer *layers_dev, uint
     p.k = a.k;
     p.V = a.V;
     p.n_layer = a.n_layer;
-    p.res_cap = res_cap_for(a.E, a.H, G) * MR;
+    p.res_cap = res_cap_for(a.d, a.E, a.H, G) * MR;
     p.nstage = stages_for<MR>(a.d, a.E, a.H, p.res_cap);
     const size_t smem = smem_bytes<MR>(a.d, a.E, a.H, p.res_cap, p.nstage);
     static size_t smem_set = 0;
@@ -630,13 +651,16 @@ cudaError_t launch_mr(const SmallStepArgs &a, const SmallLayer *layers_dev, uint
 int persistent_partials() { return sm_count(); }
 
 bool persistent_step_supported(int M, int d, int E, int H, int k, int V, int n_layer) {
-    if (M < 1 || M > 4 || n_layer < 1 || k < 1 || k > 64) return false;
+    if (M < 1 || M > 4 || n_layer < 1 || k < 1 || k > KCONV) return false;
     if (d % 4 || E % 4 || H % 4) return false;
     // Every row fits one stage; the staging of the widest activation and two
     // ring stages fit in shared memory.
     if ((size_t)std::max(d, std::max(E, H)) * 4 > (size_t)STAGE_BYTES) return false;
     const int G = sm_count();
-    const int rc = res_cap_for(E, H, G) * 4;
+    // One epilogue thread per (owned row, stream) of every phase.
+    const int most = std::max(std::max((d + G - 1) / G, (E + G - 1) / G), (H + G - 1) / G);
+    if (most * 4 > CTHREADS) return false;
+    const int rc = res_cap_for(d, E, H, G) * 4;
     return smem_bytes<4>(d, E, H, rc, 2) + 2048 <= (size_t)SMEM_LIMIT;
 }
 
