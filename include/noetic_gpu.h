@@ -186,7 +186,8 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * tensor-core tiles 128 / 256 columns wide (default: 256 while the grid
  * covers every SM twice, else 128).  Bit 6: for 1-4 streams, the whole step
  * as one persistent cooperative kernel instead of the fused small-batch
- * kernels. */
+ * kernels.  Bit 7: the CTA-pair projection kernel (256 x 256 tiles on two
+ * SMs) wherever N >= 256. */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

@@ -61,9 +61,12 @@ struct TcEpilogue {
 // Whether the tcgen05 engine takes a projection of this shape.
 bool tc_eligible(int M, int N, int K);
 
-// Tile width for an M x N projection (256 while the grid covers every SM
-// twice, else 128) and the number of column tiles at that width.
-int tc_pick_bn(int M, int N);
+// Tile choice for an M x N projection: TC_PAIR (the CTA-pair kernel, 256 x
+// 256 tiles on two SMs) when allow_pair and it fills every SM pair twice,
+// else 128 x 256 tiles while those fill every SM twice, else 128 x 128; and
+// the number of column tiles of that choice.
+constexpr int TC_PAIR = 2;
+int tc_pick_bn(int M, int N, bool allow_pair = false);
 int tc_tiles_n(int N, int bn);
 // Argmax partials per row: one per half tile (each epilogue warpgroup owns half the columns).
 int tc_argmax_parts(int N, int bn);

@@ -540,11 +540,13 @@ struct ProfScope {
     }
 };
 
-// Tile width of a tensor-core projection; engine bits 4 / 5 force 128 / 256.
+// Tile shape of a tensor-core projection; engine bits 4 / 5 / 7 force
+// 128 / 256-wide single-SM tiles / the CTA-pair kernel.
 int pick_bn(const nk_decoder *dec, int M, int N) {
     if (dec->engine & 16) return 128;
     if ((dec->engine & 32) && N >= 256) return 256;
-    return nk::tc_pick_bn(M, N);
+    if ((dec->engine & 128) && N >= 256) return nk::TC_PAIR;
+    return nk::tc_pick_bn(M, N, false);
 }
 
 // C = A.W^T (+bias) (R + ...), A read from `a` in the form `tc` selects.
@@ -1419,7 +1421,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 127) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 255) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

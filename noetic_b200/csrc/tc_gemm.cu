@@ -66,7 +66,10 @@ struct Tile {
     static constexpr int B_BYTES = BN * BK * 4;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int STAGES = BN == 256 ? 4 : 3;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+    // BN = 256: a 32 x 32 f32 transpose buffer per epilogue warp, so the
+    // epilogue reads and writes whole 128-byte row segments.
+    static constexpr int EPI_BYTES = BN == 256 ? EPI_WARPS * 32 * 32 * 4 : 0;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + 1024 + 256;
     static constexpr int CTAS_PER_SM = BN == 256 ? 1 : 2;
     // Two f32 accumulators of BN columns: the hi*hi products and the two
     // small correction products are summed in separate TMEM chains.
@@ -205,6 +208,206 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// One epilogue warp's share of a tile: TMEM lanes q*32 .. q*32+31 (output
+// rows m0 + q*32 + lane), TMEM columns [c_begin, c_end) (output columns
+// n0 + c).  Store mode writes C (+bias, +residual); SwiGLU mode writes the
+// gated product; argmax mode folds the columns into (best, best_n).
+template <int BN>
+__device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, int q, int lane, int m0, int n0,
+                                              int c_begin, int c_end, bool argmax_mode, bool vec, float &best,
+                                              uint32_t &best_n, float *stg) {
+    const int row = m0 + q * 32 + lane;
+    if (stg && !argmax_mode) {
+        // Transpose each 32 x 32 chunk through this warp's shared buffer
+        // (float4 slots XOR-swizzled by row: conflict-free both ways), then
+        // lane = column, so every load and store is one 128-byte row segment.
+        const int rbase = m0 + q * 32;
+        if (p.swiglu_H) {
+            // 64-column blocks: 32 gate columns, then the 32 value columns of
+            // the same channels; both accumulator chains summed first.
+            for (int c0 = c_begin; c0 < c_end; c0 += 64) {
+                if (n0 + c0 >= p.N) break;  // warp-uniform
+                const int j0 = (n0 + c0) >> 1;
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+#pragma unroll
+                for (int sub = 0; sub < 32; sub += 16) {
+                    float a[16], b[16], t[16];
+                    tmem_ld16(ta + sub, a);
+                    tmem_ld16(ta + BN + sub, t);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) a[jj] = a[jj] + t[jj];
+                    tmem_ld16(ta + 32 + sub, b);
+                    tmem_ld16(ta + BN + 32 + sub, t);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) b[jj] = b[jj] + t[jj];
+                    const int j = j0 + sub;
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj += 4) {
+                        float4 sv;
+                        sv.x = silu(a[jj + 0] + p.bias[j + jj + 0]) * (b[jj + 0] + p.bias[p.swiglu_H + j + jj + 0]);
+                        sv.y = silu(a[jj + 1] + p.bias[j + jj + 1]) * (b[jj + 1] + p.bias[p.swiglu_H + j + jj + 1]);
+                        sv.z = silu(a[jj + 2] + p.bias[j + jj + 2]) * (b[jj + 2] + p.bias[p.swiglu_H + j + jj + 2]);
+                        sv.w = silu(a[jj + 3] + p.bias[j + jj + 3]) * (b[jj + 3] + p.bias[p.swiglu_H + j + jj + 3]);
+                        const int c4 = (sub + jj) >> 2;
+                        *reinterpret_cast<float4 *>(stg + lane * 32 + 4 * (c4 ^ (lane & 7))) = sv;
+                    }
+                }
+                __syncwarp();
+                const int jc = j0 + lane;
+#pragma unroll 8
+                for (int r = 0; r < 32; ++r) {
+                    const int grow = rbase + r;
+                    const float sv = stg[r * 32 + 4 * ((lane >> 2) ^ (r & 7)) + (lane & 3)];
+                    if (grow < p.M) {
+                        if (p.C_lo) {
+                            const float h = tf32_round(sv);
+                            p.C[(size_t)grow * p.ldc + jc] = h;
+                            p.C_lo[(size_t)grow * p.ldc + jc] = tf32_round(sv - h);
+                        } else {
+                            p.C[(size_t)grow * p.ldc + jc] = sv;
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            return;
+        }
+        for (int c0 = c_begin; c0 < c_end; c0 += 32) {
+            if (n0 + c0 >= p.N) break;  // warp-uniform
+            float v[32], corr[32];
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4) {
+                float4 o;
+                o.x = v[4 * c4 + 0] + corr[4 * c4 + 0];
+                o.y = v[4 * c4 + 1] + corr[4 * c4 + 1];
+                o.z = v[4 * c4 + 2] + corr[4 * c4 + 2];
+                o.w = v[4 * c4 + 3] + corr[4 * c4 + 3];
+                *reinterpret_cast<float4 *>(stg + lane * 32 + 4 * (c4 ^ (lane & 7))) = o;
+            }
+            __syncwarp();
+            const int col = n0 + c0 + lane;
+            const bool cok = col < p.N;
+            const float bcol = (p.bias && cok) ? p.bias[col] : 0.0f;
+            // All 32 residual rows are requested before any is used.
+            float rv[32];
+            if (p.R) {
+#pragma unroll
+                for (int r = 0; r < 32; ++r)
+                    rv[r] = (rbase + r < p.M && cok) ? p.R[(size_t)(rbase + r) * p.ldr + col] : 0.0f;
+            }
+#pragma unroll
+            for (int r = 0; r < 32; ++r) {
+                const int grow = rbase + r;
+                float o = stg[r * 32 + 4 * ((lane >> 2) ^ (r & 7)) + (lane & 3)];
+                if (grow < p.M && cok) {
+                    if (p.bias) o = o + bcol;
+                    if (p.R) o = rv[r] + o;
+                    p.C[(size_t)grow * p.ldc + col] = o;
+                }
+            }
+            __syncwarp();
+        }
+        return;
+    }
+    // SwiGLU: 64-column blocks of (32 gate, 32 value) columns of the
+    // same 32 channels; both accumulator chains summed first.
+    for (int c0 = c_begin; p.swiglu_H && c0 < c_end; c0 += 64) {
+        if (n0 + c0 >= p.N) break;  // warp-uniform
+        const int j0 = (n0 + c0) >> 1;
+        const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+#pragma unroll
+        for (int sub = 0; sub < 32; sub += 16) {
+            float a[16], b[16], t[16];
+            tmem_ld16(ta + sub, a);
+            tmem_ld16(ta + BN + sub, t);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) a[jj] = a[jj] + t[jj];
+            tmem_ld16(ta + 32 + sub, b);
+            tmem_ld16(ta + BN + 32 + sub, t);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) b[jj] = b[jj] + t[jj];
+            if (row < p.M) {
+                const int j = j0 + sub;
+                float *out = p.C + (size_t)row * p.ldc + j;
+#pragma unroll
+                for (int jj = 0; jj < 16; jj += 4) {
+                    float4 sv;
+                    sv.x = silu(a[jj + 0] + p.bias[j + jj + 0]) * (b[jj + 0] + p.bias[p.swiglu_H + j + jj + 0]);
+                    sv.y = silu(a[jj + 1] + p.bias[j + jj + 1]) * (b[jj + 1] + p.bias[p.swiglu_H + j + jj + 1]);
+                    sv.z = silu(a[jj + 2] + p.bias[j + jj + 2]) * (b[jj + 2] + p.bias[p.swiglu_H + j + jj + 2]);
+                    sv.w = silu(a[jj + 3] + p.bias[j + jj + 3]) * (b[jj + 3] + p.bias[p.swiglu_H + j + jj + 3]);
+                    if (p.C_lo) {
+                        float4 h, l;
+                        h.x = tf32_round(sv.x); l.x = tf32_round(sv.x - h.x);
+                        h.y = tf32_round(sv.y); l.y = tf32_round(sv.y - h.y);
+                        h.z = tf32_round(sv.z); l.z = tf32_round(sv.z - h.z);
+                        h.w = tf32_round(sv.w); l.w = tf32_round(sv.w - h.w);
+                        *reinterpret_cast<float4 *>(out + jj) = h;
+                        *reinterpret_cast<float4 *>(p.C_lo + (size_t)row * p.ldc + j + jj) = l;
+                    } else {
+                        *reinterpret_cast<float4 *>(out + jj) = sv;
+                    }
+                }
+            }
+        }
+    }
+    for (int c0 = c_begin; !p.swiglu_H && c0 < c_end; c0 += 32) {
+        if (n0 + c0 >= p.N) break;  // warp-uniform
+        float v[32], corr[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = v[j] + corr[j];
+        const int nb = n0 + c0;
+        if (argmax_mode) {
+            // First strict maximum over this tile's columns, NaN skipped.
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                float o = v[j];
+                if (p.bias && nb + j < p.N) o = o + p.bias[nb + j];
+                if (nb + j < p.N && !isnan(o) && o > best) {
+                    best = o;
+                    best_n = (uint32_t)(nb + j);
+                }
+            }
+            continue;
+        }
+        if (row < p.M) {
+            float *crow = p.C + (size_t)row * p.ldc;
+            const float *rrow = p.R ? p.R + (size_t)row * p.ldr : nullptr;
+            if (vec && nb + 32 <= p.N) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    float4 o;
+                    o.x = v[j + 0]; o.y = v[j + 1]; o.z = v[j + 2]; o.w = v[j + 3];
+                    if (p.bias) {
+                        const float4 b = *reinterpret_cast<const float4 *>(p.bias + nb + j);
+                        o.x = o.x + b.x; o.y = o.y + b.y; o.z = o.z + b.z; o.w = o.w + b.w;
+                    }
+                    if (rrow) {
+                        const float4 r = *reinterpret_cast<const float4 *>(rrow + nb + j);
+                        o.x = r.x + o.x; o.y = r.y + o.y; o.z = r.z + o.z; o.w = r.w + o.w;
+                    }
+                    *reinterpret_cast<float4 *>(crow + nb + j) = o;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int n = nb + j;
+                    if (n < p.N) {
+                        float o = v[j];
+                        if (p.bias) o = o + p.bias[n];
+                        if (rrow) o = rrow[n] + o;
+                        crow[n] = o;
+                    }
+                }
+            }
+        }
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(THREADS, Tile<BN>::CTAS_PER_SM)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
@@ -218,7 +421,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned tile area (swizzle atoms must not straddle their period).
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES);  // full[S], empty[S], acc_full, acc_empty
+    // full[S], empty[S], acc_full, acc_empty after the stages and transpose buffers
+    uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + T::EPI_BYTES);
     uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 2);
     __shared__ int s_abort;
 
@@ -375,101 +579,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             const int row = m0 + q * 32 + lane;
             float best = -INFINITY;
             uint32_t best_n = 0xFFFFFFFFu;
-            // SwiGLU: 64-column blocks of (32 gate, 32 value) columns of the
-            // same 32 channels; both accumulator chains summed first.
-            for (int c0 = half * COLS; p.swiglu_H && c0 < (half + 1) * COLS; c0 += 64) {
-                if (n0 + c0 >= p.N) break;  // warp-uniform
-                const int j0 = (n0 + c0) >> 1;
-                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
-#pragma unroll
-                for (int sub = 0; sub < 32; sub += 16) {
-                    float a[16], b[16], t[16];
-                    tmem_ld16(ta + sub, a);
-                    tmem_ld16(ta + BN + sub, t);
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) a[jj] = a[jj] + t[jj];
-                    tmem_ld16(ta + 32 + sub, b);
-                    tmem_ld16(ta + BN + 32 + sub, t);
-#pragma unroll
-                    for (int jj = 0; jj < 16; ++jj) b[jj] = b[jj] + t[jj];
-                    if (row < p.M) {
-                        const int j = j0 + sub;
-                        float *out = p.C + (size_t)row * p.ldc + j;
-#pragma unroll
-                        for (int jj = 0; jj < 16; jj += 4) {
-                            float4 sv;
-                            sv.x = silu(a[jj + 0] + p.bias[j + jj + 0]) * (b[jj + 0] + p.bias[p.swiglu_H + j + jj + 0]);
-                            sv.y = silu(a[jj + 1] + p.bias[j + jj + 1]) * (b[jj + 1] + p.bias[p.swiglu_H + j + jj + 1]);
-                            sv.z = silu(a[jj + 2] + p.bias[j + jj + 2]) * (b[jj + 2] + p.bias[p.swiglu_H + j + jj + 2]);
-                            sv.w = silu(a[jj + 3] + p.bias[j + jj + 3]) * (b[jj + 3] + p.bias[p.swiglu_H + j + jj + 3]);
-                            if (p.C_lo) {
-                                float4 h, l;
-                                h.x = tf32_round(sv.x); l.x = tf32_round(sv.x - h.x);
-                                h.y = tf32_round(sv.y); l.y = tf32_round(sv.y - h.y);
-                                h.z = tf32_round(sv.z); l.z = tf32_round(sv.z - h.z);
-                                h.w = tf32_round(sv.w); l.w = tf32_round(sv.w - h.w);
-                                *reinterpret_cast<float4 *>(out + jj) = h;
-                                *reinterpret_cast<float4 *>(p.C_lo + (size_t)row * p.ldc + j + jj) = l;
-                            } else {
-                                *reinterpret_cast<float4 *>(out + jj) = sv;
-                            }
-                        }
-                    }
-                }
-            }
-            for (int c0 = half * COLS; !p.swiglu_H && c0 < (half + 1) * COLS; c0 += 32) {
-                if (n0 + c0 >= p.N) break;  // warp-uniform
-                float v[32], corr[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = v[j] + corr[j];
-                const int nb = n0 + c0;
-                if (argmax_mode) {
-                    // First strict maximum over this tile's columns, NaN skipped.
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        float o = v[j];
-                        if (p.bias && nb + j < p.N) o = o + p.bias[nb + j];
-                        if (nb + j < p.N && !isnan(o) && o > best) {
-                            best = o;
-                            best_n = (uint32_t)(nb + j);
-                        }
-                    }
-                    continue;
-                }
-                if (row < p.M) {
-                    float *crow = p.C + (size_t)row * p.ldc;
-                    const float *rrow = p.R ? p.R + (size_t)row * p.ldr : nullptr;
-                    if (vec && nb + 32 <= p.N) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 o;
-                            o.x = v[j + 0]; o.y = v[j + 1]; o.z = v[j + 2]; o.w = v[j + 3];
-                            if (p.bias) {
-                                const float4 b = *reinterpret_cast<const float4 *>(p.bias + nb + j);
-                                o.x = o.x + b.x; o.y = o.y + b.y; o.z = o.z + b.z; o.w = o.w + b.w;
-                            }
-                            if (rrow) {
-                                const float4 r = *reinterpret_cast<const float4 *>(rrow + nb + j);
-                                o.x = r.x + o.x; o.y = r.y + o.y; o.z = r.z + o.z; o.w = r.w + o.w;
-                            }
-                            *reinterpret_cast<float4 *>(crow + nb + j) = o;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int n = nb + j;
-                            if (n < p.N) {
-                                float o = v[j];
-                                if (p.bias) o = o + p.bias[n];
-                                if (rrow) o = rrow[n] + o;
-                                crow[n] = o;
-                            }
-                        }
-                    }
-                }
-            }
+            float *stg =
+                BN == 256 ? reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES) + (warp - 4) * 1024 : nullptr;
+            epilogue_cols<BN>(p, tmem, q, lane, m0, n0, half * COLS, (half + 1) * COLS, argmax_mode, vec, best, best_n,
+                              stg);
             // TMEM of this tile fully read: hand the accumulators back.
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -491,6 +604,248 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair kernel (tcgen05 cta_group::2): a cluster of two CTAs on two SMs
+// computes a 256 x 256 tile.  CTA r (rank in the pair) loads A rows
+// [128 r, 128 r + 128) and W rows [128 r, 128 r + 128) of the tile, so each
+// SM stages 32 KiB per K-block instead of 48 KiB and its tensor core reads
+// half of W from its own shared memory; the leader (rank 0) issues
+// tcgen05.mma.cta_group::2 (M = 256, N = 256) and each CTA's TMEM receives
+// its own 128 rows x 256 columns.  Both CTAs' tensor copies (each into its
+// own shared memory, from this GPU's memory only) complete on the leader's
+// full barrier; the leader's tcgen05.commit arrives on both CTAs' empty and
+// acc_full barriers; both CTAs' epilogue warps arrive on the leader's
+// acc_empty barrier.
+constexpr int P_STAGES = 6;
+constexpr int P_HALF_BYTES = 128 * BK * 4;              // 8 KiB: 128 rows x one K-block
+constexpr int P_STAGE_BYTES = 4 * P_HALF_BYTES;         // A_hi, A_lo, W_hi, W_lo halves
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr uint32_t P_TMEM_COLS = 512;
+// D f32, A/B tf32, both K-major, M = 256 (the pair), N = 256.
+constexpr uint32_t P_IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(256 >> 3) << 17) |
+                             ((uint32_t)(256 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared-memory offset in the pair's rank-0 CTA.
+__device__ __forceinline__ uint32_t at_rank0(uint32_t addr) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(addr));
+    return r;
+}
+
+__device__ __forceinline__ void pair_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, uint32_t bar_rank0, int x,
+                                                 int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"((uint64_t)map), "r"(bar_rank0), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p; }"
+        ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// Arrive on the barrier at this offset in both CTAs of the pair once every
+// MMA issued so far has completed.
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        ::"r"(bar), "h"((unsigned short)3)
+        : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+tc_pair_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
+               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(smem + P_STAGES * P_STAGE_BYTES);  // full[S], empty[S], acc_full, acc_empty
+    uint32_t *tmem_slot = (uint32_t *)(bars + 2 * P_STAGES + 2);
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const int n_tiles_n = (p.N + 255) / 256;
+    const int n_tiles = n_tiles_n * ((p.M + 255) / 256);
+    const int kblocks = (p.K + BK - 1) / BK;
+
+    const uint32_t bar_full0 = smem_u32(&bars[0]);
+    const uint32_t bar_empty0 = smem_u32(&bars[P_STAGES]);
+    const uint32_t bar_acc_full = smem_u32(&bars[2 * P_STAGES]);
+    const uint32_t bar_acc_empty = smem_u32(&bars[2 * P_STAGES + 1]);
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(bar_full0 + 8 * s, 1);
+            mbar_init(bar_empty0 + 8 * s, 1);
+        }
+        mbar_init(bar_acc_full, 1);
+        mbar_init(bar_acc_empty, 2 * EPI_WARPS);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAh) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAl) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBh) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBl) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(P_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    pair_sync();  // both CTAs' barriers initialised before any cross-CTA signal
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer (both CTAs): this CTA's halves, completing on the
+        // leader's full barrier; the leader also arms it with both halves' bytes.
+        int stage = 0;
+        uint32_t phase = 0;
+        int issued = 0;
+        const uint32_t full0_r0 = at_rank0(bar_full0);
+        for (int t = pair; t < n_tiles && !*(volatile int *)&s_abort; t += n_pairs) {
+            const int m0 = (t / n_tiles_n) * 256 + (int)rank * 128;
+            const int nb = (t % n_tiles_n) * 256 + (int)rank * 128;
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
+                    atomicExch(p.err, 105);
+                    s_abort = 1;
+                    break;
+                }
+                if (*(volatile int *)&s_abort) break;
+                uint8_t *st = smem + stage * P_STAGE_BYTES;
+                if (rank == 0) mbar_expect_tx(bar_full0 + 8 * stage, 2 * P_STAGE_BYTES);
+                const uint32_t full = full0_r0 + 8 * stage;
+                const int kx = kb * BK;
+                tma_load_2d_pair(smem_u32(st), &mapAh, full, kx, m0);
+                tma_load_2d_pair(smem_u32(st + P_HALF_BYTES), &mapAl, full, kx, m0);
+                tma_load_2d_pair(smem_u32(st + 2 * P_HALF_BYTES), &mapBh, full, kx, nb);
+                tma_load_2d_pair(smem_u32(st + 3 * P_HALF_BYTES), &mapBl, full, kx, nb);
+                ++issued;
+                if (++stage == P_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+        }
+        // Drain: a stage's copies have landed once the leader's MMAs have
+        // consumed it, which its empty barrier records; wait (bounded) for the
+        // last issued stages so no copy still writes this CTA's shared memory
+        // when it exits.
+        {
+            int s2 = 0;
+            uint32_t ph2 = 0;
+            for (int i = 0; i < issued; ++i) {
+                if (i >= issued - P_STAGES) mbar_wait(bar_empty0 + 8 * s2, ph2);
+                if (++s2 == P_STAGES) {
+                    s2 = 0;
+                    ph2 ^= 1;
+                }
+            }
+        }
+    } else if (warp == 1 && lane == 0 && rank == 0) {
+        // ---- MMA issuer (leader only)
+        int stage = 0;
+        uint32_t phase = 0;
+        int i = 0;
+        for (int t = pair; t < n_tiles; t += n_pairs, ++i) {
+            if (!mbar_wait(bar_acc_empty, (uint32_t)((i & 1) ^ 1)) || *(volatile int *)&s_abort) {
+                atomicExch(p.err, 108);
+                s_abort = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            bool ok = true;
+            for (int kb = 0; kb < kblocks; ++kb) {
+                if (!mbar_wait(bar_full0 + 8 * stage, phase) || *(volatile int *)&s_abort) {
+                    atomicExch(p.err, 106);
+                    s_abort = 1;
+                    ok = false;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t base = smem_u32(smem + stage * P_STAGE_BYTES);
+                const uint64_t dAh = smem_desc(base), dAl = smem_desc(base + P_HALF_BYTES);
+                const uint64_t dBh = smem_desc(base + 2 * P_HALF_BYTES), dBl = smem_desc(base + 3 * P_HALF_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < BK / 8; ++kk) {
+                    const uint64_t off = (uint64_t)((kk * 32) >> 4);
+                    const uint32_t acc = (kb | kk) ? 1u : 0u;
+                    mma_tf32_pair(tmem, dAh + off, dBh + off, P_IDESC, acc);
+                    mma_tf32_pair(tmem + 256, dAh + off, dBl + off, P_IDESC, acc);
+                    mma_tf32_pair(tmem + 256, dAl + off, dBh + off, P_IDESC, 1u);
+                }
+                mma_commit_pair(bar_empty0 + 8 * stage);
+                if (++stage == P_STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            }
+            mma_commit_pair(bar_acc_full);
+            if (!ok) break;
+        }
+    } else if (warp >= 4) {
+        // ---- epilogue (both CTAs): this CTA's 128 rows x 256 columns
+        const int q = warp & 3;
+        const int half = (warp - 4) >> 2;
+        const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
+        const bool argmax_mode = p.best_val != nullptr;
+        const uint32_t acc_empty_r0 = at_rank0(bar_acc_empty);
+        int i = 0;
+        for (int t = pair; t < n_tiles; t += n_pairs, ++i) {
+            const int m0 = (t / n_tiles_n) * 256 + (int)rank * 128;
+            const int tn = t % n_tiles_n;
+            const int n0 = tn * 256;
+            const bool ok = mbar_wait(bar_acc_full, (uint32_t)(i & 1)) && !*(volatile int *)&s_abort;
+            __syncwarp();
+            if (!ok) {
+                if (lane == 0) atomicExch(p.err, 107);
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const int row = m0 + q * 32 + lane;
+            float best = -INFINITY;
+            uint32_t best_n = 0xFFFFFFFFu;
+            epilogue_cols<256>(p, tmem, q, lane, m0, n0, half * 128, half * 128 + 128, argmax_mode, vec, best,
+                               best_n, nullptr);
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0)
+                asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(acc_empty_r0)
+                             : "memory");
+            if (argmax_mode && row < p.M) {
+                const size_t slot = (size_t)row * p.n_tiles + 2 * tn + half;
+                p.best_val[slot] = best;
+                p.best_idx[slot] = best_n;
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    pair_sync();  // the peer is done with this CTA's barriers and TMEM
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P_TMEM_COLS) : "memory");
     }
 }
 
@@ -557,8 +912,9 @@ bool tc_eligible(int M, int N, int K) {
     return M >= BM && N >= 128 && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
 }
 
+// The CTA-pair kernel while it fills every SM pair at least twice, else
 // BN = 256 while the grid still fills every SM twice over, else 128.
-int tc_pick_bn(int M, int N) {
+int tc_pick_bn(int M, int N, bool allow_pair) {
     static int num_sms = 0;
     if (!num_sms) {
         int dev = 0;
@@ -567,10 +923,15 @@ int tc_pick_bn(int M, int N) {
         if (num_sms <= 0) num_sms = 148;
     }
     const long tiles256 = (long)((N + 255) / 256) * ((M + BM - 1) / BM);
+    const long pair_tiles = (long)((N + 255) / 256) * ((M + 255) / 256);
+    if (allow_pair && N >= 256 && pair_tiles >= 2L * (num_sms / 2)) return TC_PAIR;
     return (N >= 256 && tiles256 >= 2L * num_sms) ? 256 : 128;
 }
 
-int tc_tiles_n(int N, int bn) { return (N + bn - 1) / bn; }
+int tc_tiles_n(int N, int bn) {
+    const int w = bn == TC_PAIR ? 256 : bn;
+    return (N + w - 1) / w;
+}
 int tc_argmax_parts(int N, int bn) { return 2 * tc_tiles_n(N, bn); }
 
 cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
@@ -656,9 +1017,33 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
     return cudaGetLastError();
 }
 
+cudaError_t launch_pair(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, TcArgs a, int M,
+                        cudaStream_t st) {
+    static thread_local int attr_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (attr_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        attr_dev = dev;
+    }
+    static int num_sms = 0;
+    if (!num_sms) {
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (num_sms <= 0) num_sms = 148;
+    }
+    // Persistent pairs: each cluster of two CTAs walks 256 x 256 tiles.
+    const long tiles = (long)((W.N + 255) / 256) * ((M + 255) / 256);
+    const unsigned pairs = (unsigned)std::max<long>(1, std::min<long>(tiles, num_sms / 2));
+    a.full_units = (int)tiles;
+    tc_pair_kernel<<<2 * pairs, THREADS, P_SMEM_BYTES, st>>>(mAh, mAl, *(const CUtensorMap *)W.map_hi128,
+                                                             *(const CUtensorMap *)W.map_lo128, a);
+    return cudaGetLastError();
+}
+
 cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
                     int bn, cudaStream_t st, int *err) {
-    if (W.K != K || M <= 0 || (bn != 128 && bn != 256)) return cudaErrorInvalidValue;
+    if (W.K != K || M <= 0 || (bn != 128 && bn != 256 && bn != TC_PAIR)) return cudaErrorInvalidValue;
     // SwiGLU mode and the interleaved operand go together; argmax never with it.
     if (ep.swiglu != (W.pair_half > 0) || (ep.swiglu && (ep.best_val || !ep.bias))) return cudaErrorInvalidValue;
     // Tiles read A rows while other tiles' epilogues write: no output may
@@ -675,6 +1060,7 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
     TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err,
               ep.swiglu ? W.pair_half : 0, ep.C_lo, 0};
+    if (bn == TC_PAIR) return launch_pair(mAh, mAl, W, a, M, st);
     return bn == 256 ? launch_tc<256>(mAh, mAl, W, a, M, st) : launch_tc<128>(mAh, mAl, W, a, M, st);
 }
 

@@ -21,7 +21,8 @@ def _ids(S, T, V, base):
     return uniform_prompts(S, T, V, base)
 
 
-@pytest.mark.parametrize("tile_bits", [16, 32])  # tensor-core tiles 128 / 256 columns wide
+# tensor-core tiles 128 / 256 columns wide on one SM; 256 x 256 on a CTA pair
+@pytest.mark.parametrize("tile_bits", [16, 32, 128])
 def test_tensor_core_engine_matches_f32_engine(gpu, orc, tile_bits):
     om, gm = same_model(orc, gpu, WIDE, seed=1)
     S, T = 384, 4
@@ -98,7 +99,8 @@ def test_headline_model_stream_subset(gpu, orc):
             assert state_rel_err(st[s, layer, k * E:], ost[layer, k * E:]) <= 1e-4, (s, layer)
 
 
-def test_fused_argmax_epilogue_matches_materialised_logits(gpu, orc):
+@pytest.mark.parametrize("engine", [0, 128])  # default tiles / the CTA-pair kernel
+def test_fused_argmax_epilogue_matches_materialised_logits(gpu, orc, engine):
     """Greedy steps through the logits projection's argmax epilogue (no
     logits stored) pick the same tokens as argmax over stored logits, except
     where the two best logits are within 1e-4."""
@@ -106,6 +108,7 @@ def test_fused_argmax_epilogue_matches_materialised_logits(gpu, orc):
     S = 256
     ids = _ids(S, 3, WIDE["vocab"], 31)
     fused, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    fused.set_engine(engine)
     for t in range(3):
         tok = fused.step_greedy(ids[:, t])
         lg = plain.step(ids[:, t])
@@ -143,16 +146,19 @@ def test_hidden_width_off_the_interleave_grid(gpu, orc):
     assert np.abs(a[7] - ref).max() <= 1e-3
 
 
-def test_last_wave_half_width_units(gpu, orc):
-    """16384 streams of a d=1024 model: out_proj and down_proj have 512
-    tiles of 128 x 256 on 148 SMs, so the last 68 tiles run as 136
-    half-width units (in_proj: 56 -> 112); every stream, the last rows and
-    columns included, equals the f32 engine."""
+@pytest.mark.parametrize("engine", [0, 128])
+def test_large_batch_tilings(gpu, orc, engine):
+    """16384 streams of a d=1024 model.  Engine 0: out_proj and down_proj
+    have 512 tiles of 128 x 256 on 148 SMs, so the last 68 tiles run as 136
+    half-width units (in_proj: 56 -> 112).  Engine 128: every projection
+    runs on the CTA-pair kernel (256 x 256 tiles).  Every stream, the last
+    rows and columns included, equals the f32 engine."""
     kw = dict(vocab=2048, d_model=1024, n_layer=1, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
     om, gm = same_model(orc, gpu, kw, seed=8)
     S = 16384
     ids = _ids(S, 2, kw["vocab"], 900)
     tc, f32 = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    tc.set_engine(engine)
     f32.set_engine(1)
     for t in range(2):
         a = tc.step(ids[:, t]).copy()
