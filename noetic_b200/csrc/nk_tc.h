@@ -56,6 +56,12 @@ struct TcEpilogue {
     // operand pair hi = tf32(s) into C, lo = tf32(s - hi) into C_lo.
     bool swiglu = false;
     float *C_lo = nullptr;
+    // Split-K workspace (store mode with 256-wide tiles covering less than
+    // one wave): partial tiles and per-tile counters, zero between launches.
+    float *ws = nullptr;
+    size_t ws_floats = 0;
+    int *flags = nullptr;
+    int n_flags = 0;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.
@@ -68,6 +74,10 @@ bool tc_eligible(int M, int N, int K);
 constexpr int TC_PAIR = 2;
 int tc_pick_bn(int M, int N, bool allow_pair = false);
 int tc_tiles_n(int N, int bn);
+// K splits the 256-wide store kernel uses for an M x N x K projection (1: none).
+int tc_ksplit(int M, int N, int K, int bn);
+// Split-K workspace a caller provides to cover any projection on this GPU.
+size_t tc_ksplit_ws_floats();
 // Argmax partials per row: one per half tile (each epilogue warpgroup owns half the columns).
 int tc_argmax_parts(int N, int bn);
 

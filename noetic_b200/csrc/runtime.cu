@@ -445,6 +445,10 @@ struct nk_decoder {
     // one per (tokens in, tokens out) device buffer pair
     std::vector<nk::SmallLayer> small_layers;
     // persistent step kernel: device copy of the layer pointers, barrier words
+    // split-K workspace of the tensor-core projections (counters zeroed)
+    float *ksplit_ws = nullptr;
+    int *ksplit_flags = nullptr;
+    static constexpr int KSPLIT_FLAGS = 4096;
     nk::SmallLayer *layers_dev = nullptr;
     const float *layers_arena = nullptr;  // model arena the layer tables point into
     uint32_t *sync = nullptr;
@@ -478,7 +482,7 @@ struct nk_decoder {
                         (void *)p_lens})
             if (p) cudaFree(p);
         for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo,
-                        (void *)layers_dev, (void *)sync})
+                        (void *)layers_dev, (void *)sync, (void *)ksplit_ws, (void *)ksplit_flags})
             if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         for (auto &gph : graphs) cudaGraphExecDestroy(gph.exec);
@@ -560,6 +564,10 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         ep.bias = bias;
         ep.R = R;
         ep.ldr = N;
+        ep.ws = dec->ksplit_ws;
+        ep.ws_floats = nk::tc_ksplit_ws_floats();
+        ep.flags = dec->ksplit_flags;
+        ep.n_flags = nk_decoder::KSPLIT_FLAGS;
         cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, N), dec->stream, dec->err),
                    "tcgen05 projection");
         dec->launches += 1;
@@ -673,8 +681,8 @@ void check_err_flag(nk_decoder *dec) {
         cuda_check(cudaMemsetAsync(dec->err, 0, sizeof(int), dec->stream), "clear error flag");
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
-                                ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 111-113 persistent "
-                                "step wait expired)");
+                                ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 105-108 CTA-pair pipeline wait expired, 111-113 "
+                                "persistent step wait expired, 121-123 split-K hand-off wait expired)");
     }
 }
 
@@ -1173,6 +1181,9 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         dalloc(&dec->tok_b, S, "tokens");
         dalloc(&dec->err, 1, "error flag");
         dalloc(&dec->sync, 2, "barrier words");
+        dalloc(&dec->ksplit_ws, nk::tc_ksplit_ws_floats(), "split-K workspace");
+        dalloc(&dec->ksplit_flags, nk_decoder::KSPLIT_FLAGS, "split-K counters");
+        cuda_check(cudaMemset(dec->ksplit_flags, 0, nk_decoder::KSPLIT_FLAGS * sizeof(int)), "memset");
         dalloc(&dec->layers_dev, model->cfg.n_layer, "layer table");
         dalloc(&dec->rng, S * 4, "rng");
         cuda_check(cudaMemset(dec->err, 0, sizeof(int)), "memset");

@@ -96,25 +96,51 @@ struct TcArgs {
     // partial wave of the grid) runs as two units of width BN / 2, so that
     // wave takes half as long.
     int full_units;
+    // Split-K (BN = 256 store mode, ksplit > 1): every tile runs as ksplit
+    // units over consecutive K ranges.  Units 1.. write their partial tile to
+    // ws and count it in flags[tile]; unit 0 waits for them and adds them in
+    // order.  All partial units come before every unit 0 in the unit order.
+    int ksplit;
+    float *ws;
+    int *flags;
 };
 
-// Work unit u of the tile loop: output rows m0.., columns n0.. of `width`.
+// Work unit u of the tile loop: output rows m0.., columns n0.. of `width`,
+// K-blocks [kb0, kb1); ks = split index (0 finishes the tile).
 struct Unit {
-    int m0, n0, tn, width;
+    int m0, n0, tn, width, t, ks, kb0, kb1;
 };
 
 template <int BN>
-__device__ __forceinline__ Unit unit_of(int u, int full_units, int n_tiles_n) {
-    int t = u, hs = -1;
-    if (BN == 256 && u >= full_units) {
-        t = full_units + ((u - full_units) >> 1);
-        hs = (u - full_units) & 1;
+__device__ __forceinline__ Unit unit_of(int u, const TcArgs &p, int n_tiles_n, int n_tiles, int kblocks) {
+    int t = u, hs = -1, ks = 0;
+    if (BN == 256 && p.ksplit > 1) {
+        const int parts = n_tiles * (p.ksplit - 1);
+        if (u < parts) {
+            ks = 1 + u / n_tiles;
+            t = u - (ks - 1) * n_tiles;
+        } else {
+            t = u - parts;
+        }
+    } else if (BN == 256 && u >= p.full_units) {
+        t = p.full_units + ((u - p.full_units) >> 1);
+        hs = (u - p.full_units) & 1;
     }
     Unit x;
+    x.t = t;
+    x.ks = ks;
     x.m0 = (t / n_tiles_n) * BM;
     x.tn = t % n_tiles_n;
     x.n0 = x.tn * BN + (hs > 0 ? BN / 2 : 0);
     x.width = hs < 0 ? BN : BN / 2;
+    if (BN == 256 && p.ksplit > 1) {
+        const int per = (kblocks + p.ksplit - 1) / p.ksplit;
+        x.kb0 = ks * per;
+        x.kb1 = min(kblocks, x.kb0 + per);
+    } else {
+        x.kb0 = 0;
+        x.kb1 = kblocks;
+    }
     return x;
 }
 
@@ -212,10 +238,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // rows m0 + q*32 + lane), TMEM columns [c_begin, c_end) (output columns
 // n0 + c).  Store mode writes C (+bias, +residual); SwiGLU mode writes the
 // gated product; argmax mode folds the columns into (best, best_n).
+// With split-K (stg only): part_out != null writes this unit's partial tile
+// ([BM][BN], no bias / residual) instead of C; parts != null adds the
+// ksplit - 1 partial tiles at parts, parts + BM*BN, ... in order before the
+// bias and residual.
 template <int BN>
 __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, int q, int lane, int m0, int n0,
                                               int c_begin, int c_end, bool argmax_mode, bool vec, float &best,
-                                              uint32_t &best_n, float *stg) {
+                                              uint32_t &best_n, float *stg, const float *parts = nullptr,
+                                              float *part_out = nullptr) {
     const int row = m0 + q * 32 + lane;
     if (stg && !argmax_mode) {
         // Transpose each 32 x 32 chunk through this warp's shared buffer
@@ -289,6 +320,26 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
             __syncwarp();
             const int col = n0 + c0 + lane;
             const bool cok = col < p.N;
+            if (part_out) {
+#pragma unroll 8
+                for (int r = 0; r < 32; ++r)
+                    part_out[(size_t)(q * 32 + r) * BN + c0 + lane] = stg[r * 32 + 4 * ((lane >> 2) ^ (r & 7)) + (lane & 3)];
+                __syncwarp();
+                continue;
+            }
+            if (parts) {
+                for (int ks = 1; ks < p.ksplit; ++ks) {
+                    const float *pt = parts + (size_t)(ks - 1) * BM * BN + (size_t)(q * 32) * BN + c0 + lane;
+                    float pv[32];
+#pragma unroll
+                    for (int r = 0; r < 32; ++r) pv[r] = pt[(size_t)r * BN];
+#pragma unroll
+                    for (int r = 0; r < 32; ++r) {
+                        float *sp = stg + r * 32 + 4 * ((lane >> 2) ^ (r & 7)) + (lane & 3);
+                        *sp = *sp + pv[r];
+                    }
+                }
+            }
             const float bcol = (p.bias && cok) ? p.bias[col] : 0.0f;
             // All 32 residual rows are requested before any is used.
             float rv[32];
@@ -425,11 +476,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + T::EPI_BYTES);
     uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 2);
     __shared__ int s_abort;
+    __shared__ int s_epi_cnt, s_go;  // split-K hand-offs among the epilogue warps
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles_n = (p.N + BN - 1) / BN;
     const int n_tiles = n_tiles_n * ((p.M + BM - 1) / BM);
-    const int n_units = p.full_units + 2 * (n_tiles - p.full_units);
+    const int n_units =
+        (BN == 256 && p.ksplit > 1) ? n_tiles * p.ksplit : p.full_units + 2 * (n_tiles - p.full_units);
     const int kblocks = (p.K + BK - 1) / BK;
 
     const uint32_t bar_full0 = smem_u32(&bars[0]);
@@ -439,6 +492,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
 
     if (threadIdx.x == 0) {
         s_abort = 0;
+        s_epi_cnt = 0;
+        s_go = 0;
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(bar_full0 + 8 * s, 1);
             mbar_init(bar_empty0 + 8 * s, 1);
@@ -473,11 +528,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         uint32_t phase = 0;
         int issued = 0;
         for (int u = blockIdx.x; u < n_units && !*(volatile int *)&s_abort; u += gridDim.x) {
-            const Unit un = unit_of<BN>(u, p.full_units, n_tiles_n);
+            const Unit un = unit_of<BN>(u, p, n_tiles_n, n_tiles, kblocks);
             const bool wide = un.width == BN;
             const CUtensorMap *mBh = wide ? &mapBh : &mapBh2, *mBl = wide ? &mapBl : &mapBl2;
             const uint32_t bytes = wide ? STAGE_BYTES : 2 * A_BYTES + B_BYTES;
-            for (int kb = 0; kb < kblocks; ++kb) {
+            for (int kb = un.kb0; kb < un.kb1; ++kb) {
                 if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
                     atomicExch(p.err, 101);
                     s_abort = 1;
@@ -518,7 +573,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         uint32_t phase = 0;
         int i = 0;
         for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
-            const uint32_t idesc = (BN != 256 || u < p.full_units) ? IDESC : IDESC_HALF;
+            const Unit un = unit_of<BN>(u, p, n_tiles_n, n_tiles, kblocks);
+            const uint32_t idesc = un.width == BN ? IDESC : IDESC_HALF;
             // The accumulators are free once the epilogue drained tile i - 1.
             if (!mbar_wait(bar_acc_empty, (uint32_t)((i & 1) ^ 1)) || *(volatile int *)&s_abort) {
                 atomicExch(p.err, 104);
@@ -527,7 +583,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             bool ok = true;
-            for (int kb = 0; kb < kblocks; ++kb) {
+            for (int kb = un.kb0; kb < un.kb1; ++kb) {
                 if (!mbar_wait(bar_full0 + 8 * stage, phase) || *(volatile int *)&s_abort) {
                     atomicExch(p.err, 102);
                     s_abort = 1;
@@ -541,7 +597,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
                     const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
-                    const uint32_t acc = (kb | kk) ? 1u : 0u;
+                    const uint32_t acc = (kb != un.kb0 || kk) ? 1u : 0u;
                     mma_tf32(tmem, dAh + off, dBh + off, idesc, acc);
                     mma_tf32(tmem + BN, dAh + off, dBl + off, idesc, acc);
                     mma_tf32(tmem + BN, dAl + off, dBh + off, idesc, 1u);
@@ -564,9 +620,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         const int half = (warp - 4) >> 2;
         const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
         const bool argmax_mode = p.best_val != nullptr;
-        int i = 0;
+        const bool split = BN == 256 && p.ksplit > 1;
+        int i = 0, n_part = 0, n_fin = 0;
         for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
-            const Unit un = unit_of<BN>(u, p.full_units, n_tiles_n);
+            const Unit un = unit_of<BN>(u, p, n_tiles_n, n_tiles, kblocks);
             const int m0 = un.m0, n0 = un.n0;
             const int COLS = un.width / 2;  // columns of this warpgroup
             const bool ok = mbar_wait(bar_acc_full, (uint32_t)(i & 1)) && !*(volatile int *)&s_abort;
@@ -576,17 +633,74 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 break;
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const float *parts = nullptr;
+            float *part_out = nullptr;
+            if (split) {
+                const size_t tile_floats = (size_t)BM * BN;
+                if (un.ks > 0) {
+                    part_out = p.ws + ((size_t)un.t * (p.ksplit - 1) + (un.ks - 1)) * tile_floats;
+                } else {
+                    // The tile's other K ranges: wait (bounded) until all are
+                    // published, then every epilogue warp reads them.
+                    parts = p.ws + (size_t)un.t * (p.ksplit - 1) * tile_floats;
+                    ++n_fin;
+                    if (warp == 4 && lane == 0) {
+                        const uint64_t t0 = globaltimer();
+                        for (;;) {
+                            int v;
+                            asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p.flags + un.t) : "memory");
+                            if (v >= p.ksplit - 1) break;
+                            if (globaltimer() - t0 > WAIT_NS) {
+                                atomicExch(p.err, 121);
+                                break;
+                            }
+                        }
+                        p.flags[un.t] = 0;  // ready for the next launch
+                        __threadfence_block();
+                        *(volatile int *)&s_go = n_fin;
+                    }
+                    if (lane == 0) {
+                        const uint64_t t0 = globaltimer();
+                        while (*(volatile int *)&s_go < n_fin)
+                            if (globaltimer() - t0 > WAIT_NS) {
+                                atomicExch(p.err, 122);
+                                break;
+                            }
+                        __threadfence();
+                    }
+                    __syncwarp();
+                }
+            }
             const int row = m0 + q * 32 + lane;
             float best = -INFINITY;
             uint32_t best_n = 0xFFFFFFFFu;
             float *stg =
                 BN == 256 ? reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES) + (warp - 4) * 1024 : nullptr;
             epilogue_cols<BN>(p, tmem, q, lane, m0, n0, half * COLS, (half + 1) * COLS, argmax_mode, vec, best, best_n,
-                              stg);
+                              stg, parts, part_out);
             // TMEM of this tile fully read: hand the accumulators back.
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_acc_empty) : "memory");
+            if (part_out) {
+                // Publish the partial once all eight epilogue warps wrote theirs.
+                ++n_part;
+                if (lane == 0) {
+                    __threadfence();
+                    atomicAdd(&s_epi_cnt, 1);
+                }
+                if (warp == 4 && lane == 0) {
+                    const uint64_t t0 = globaltimer();
+                    while (*(volatile int *)&s_epi_cnt < EPI_WARPS * n_part)
+                        if (globaltimer() - t0 > WAIT_NS) {
+                            atomicExch(p.err, 123);
+                            break;
+                        }
+                    __threadfence();
+                    atomicAdd(p.flags + un.t, 1);
+                }
+                __syncwarp();
+            }
             if (argmax_mode && row < p.M) {
                 // Each warpgroup holds the first maximum of its half of the
                 // tile's columns: partial 2*tile_n + half, so partial order is
@@ -912,6 +1026,30 @@ bool tc_eligible(int M, int N, int K) {
     return M >= BM && N >= 128 && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
 }
 
+int sm_count_cached() {
+    static int num_sms = 0;
+    if (!num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (num_sms <= 0) num_sms = 148;
+    }
+    return num_sms;
+}
+
+// K splits for a 128 x 256-tile store projection whose tiles cover less
+// than one wave: as many as fit the SMs, each at least 4 K-blocks, at most 8.
+int tc_ksplit(int M, int N, int K, int bn) {
+    if (bn != 256) return 1;
+    const long tiles = (long)((N + 255) / 256) * ((M + BM - 1) / BM);
+    const int sms = sm_count_cached();
+    if (tiles <= 0 || tiles >= sms) return 1;
+    const int kblocks = (K + BK - 1) / BK;
+    int ks = (int)std::min<long>(sms / tiles, 8);
+    ks = std::min(ks, kblocks / 4);
+    return ks >= 2 ? ks : 1;
+}
+
 // The CTA-pair kernel while it fills every SM pair at least twice, else
 // BN = 256 while the grid still fills every SM twice over, else 128.
 int tc_pick_bn(int M, int N, bool allow_pair) {
@@ -925,8 +1063,28 @@ int tc_pick_bn(int M, int N, bool allow_pair) {
     const long tiles256 = (long)((N + 255) / 256) * ((M + BM - 1) / BM);
     const long pair_tiles = (long)((N + 255) / 256) * ((M + 255) / 256);
     if (allow_pair && N >= 256 && pair_tiles >= 2L * (num_sms / 2)) return TC_PAIR;
-    return (N >= 256 && tiles256 >= 2L * num_sms) ? 256 : 128;
+    if (N < 256) return 128;
+    // Compare the fraction of SM time each width keeps busy.  A 128-wide
+    // tile moves 4/3 the operand bytes per flop of a 256-wide one (the main
+    // loop is bound by operand bandwidth into shared memory), so it counts
+    // 3/4.  256-wide: a partial last wave of at most half the SMs runs as
+    // half-width units, and fewer tiles than SMs are split along K.
+    double e256;
+    if (tiles256 < num_sms) {
+        const int ks = tc_ksplit(M, N, 1 << 20, 256);
+        e256 = (double)(tiles256 * ks) / num_sms;
+    } else {
+        const long rem = tiles256 % num_sms;
+        const double waves = (double)(tiles256 / num_sms) + (rem == 0 ? 0.0 : (2 * rem <= num_sms ? 0.5 : 1.0));
+        e256 = (double)tiles256 / (waves * num_sms);
+    }
+    const long tiles128 = (long)((N + 127) / 128) * ((M + BM - 1) / BM);
+    const long slots128 = 2L * num_sms;
+    const double e128 = 0.75 * (double)tiles128 / ((double)((tiles128 + slots128 - 1) / slots128) * slots128);
+    return e256 >= e128 ? 256 : 128;
 }
+
+size_t tc_ksplit_ws_floats() { return (size_t)sm_count_cached() * BM * 256; }
 
 int tc_tiles_n(int N, int bn) {
     const int w = bn == TC_PAIR ? 256 : bn;
@@ -1006,11 +1164,19 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
     }
     const long tiles = (long)tc_tiles_n(W.N, BN) * ((M + BM - 1) / BM);
     const long slots = (long)num_sms * Tile<BN>::CTAS_PER_SM;
-    const unsigned grid = (unsigned)std::min<long>(tiles, slots);
+    unsigned grid = (unsigned)std::min<long>(tiles, slots);
     // A last wave that covers at most half the grid runs as half-width units
     // (full-width tiles only for the argmax epilogue's partial layout).
     const long rem = tiles % (long)grid;
     a.full_units = (int)((BN == 256 && !a.best_val && rem > 0 && 2 * rem <= (long)grid) ? tiles - rem : tiles);
+    // Fewer tiles than SMs: split K so that the units fill the grid.
+    a.ksplit = 1;
+    const int ks = tc_ksplit(M, W.N, W.K, BN);
+    if (BN == 256 && ks > 1 && !a.best_val && !a.swiglu_H && a.ws && a.flags) {
+        a.ksplit = ks;
+        a.full_units = (int)tiles;
+        grid = (unsigned)std::min<long>(tiles * ks, slots);
+    }
     tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(
         mAh, mAl, *(const CUtensorMap *)mh, *(const CUtensorMap *)ml, *(const CUtensorMap *)W.map_hi128,
         *(const CUtensorMap *)W.map_lo128, a);
@@ -1059,7 +1225,16 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     alignas(64) CUtensorMap mAh, mAl;
     if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
     TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err,
-              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0};
+              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 1, ep.ws, ep.flags};
+    if (a.ws) {
+        // Split-K only when the workspace and flags cover every tile.
+        const long tiles = (long)tc_tiles_n(W.N, 256) * ((M + BM - 1) / BM);
+        const int ks = tc_ksplit(M, W.N, K, 256);
+        if (ks < 2 || tiles > ep.n_flags || (size_t)tiles * (ks - 1) * BM * 256 > ep.ws_floats) {
+            a.ws = nullptr;
+            a.flags = nullptr;
+        }
+    }
     if (bn == TC_PAIR) return launch_pair(mAh, mAl, W, a, M, st);
     return bn == 256 ? launch_tc<256>(mAh, mAl, W, a, M, st) : launch_tc<128>(mAh, mAl, W, a, M, st);
 }

@@ -109,6 +109,7 @@ def test_fused_argmax_epilogue_matches_materialised_logits(gpu, orc, engine):
     ids = _ids(S, 3, WIDE["vocab"], 31)
     fused, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
     fused.set_engine(engine)
+    plain.set_engine(engine)
     for t in range(3):
         tok = fused.step_greedy(ids[:, t])
         lg = plain.step(ids[:, t])
@@ -170,5 +171,34 @@ def test_large_batch_tilings(gpu, orc, engine):
     for s in [0, 16383]:
         od = orc.Decoder(om)
         for t in range(2):
+            ref = od.step(ids[s, t])
+        assert np.abs(a[s] - ref).max() <= 1e-3, s
+
+
+def test_split_k_small_grids(gpu, orc):
+    """2048 streams (one GPU's share of 16384 on eight): out_proj and
+    down_proj have 64 tiles of 128 x 256 for 148 SMs, so each tile runs as
+    two K halves whose partial sums are added in a fixed order; the result
+    equals the f32 engine's, and two runs are bit-identical."""
+    kw = dict(vocab=2048, d_model=1024, n_layer=2, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=9)
+    S = 2048
+    ids = _ids(S, 3, kw["vocab"], 4100)
+    tc, tc2, f32 = gpu.Decoder(gm, S), gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    f32.set_engine(1)
+    tc.profile_begin()
+    for t in range(3):
+        a = tc.step(ids[:, t]).copy()
+        a2 = tc2.step(ids[:, t]).copy()
+        b = f32.step(ids[:, t])
+        assert np.array_equal(a, a2), t
+        assert np.abs(a - b).max() <= 1e-4, t
+    assert tc.profile_end()["tensor_core"]
+    sa, _ = tc.get_state()
+    sb, _ = f32.get_state()
+    assert state_rel_err(sa, sb) <= 1e-5
+    for s in [0, 2047]:
+        od = orc.Decoder(om)
+        for t in range(3):
             ref = od.step(ids[s, t])
         assert np.abs(a[s] - ref).max() <= 1e-3, s
