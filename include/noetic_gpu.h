@@ -187,7 +187,8 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * covers every SM twice, else 128).  Bit 6: for 1-4 streams, the whole step
  * as one persistent cooperative kernel instead of the fused small-batch
  * kernels.  Bit 7: the CTA-pair projection kernel (256 x 256 tiles on two
- * SMs) wherever N >= 256. */
+ * SMs) wherever N >= 256.  Bit 8: whole tiles per CTA instead of stream-K
+ * (equal K-block ranges per SM, partial tiles summed in a fixed order). */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

@@ -56,8 +56,8 @@ struct TcEpilogue {
     // operand pair hi = tf32(s) into C, lo = tf32(s - hi) into C_lo.
     bool swiglu = false;
     float *C_lo = nullptr;
-    // Split-K workspace (store mode with 256-wide tiles covering less than
-    // one wave): partial tiles and per-tile counters, zero between launches.
+    // Stream-K workspace (store and SwiGLU modes with 256-wide tiles): one
+    // partial tile per SM and one counter per SM, zero between launches.
     float *ws = nullptr;
     size_t ws_floats = 0;
     int *flags = nullptr;
@@ -68,16 +68,15 @@ struct TcEpilogue {
 bool tc_eligible(int M, int N, int K);
 
 // Tile choice for an M x N projection: TC_PAIR (the CTA-pair kernel, 256 x
-// 256 tiles on two SMs) when allow_pair and it fills every SM pair twice,
-// else 128 x 256 tiles while those fill every SM twice, else 128 x 128; and
-// the number of column tiles of that choice.
+// 256 tiles on two SMs) when allow_pair and it fills every SM pair twice;
+// else 128 x 256 tiles (spread over the SMs by stream-K when stream_k, the
+// store and SwiGLU epilogues) or 128 x 128 tiles, whichever keeps more SM
+// time busy; and the number of column tiles of that choice.
 constexpr int TC_PAIR = 2;
-int tc_pick_bn(int M, int N, bool allow_pair = false);
+int tc_pick_bn(int M, int N, bool allow_pair = false, bool stream_k = true);
 int tc_tiles_n(int N, int bn);
-// K splits the 256-wide store kernel uses for an M x N x K projection (1: none).
-int tc_ksplit(int M, int N, int K, int bn);
-// Split-K workspace a caller provides to cover any projection on this GPU.
-size_t tc_ksplit_ws_floats();
+// Stream-K workspace (one 128 x 256 partial tile per SM) a caller provides.
+size_t tc_stream_k_ws_floats();
 // Argmax partials per row: one per half tile (each epilogue warpgroup owns half the columns).
 int tc_argmax_parts(int N, int bn);
 

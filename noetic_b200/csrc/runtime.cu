@@ -445,7 +445,7 @@ struct nk_decoder {
     // one per (tokens in, tokens out) device buffer pair
     std::vector<nk::SmallLayer> small_layers;
     // persistent step kernel: device copy of the layer pointers, barrier words
-    // split-K workspace of the tensor-core projections (counters zeroed)
+    // stream-K workspace of the tensor-core projections (counters zeroed)
     float *ksplit_ws = nullptr;
     int *ksplit_flags = nullptr;
     static constexpr int KSPLIT_FLAGS = 4096;
@@ -545,12 +545,13 @@ struct ProfScope {
 };
 
 // Tile shape of a tensor-core projection; engine bits 4 / 5 / 7 force
-// 128 / 256-wide single-SM tiles / the CTA-pair kernel.
-int pick_bn(const nk_decoder *dec, int M, int N) {
+// 128 / 256-wide single-SM tiles / the CTA-pair kernel; bit 8 keeps whole
+// tiles (no stream-K).
+int pick_bn(const nk_decoder *dec, int M, int N, bool argmax = false) {
     if (dec->engine & 16) return 128;
     if ((dec->engine & 32) && N >= 256) return 256;
     if ((dec->engine & 128) && N >= 256) return nk::TC_PAIR;
-    return nk::tc_pick_bn(M, N, false);
+    return nk::tc_pick_bn(M, N, false, !argmax && !(dec->engine & 256));
 }
 
 // C = A.W^T (+bias) (R + ...), A read from `a` in the form `tc` selects.
@@ -564,8 +565,8 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         ep.bias = bias;
         ep.R = R;
         ep.ldr = N;
-        ep.ws = dec->ksplit_ws;
-        ep.ws_floats = nk::tc_ksplit_ws_floats();
+        ep.ws = (dec->engine & 256) ? nullptr : dec->ksplit_ws;
+        ep.ws_floats = nk::tc_stream_k_ws_floats();
         ep.flags = dec->ksplit_flags;
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
         cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, N), dec->stream, dec->err),
@@ -593,6 +594,10 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
         ep.swiglu = true;
         ep.bias = bias;
         ep.ldc = H;
+        ep.ws = (dec->engine & 256) ? nullptr : dec->ksplit_ws;
+        ep.ws_floats = nk::tc_stream_k_ws_floats();
+        ep.flags = dec->ksplit_flags;
+        ep.n_flags = nk_decoder::KSPLIT_FLAGS;
         Act out = gated;
         if (t_dn) {
             out = Act{nullptr, scratch, scratch + (size_t)M * H};
@@ -618,7 +623,7 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
 void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W,
                     const nk::TcOperand *Wtc, int N, uint32_t *tokens) {
     if (tc) {
-        const int bn = pick_bn(dec, M, N);
+        const int bn = pick_bn(dec, M, N, true);
         {
             ProfScope prof(dec, M, N, K, false, false);
             nk::TcEpilogue ep;
@@ -682,7 +687,7 @@ void check_err_flag(nk_decoder *dec) {
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
                                 ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 105-108 CTA-pair pipeline wait expired, 111-113 "
-                                "persistent step wait expired, 121-123 split-K hand-off wait expired)");
+                                "persistent step wait expired, 121-123 stream-K hand-off wait expired)");
     }
 }
 
@@ -1181,8 +1186,8 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         dalloc(&dec->tok_b, S, "tokens");
         dalloc(&dec->err, 1, "error flag");
         dalloc(&dec->sync, 2, "barrier words");
-        dalloc(&dec->ksplit_ws, nk::tc_ksplit_ws_floats(), "split-K workspace");
-        dalloc(&dec->ksplit_flags, nk_decoder::KSPLIT_FLAGS, "split-K counters");
+        dalloc(&dec->ksplit_ws, nk::tc_stream_k_ws_floats(), "stream-K workspace");
+        dalloc(&dec->ksplit_flags, nk_decoder::KSPLIT_FLAGS, "stream-K counters");
         cuda_check(cudaMemset(dec->ksplit_flags, 0, nk_decoder::KSPLIT_FLAGS * sizeof(int)), "memset");
         dalloc(&dec->layers_dev, model->cfg.n_layer, "layer table");
         dalloc(&dec->rng, S * 4, "rng");
@@ -1432,7 +1437,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 255) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 511) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

@@ -92,56 +92,58 @@ struct TcArgs {
     int *err;
     int swiglu_H;        // SwiGLU mode when > 0 (interleaved operand)
     float *C_lo;         // SwiGLU mode: lo half of the operand pair, or null for f32
-    // Tiles [0, full_units) run at width BN; each later tile (the last,
-    // partial wave of the grid) runs as two units of width BN / 2, so that
-    // wave takes half as long.
-    int full_units;
-    // Split-K (BN = 256 store mode, ksplit > 1): every tile runs as ksplit
-    // units over consecutive K ranges.  Units 1.. write their partial tile to
-    // ws and count it in flags[tile]; unit 0 waits for them and adds them in
-    // order.  All partial units come before every unit 0 in the unit order.
-    int ksplit;
+    // Tiles [0, sk_t0) run whole, tile c + w gridDim.x on CTA c.  With
+    // skb > 0 (256-wide store and SwiGLU modes) the remaining tiles -- the
+    // partial last wave -- are spread by K-block (stream-K): CTA c then owns
+    // K-blocks [c skb, (c+1) skb) of their tile-major K-block sequence.  A
+    // tile cut at a range boundary is finished by the CTA that holds its
+    // first K-blocks: the CTAs holding the rest write their partial tile to
+    // ws slot c and set flags[c]; the finisher adds the slots in order.  A
+    // finishing piece is the last piece of its CTA and a partial piece the
+    // first of its CTA's stream-K range, so no CTA waits on work queued
+    // behind a wait.  Whole waves stay data-parallel so that concurrently
+    // running CTAs share A rows in L2.
+    int skb;
+    int sk_t0;
     float *ws;
     int *flags;
 };
 
-// Work unit u of the tile loop: output rows m0.., columns n0.. of `width`,
-// K-blocks [kb0, kb1); ks = split index (0 finishes the tile).
-struct Unit {
-    int m0, n0, tn, width, t, ks, kb0, kb1;
+// One piece of a CTA's work: tile t, K-blocks [kb0, kb1).  np < 0: a partial
+// piece (written to ws slot blockIdx.x); np == 0: the whole tile; np > 0:
+// the tile's first K-blocks, finished after adding slots blockIdx.x + 1 ..
+// blockIdx.x + np.
+struct Piece {
+    int t, kb0, kb1, np;
 };
 
-template <int BN>
-__device__ __forceinline__ Unit unit_of(int u, const TcArgs &p, int n_tiles_n, int n_tiles, int kblocks) {
-    int t = u, hs = -1, ks = 0;
-    if (BN == 256 && p.ksplit > 1) {
-        const int parts = n_tiles * (p.ksplit - 1);
-        if (u < parts) {
-            ks = 1 + u / n_tiles;
-            t = u - (ks - 1) * n_tiles;
-        } else {
-            t = u - parts;
-        }
-    } else if (BN == 256 && u >= p.full_units) {
-        t = p.full_units + ((u - p.full_units) >> 1);
-        hs = (u - p.full_units) & 1;
+__device__ __forceinline__ bool next_piece(const TcArgs &p, int n_tiles, int kblocks, int &cursor, Piece &pc) {
+    const int G = gridDim.x, c = blockIdx.x;
+    const int dp_tiles = p.skb > 0 ? p.sk_t0 : n_tiles;
+    const int n_dp = c < dp_tiles ? (dp_tiles - c + G - 1) / G : 0;
+    if (cursor < n_dp) {
+        pc.t = c + cursor * G;
+        ++cursor;
+        pc.kb0 = 0;
+        pc.kb1 = kblocks;
+        pc.np = 0;
+        return true;
     }
-    Unit x;
-    x.t = t;
-    x.ks = ks;
-    x.m0 = (t / n_tiles_n) * BM;
-    x.tn = t % n_tiles_n;
-    x.n0 = x.tn * BN + (hs > 0 ? BN / 2 : 0);
-    x.width = hs < 0 ? BN : BN / 2;
-    if (BN == 256 && p.ksplit > 1) {
-        const int per = (kblocks + p.ksplit - 1) / p.ksplit;
-        x.kb0 = ks * per;
-        x.kb1 = min(kblocks, x.kb0 + per);
-    } else {
-        x.kb0 = 0;
-        x.kb1 = kblocks;
-    }
-    return x;
+    if (p.skb <= 0) return false;
+    const long total = (long)(n_tiles - p.sk_t0) * kblocks;
+    const long begin = (long)c * p.skb;
+    const long end = begin + p.skb < total ? begin + p.skb : total;
+    const long pos = begin + (cursor - n_dp);
+    if (pos >= end) return false;
+    const int tl = (int)(pos / kblocks);
+    pc.t = p.sk_t0 + tl;
+    pc.kb0 = (int)(pos - (long)tl * kblocks);
+    pc.kb1 = (int)((long)pc.kb0 + (end - pos) < kblocks ? (long)pc.kb0 + (end - pos) : kblocks);
+    cursor += pc.kb1 - pc.kb0;
+    if (pc.kb0 == 0 && pc.kb1 == kblocks) pc.np = 0;
+    else if (pc.kb0 > 0) pc.np = -1;
+    else pc.np = (kblocks - pc.kb1 + p.skb - 1) / p.skb;
+    return true;
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -238,22 +240,22 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // rows m0 + q*32 + lane), TMEM columns [c_begin, c_end) (output columns
 // n0 + c).  Store mode writes C (+bias, +residual); SwiGLU mode writes the
 // gated product; argmax mode folds the columns into (best, best_n).
-// With split-K (stg only): part_out != null writes this unit's partial tile
-// ([BM][BN], no bias / residual) instead of C; parts != null adds the
-// ksplit - 1 partial tiles at parts, parts + BM*BN, ... in order before the
-// bias and residual.
+// Stream-K (stg only): part_out != null writes this piece's partial tile
+// ([BM][BN] raw sums, no bias / residual / SwiGLU) instead of C; parts !=
+// null adds the nparts partial tiles at parts, parts + BM*BN, ... in order
+// before the bias and residual (or SwiGLU).
 template <int BN>
 __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, int q, int lane, int m0, int n0,
                                               int c_begin, int c_end, bool argmax_mode, bool vec, float &best,
                                               uint32_t &best_n, float *stg, const float *parts = nullptr,
-                                              float *part_out = nullptr) {
+                                              int nparts = 0, float *part_out = nullptr) {
     const int row = m0 + q * 32 + lane;
     if (stg && !argmax_mode) {
         // Transpose each 32 x 32 chunk through this warp's shared buffer
         // (float4 slots XOR-swizzled by row: conflict-free both ways), then
         // lane = column, so every load and store is one 128-byte row segment.
         const int rbase = m0 + q * 32;
-        if (p.swiglu_H) {
+        if (p.swiglu_H && !part_out) {
             // 64-column blocks: 32 gate columns, then the 32 value columns of
             // the same channels; both accumulator chains summed first.
             for (int c0 = c_begin; c0 < c_end; c0 += 64) {
@@ -271,6 +273,18 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                     tmem_ld16(ta + BN + 32 + sub, t);
 #pragma unroll
                     for (int jj = 0; jj < 16; ++jj) b[jj] = b[jj] + t[jj];
+                    for (int ks = 0; ks < nparts; ++ks) {
+                        const float *pt = parts + (size_t)ks * BM * BN + (size_t)(q * 32 + lane) * BN + c0 + sub;
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj += 4) {
+                            const float4 pa = *reinterpret_cast<const float4 *>(pt + jj);
+                            const float4 pb = *reinterpret_cast<const float4 *>(pt + 32 + jj);
+                            a[jj] = a[jj] + pa.x; a[jj + 1] = a[jj + 1] + pa.y;
+                            a[jj + 2] = a[jj + 2] + pa.z; a[jj + 3] = a[jj + 3] + pa.w;
+                            b[jj] = b[jj] + pb.x; b[jj + 1] = b[jj + 1] + pb.y;
+                            b[jj + 2] = b[jj + 2] + pb.z; b[jj + 3] = b[jj + 3] + pb.w;
+                        }
+                    }
                     const int j = j0 + sub;
 #pragma unroll
                     for (int jj = 0; jj < 16; jj += 4) {
@@ -328,8 +342,8 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                 continue;
             }
             if (parts) {
-                for (int ks = 1; ks < p.ksplit; ++ks) {
-                    const float *pt = parts + (size_t)(ks - 1) * BM * BN + (size_t)(q * 32) * BN + c0 + lane;
+                for (int ks = 0; ks < nparts; ++ks) {
+                    const float *pt = parts + (size_t)ks * BM * BN + (size_t)(q * 32) * BN + c0 + lane;
                     float pv[32];
 #pragma unroll
                     for (int r = 0; r < 32; ++r) pv[r] = pt[(size_t)r * BN];
@@ -462,13 +476,10 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
 template <int BN>
 __global__ void __launch_bounds__(THREADS, Tile<BN>::CTAS_PER_SM)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
-               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
-               const __grid_constant__ CUtensorMap mapBh2, const __grid_constant__ CUtensorMap mapBl2, TcArgs p) {
+               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
     using T = Tile<BN>;
     constexpr int STAGES = T::STAGES, STAGE_BYTES = T::STAGE_BYTES, B_BYTES = T::B_BYTES;
     constexpr uint32_t TMEM_COLS = T::TMEM_COLS, IDESC = T::IDESC;
-    // Half-width units: N = BN / 2 in the instruction descriptor.
-    constexpr uint32_t IDESC_HALF = (IDESC & ~(0x3Fu << 17)) | ((uint32_t)(BN >> 4) << 17);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned tile area (swizzle atoms must not straddle their period).
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -476,13 +487,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     uint64_t *bars = (uint64_t *)(smem + STAGES * STAGE_BYTES + T::EPI_BYTES);
     uint32_t *tmem_slot = (uint32_t *)(bars + 2 * STAGES + 2);
     __shared__ int s_abort;
-    __shared__ int s_epi_cnt, s_go;  // split-K hand-offs among the epilogue warps
+    __shared__ int s_epi_cnt, s_go;  // stream-K hand-offs among the epilogue warps
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles_n = (p.N + BN - 1) / BN;
     const int n_tiles = n_tiles_n * ((p.M + BM - 1) / BM);
-    const int n_units =
-        (BN == 256 && p.ksplit > 1) ? n_tiles * p.ksplit : p.full_units + 2 * (n_tiles - p.full_units);
     const int kblocks = (p.K + BK - 1) / BK;
 
     const uint32_t bar_full0 = smem_u32(&bars[0]);
@@ -505,10 +514,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapAl) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBh) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBl) : "memory");
-        if (p.full_units < n_tiles) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBh2) : "memory");
-            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&mapBl2) : "memory");
-        }
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -522,17 +527,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        // ---- TMA producer: runs ahead into the next tile's K-blocks while
+        // ---- TMA producer: runs ahead into the next piece's K-blocks while
         // the epilogue drains the current one.
         int stage = 0;
         uint32_t phase = 0;
-        int issued = 0;
-        for (int u = blockIdx.x; u < n_units && !*(volatile int *)&s_abort; u += gridDim.x) {
-            const Unit un = unit_of<BN>(u, p, n_tiles_n, n_tiles, kblocks);
-            const bool wide = un.width == BN;
-            const CUtensorMap *mBh = wide ? &mapBh : &mapBh2, *mBl = wide ? &mapBl : &mapBl2;
-            const uint32_t bytes = wide ? STAGE_BYTES : 2 * A_BYTES + B_BYTES;
-            for (int kb = un.kb0; kb < un.kb1; ++kb) {
+        int issued = 0, cursor = 0;
+        Piece pc;
+        while (!*(volatile int *)&s_abort && next_piece(p, n_tiles, kblocks, cursor, pc)) {
+            const int m0 = (pc.t / n_tiles_n) * BM, n0 = (pc.t % n_tiles_n) * BN;
+            for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
                 if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
                     atomicExch(p.err, 101);
                     s_abort = 1;
@@ -541,12 +544,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 if (*(volatile int *)&s_abort) break;
                 uint8_t *st = smem + stage * STAGE_BYTES;
                 const uint32_t full = bar_full0 + 8 * stage;
-                mbar_expect_tx(full, bytes);
+                mbar_expect_tx(full, STAGE_BYTES);
                 const int kx = kb * BK;
-                tma_load_2d(smem_u32(st), &mapAh, full, kx, un.m0);
-                tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, un.m0);
-                tma_load_2d(smem_u32(st + 2 * A_BYTES), mBh, full, kx, un.n0);
-                tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), mBl, full, kx, un.n0);
+                tma_load_2d(smem_u32(st), &mapAh, full, kx, m0);
+                tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, m0);
+                tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
+                tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
                 ++issued;
                 if (++stage == STAGES) {
                     stage = 0;
@@ -571,11 +574,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         // ---- MMA issuer
         int stage = 0;
         uint32_t phase = 0;
-        int i = 0;
-        for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
-            const Unit un = unit_of<BN>(u, p, n_tiles_n, n_tiles, kblocks);
-            const uint32_t idesc = un.width == BN ? IDESC : IDESC_HALF;
-            // The accumulators are free once the epilogue drained tile i - 1.
+        int i = 0, cursor = 0;
+        Piece pc;
+        for (; next_piece(p, n_tiles, kblocks, cursor, pc); ++i) {
+            // The accumulators are free once the epilogue drained piece i - 1.
             if (!mbar_wait(bar_acc_empty, (uint32_t)((i & 1) ^ 1)) || *(volatile int *)&s_abort) {
                 atomicExch(p.err, 104);
                 s_abort = 1;
@@ -583,7 +585,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             }
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             bool ok = true;
-            for (int kb = un.kb0; kb < un.kb1; ++kb) {
+            for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
                 if (!mbar_wait(bar_full0 + 8 * stage, phase) || *(volatile int *)&s_abort) {
                     atomicExch(p.err, 102);
                     s_abort = 1;
@@ -597,10 +599,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
 #pragma unroll
                 for (int kk = 0; kk < BK / 8; ++kk) {
                     const uint64_t off = (uint64_t)((kk * 32) >> 4);  // 8 tf32 = 32 bytes along the swizzled row
-                    const uint32_t acc = (kb != un.kb0 || kk) ? 1u : 0u;
-                    mma_tf32(tmem, dAh + off, dBh + off, idesc, acc);
-                    mma_tf32(tmem + BN, dAh + off, dBl + off, idesc, acc);
-                    mma_tf32(tmem + BN, dAl + off, dBh + off, idesc, 1u);
+                    const uint32_t acc = (kb != pc.kb0 || kk) ? 1u : 0u;
+                    mma_tf32(tmem, dAh + off, dBh + off, IDESC, acc);
+                    mma_tf32(tmem + BN, dAh + off, dBl + off, IDESC, acc);
+                    mma_tf32(tmem + BN, dAl + off, dBh + off, IDESC, 1u);
                 }
                 mma_commit(bar_empty0 + 8 * stage);
                 if (++stage == STAGES) {
@@ -618,14 +620,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         // 32*(w%4) .. +31 and half of the columns (warpgroup (w-4)/4).
         const int q = warp & 3;
         const int half = (warp - 4) >> 2;
+        constexpr int COLS = BN / 2;
         const bool vec = (p.ldc % 4 == 0) && (!p.R || p.ldr % 4 == 0);
         const bool argmax_mode = p.best_val != nullptr;
-        const bool split = BN == 256 && p.ksplit > 1;
-        int i = 0, n_part = 0, n_fin = 0;
-        for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
-            const Unit un = unit_of<BN>(u, p, n_tiles_n, n_tiles, kblocks);
-            const int m0 = un.m0, n0 = un.n0;
-            const int COLS = un.width / 2;  // columns of this warpgroup
+        const size_t tile_floats = (size_t)BM * BN;
+        int i = 0, cursor = 0, n_part = 0, n_fin = 0;
+        Piece pc;
+        for (; next_piece(p, n_tiles, kblocks, cursor, pc); ++i) {
+            const int m0 = (pc.t / n_tiles_n) * BM, tn = pc.t % n_tiles_n, n0 = tn * BN;
             const bool ok = mbar_wait(bar_acc_full, (uint32_t)(i & 1)) && !*(volatile int *)&s_abort;
             __syncwarp();
             if (!ok) {
@@ -635,41 +637,43 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const float *parts = nullptr;
             float *part_out = nullptr;
-            if (split) {
-                const size_t tile_floats = (size_t)BM * BN;
-                if (un.ks > 0) {
-                    part_out = p.ws + ((size_t)un.t * (p.ksplit - 1) + (un.ks - 1)) * tile_floats;
-                } else {
-                    // The tile's other K ranges: wait (bounded) until all are
-                    // published, then every epilogue warp reads them.
-                    parts = p.ws + (size_t)un.t * (p.ksplit - 1) * tile_floats;
-                    ++n_fin;
-                    if (warp == 4 && lane == 0) {
+            if (pc.np < 0) {
+                part_out = p.ws + (size_t)blockIdx.x * tile_floats;
+            } else if (pc.np > 0) {
+                // Wait (bounded) until the next np CTAs published their
+                // partials of this tile, then every epilogue warp reads them.
+                parts = p.ws + (size_t)(blockIdx.x + 1) * tile_floats;
+                ++n_fin;
+                if (warp == 4 && lane == 0) {
+                    for (int c = 1; c <= pc.np; ++c) {
                         const uint64_t t0 = globaltimer();
                         for (;;) {
                             int v;
-                            asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p.flags + un.t) : "memory");
-                            if (v >= p.ksplit - 1) break;
+                            asm volatile("ld.acquire.gpu.global.s32 %0, [%1];"
+                                         : "=r"(v)
+                                         : "l"(p.flags + blockIdx.x + c)
+                                         : "memory");
+                            if (v) break;
                             if (globaltimer() - t0 > WAIT_NS) {
                                 atomicExch(p.err, 121);
                                 break;
                             }
                         }
-                        p.flags[un.t] = 0;  // ready for the next launch
-                        __threadfence_block();
-                        *(volatile int *)&s_go = n_fin;
+                        p.flags[blockIdx.x + c] = 0;  // ready for the next launch
                     }
-                    if (lane == 0) {
-                        const uint64_t t0 = globaltimer();
-                        while (*(volatile int *)&s_go < n_fin)
-                            if (globaltimer() - t0 > WAIT_NS) {
-                                atomicExch(p.err, 122);
-                                break;
-                            }
-                        __threadfence();
-                    }
-                    __syncwarp();
+                    __threadfence_block();
+                    *(volatile int *)&s_go = n_fin;
                 }
+                if (lane == 0) {
+                    const uint64_t t0 = globaltimer();
+                    while (*(volatile int *)&s_go < n_fin)
+                        if (globaltimer() - t0 > WAIT_NS) {
+                            atomicExch(p.err, 122);
+                            break;
+                        }
+                    __threadfence();
+                }
+                __syncwarp();
             }
             const int row = m0 + q * 32 + lane;
             float best = -INFINITY;
@@ -677,8 +681,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             float *stg =
                 BN == 256 ? reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES) + (warp - 4) * 1024 : nullptr;
             epilogue_cols<BN>(p, tmem, q, lane, m0, n0, half * COLS, (half + 1) * COLS, argmax_mode, vec, best, best_n,
-                              stg, parts, part_out);
-            // TMEM of this tile fully read: hand the accumulators back.
+                              stg, parts, pc.np > 0 ? pc.np : 0, part_out);
+            // TMEM of this piece fully read: hand the accumulators back.
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar_acc_empty) : "memory");
@@ -697,7 +701,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                             break;
                         }
                     __threadfence();
-                    atomicAdd(p.flags + un.t, 1);
+                    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p.flags + blockIdx.x), "r"(1) : "memory");
                 }
                 __syncwarp();
             }
@@ -706,7 +710,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 // tile's columns: partial 2*tile_n + half, so partial order is
                 // column order and the reduction's earliest-partial tie rule
                 // keeps the first maximum.
-                const size_t slot = (size_t)row * p.n_tiles + 2 * un.tn + half;
+                const size_t slot = (size_t)row * p.n_tiles + 2 * tn + half;
                 p.best_val[slot] = best;
                 p.best_idx[slot] = best_n;
             }
@@ -1037,54 +1041,28 @@ int sm_count_cached() {
     return num_sms;
 }
 
-// K splits for a 128 x 256-tile store projection whose tiles cover less
-// than one wave: as many as fit the SMs, each at least 4 K-blocks, at most 8.
-int tc_ksplit(int M, int N, int K, int bn) {
-    if (bn != 256) return 1;
-    const long tiles = (long)((N + 255) / 256) * ((M + BM - 1) / BM);
-    const int sms = sm_count_cached();
-    if (tiles <= 0 || tiles >= sms) return 1;
-    const int kblocks = (K + BK - 1) / BK;
-    int ks = (int)std::min<long>(sms / tiles, 8);
-    ks = std::min(ks, kblocks / 4);
-    return ks >= 2 ? ks : 1;
-}
-
-// The CTA-pair kernel while it fills every SM pair at least twice, else
-// BN = 256 while the grid still fills every SM twice over, else 128.
-int tc_pick_bn(int M, int N, bool allow_pair) {
-    static int num_sms = 0;
-    if (!num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (num_sms <= 0) num_sms = 148;
-    }
+// The CTA-pair kernel when allowed and it fills every SM pair at least
+// twice.  Otherwise 128 x 256 tiles, spread by stream-K (so any tile count
+// keeps every SM busy) when the epilogue allows it; for the argmax epilogue
+// whole tiles, compared with 128 x 128 tiles by the fraction of SM time each
+// keeps busy (a 128-wide tile moves 4/3 the operand bytes per flop, and the
+// main loop is bound by operand bandwidth into shared memory).
+int tc_pick_bn(int M, int N, bool allow_pair, bool stream_k) {
+    const int num_sms = sm_count_cached();
     const long tiles256 = (long)((N + 255) / 256) * ((M + BM - 1) / BM);
     const long pair_tiles = (long)((N + 255) / 256) * ((M + 255) / 256);
     if (allow_pair && N >= 256 && pair_tiles >= 2L * (num_sms / 2)) return TC_PAIR;
     if (N < 256) return 128;
-    // Compare the fraction of SM time each width keeps busy.  A 128-wide
-    // tile moves 4/3 the operand bytes per flop of a 256-wide one (the main
-    // loop is bound by operand bandwidth into shared memory), so it counts
-    // 3/4.  256-wide: a partial last wave of at most half the SMs runs as
-    // half-width units, and fewer tiles than SMs are split along K.
-    double e256;
-    if (tiles256 < num_sms) {
-        const int ks = tc_ksplit(M, N, 1 << 20, 256);
-        e256 = (double)(tiles256 * ks) / num_sms;
-    } else {
-        const long rem = tiles256 % num_sms;
-        const double waves = (double)(tiles256 / num_sms) + (rem == 0 ? 0.0 : (2 * rem <= num_sms ? 0.5 : 1.0));
-        e256 = (double)tiles256 / (waves * num_sms);
-    }
+    if (stream_k) return 256;
+    const double e256 =
+        (double)tiles256 / ((double)((tiles256 + num_sms - 1) / num_sms) * num_sms);
     const long tiles128 = (long)((N + 127) / 128) * ((M + BM - 1) / BM);
     const long slots128 = 2L * num_sms;
     const double e128 = 0.75 * (double)tiles128 / ((double)((tiles128 + slots128 - 1) / slots128) * slots128);
     return e256 >= e128 ? 256 : 128;
 }
 
-size_t tc_ksplit_ws_floats() { return (size_t)sm_count_cached() * BM * 256; }
+size_t tc_stream_k_ws_floats() { return (size_t)sm_count_cached() * BM * 256; }
 
 int tc_tiles_n(int N, int bn) {
     const int w = bn == TC_PAIR ? 256 : bn;
@@ -1165,21 +1143,27 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
     const long tiles = (long)tc_tiles_n(W.N, BN) * ((M + BM - 1) / BM);
     const long slots = (long)num_sms * Tile<BN>::CTAS_PER_SM;
     unsigned grid = (unsigned)std::min<long>(tiles, slots);
-    // A last wave that covers at most half the grid runs as half-width units
-    // (full-width tiles only for the argmax epilogue's partial layout).
-    const long rem = tiles % (long)grid;
-    a.full_units = (int)((BN == 256 && !a.best_val && rem > 0 && 2 * rem <= (long)grid) ? tiles - rem : tiles);
-    // Fewer tiles than SMs: split K so that the units fill the grid.
-    a.ksplit = 1;
-    const int ks = tc_ksplit(M, W.N, W.K, BN);
-    if (BN == 256 && ks > 1 && !a.best_val && !a.swiglu_H && a.ws && a.flags) {
-        a.ksplit = ks;
-        a.full_units = (int)tiles;
-        grid = (unsigned)std::min<long>(tiles * ks, slots);
+    a.skb = 0;
+    a.sk_t0 = (int)tiles;
+    // The A operand pair (hi + lo) of this projection; when it fits well
+    // inside L2, CTAs far apart in the tile order lose nothing by reading
+    // different rows of it, and every tile is spread by K.
+    const bool a_in_l2 = (size_t)M * W.K * 8 <= ((size_t)48 << 20);
+    if (BN == 256 && !a.best_val && a.ws && a.flags && (tiles % slots != 0 || a_in_l2)) {
+        // Whole waves stay whole tiles (unless A fits in L2); the rest is
+        // spread over every CTA in equal K-block ranges of at least 8 K-blocks.
+        const long dp = a_in_l2 ? 0 : (tiles / slots) * slots;
+        const long kblocks = (W.K + BK - 1) / BK;
+        const long total = (tiles - dp) * kblocks;
+        long ctas = std::min<long>(slots, std::max<long>(1, total / 8));
+        const long per = (total + ctas - 1) / ctas;
+        ctas = (total + per - 1) / per;
+        a.skb = (int)per;
+        a.sk_t0 = (int)dp;
+        grid = (unsigned)(dp > 0 ? slots : ctas);
     }
-    tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(
-        mAh, mAl, *(const CUtensorMap *)mh, *(const CUtensorMap *)ml, *(const CUtensorMap *)W.map_hi128,
-        *(const CUtensorMap *)W.map_lo128, a);
+    tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(mAh, mAl, *(const CUtensorMap *)mh,
+                                                                    *(const CUtensorMap *)ml, a);
     return cudaGetLastError();
 }
 
@@ -1201,7 +1185,6 @@ cudaError_t launch_pair(const CUtensorMap &mAh, const CUtensorMap &mAl, const Tc
     // Persistent pairs: each cluster of two CTAs walks 256 x 256 tiles.
     const long tiles = (long)((W.N + 255) / 256) * ((M + 255) / 256);
     const unsigned pairs = (unsigned)std::max<long>(1, std::min<long>(tiles, num_sms / 2));
-    a.full_units = (int)tiles;
     tc_pair_kernel<<<2 * pairs, THREADS, P_SMEM_BYTES, st>>>(mAh, mAl, *(const CUtensorMap *)W.map_hi128,
                                                              *(const CUtensorMap *)W.map_lo128, a);
     return cudaGetLastError();
@@ -1225,12 +1208,11 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     alignas(64) CUtensorMap mAh, mAl;
     if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
     TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err,
-              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 1, ep.ws, ep.flags};
+              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 0, ep.ws, ep.flags};
     if (a.ws) {
-        // Split-K only when the workspace and flags cover every tile.
-        const long tiles = (long)tc_tiles_n(W.N, 256) * ((M + BM - 1) / BM);
-        const int ks = tc_ksplit(M, W.N, K, 256);
-        if (ks < 2 || tiles > ep.n_flags || (size_t)tiles * (ks - 1) * BM * 256 > ep.ws_floats) {
+        // Stream-K needs one partial slot and one counter per SM.
+        const int sms = sm_count_cached();
+        if (ep.n_flags < sms || ep.ws_floats < (size_t)sms * BM * 256) {
             a.ws = nullptr;
             a.flags = nullptr;
         }

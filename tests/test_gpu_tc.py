@@ -149,9 +149,9 @@ def test_hidden_width_off_the_interleave_grid(gpu, orc):
 
 @pytest.mark.parametrize("engine", [0, 128])
 def test_large_batch_tilings(gpu, orc, engine):
-    """16384 streams of a d=1024 model.  Engine 0: out_proj and down_proj
-    have 512 tiles of 128 x 256 on 148 SMs, so the last 68 tiles run as 136
-    half-width units (in_proj: 56 -> 112).  Engine 128: every projection
+    """16384 streams of a d=1024 model.  Engine 0: stream-K over 148 SMs
+    (out_proj: 512 tiles x 64 K-blocks, 222 K-blocks per CTA, so most CTAs
+    finish one tile cut at a range boundary).  Engine 128: every projection
     runs on the CTA-pair kernel (256 x 256 tiles).  Every stream, the last
     rows and columns included, equals the f32 engine."""
     kw = dict(vocab=2048, d_model=1024, n_layer=1, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
@@ -175,11 +175,12 @@ def test_large_batch_tilings(gpu, orc, engine):
         assert np.abs(a[s] - ref).max() <= 1e-3, s
 
 
-def test_split_k_small_grids(gpu, orc):
-    """2048 streams (one GPU's share of 16384 on eight): out_proj and
-    down_proj have 64 tiles of 128 x 256 for 148 SMs, so each tile runs as
-    two K halves whose partial sums are added in a fixed order; the result
-    equals the f32 engine's, and two runs are bit-identical."""
+def test_stream_k_small_grids(gpu, orc):
+    """2048 streams (one GPU's share of 16384 on eight): out_proj has 64
+    tiles x 64 K-blocks for 148 SMs, 28 K-blocks per CTA, so a tile spans up
+    to three CTAs and its first CTA adds the others' partial sums in a fixed
+    order; the result equals the f32 engine's, and two runs are
+    bit-identical."""
     kw = dict(vocab=2048, d_model=1024, n_layer=2, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
     om, gm = same_model(orc, gpu, kw, seed=9)
     S = 2048
