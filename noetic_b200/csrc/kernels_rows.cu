@@ -20,6 +20,8 @@ inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + thre
 
 __global__ void embed_rows_k(const uint32_t *__restrict__ tokens, const float *__restrict__ emb,
                              float *__restrict__ x, int M, int d, int vocab, int *err) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)M * d) return;
     const int m = (int)(i / d), j = (int)(i - (int64_t)m * d);
@@ -79,6 +81,8 @@ __device__ __forceinline__ void put4(const RowOut &o, size_t i, float4 v) {
 // One warp per row.
 __global__ void rmsnorm_k(const float *__restrict__ x, const float *__restrict__ gain, float eps, RowOut out,
                           int M, int d) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (warp >= M) return;
@@ -92,6 +96,8 @@ __global__ void rmsnorm_k(const float *__restrict__ x, const float *__restrict__
 }
 
 __global__ void advance_heads_k(uint32_t *heads, const uint32_t *adv, int S, int k) {
+    pdl_wait();
+    pdl_trigger();
     const int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= S) return;
     const uint32_t a = adv ? adv[s] : 1u;
@@ -114,6 +120,8 @@ template <int K, int VW>
 __global__ void ssm_decode_k(const float *__restrict__ u, float *__restrict__ state,
                              const uint32_t *__restrict__ heads, const float *__restrict__ conv_w,
                              const float *__restrict__ conv_b, RowOut g, int S, int E, int k_dyn) {
+    pdl_wait();
+    pdl_trigger();
     const int k = K > 0 ? K : k_dyn;
     const int j0 = (blockIdx.x * blockDim.x + threadIdx.x) * VW;
     if (j0 >= E) return;
@@ -391,6 +399,8 @@ __global__ void swiglu_k(const float *__restrict__ up, RowOut out, int M, int H)
 // earlier tile" so ties resolve to the earliest tile as in a serial scan.
 __global__ void argmax_partials_k(const float *__restrict__ val, const uint32_t *__restrict__ idx, int n_tiles,
                                   int M, uint32_t *__restrict__ out) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.x;
     float bv = -INFINITY;
     int bt = n_tiles;
@@ -528,8 +538,7 @@ cudaError_t embed_rows(const uint32_t *tokens, const float *emb, float *x, int M
                        int *err, cudaStream_t st) {
     const int64_t n = (int64_t)M * d;
     if (n == 0) return cudaSuccess;
-    embed_rows_k<<<blocks_for(n, 256), 256, 0, st>>>(tokens, emb, x, M, d, vocab, err);
-    return cudaGetLastError();
+    return pdl_launch(embed_rows_k, dim3(blocks_for(n, 256)), dim3(256), 0, st, tokens, emb, x, M, d, vocab, err);
 }
 
 cudaError_t embed_prompt_chunk(const uint32_t *ids, const uint32_t *lens, int max_t, int t0, int tc,
@@ -545,14 +554,12 @@ cudaError_t embed_prompt_chunk(const uint32_t *ids, const uint32_t *lens, int ma
 cudaError_t rmsnorm_rows(const float *x, const float *gain, float eps, RowOut out, int M, int d,
                          cudaStream_t st) {
     if (M == 0) return cudaSuccess;
-    rmsnorm_k<<<blocks_for((int64_t)M * 32, 256), 256, 0, st>>>(x, gain, eps, out, M, d);
-    return cudaGetLastError();
+    return pdl_launch(rmsnorm_k, dim3(blocks_for((int64_t)M * 32, 256)), dim3(256), 0, st, x, gain, eps, out, M, d);
 }
 
 cudaError_t advance_heads(uint32_t *heads, const uint32_t *adv, int S, int k, cudaStream_t st) {
     if (S == 0) return cudaSuccess;
-    advance_heads_k<<<blocks_for(S, 256), 256, 0, st>>>(heads, adv, S, k);
-    return cudaGetLastError();
+    return pdl_launch(advance_heads_k, dim3(blocks_for(S, 256)), dim3(256), 0, st, heads, adv, S, k);
 }
 
 cudaError_t advance_heads_prompt(uint32_t *heads, const uint32_t *lens, int t0, int tc, int S, int k,
@@ -569,16 +576,17 @@ cudaError_t ssm_decode(const float *u, float *state, const uint32_t *heads, cons
     const int per = vec ? 4 : 1;
     dim3 grid((unsigned)((E / per + 127) / 128), (unsigned)std::min(S, 65535));
     switch (vec ? k : -k) {
-#define NK_CASE(KK)                                                                                             \
-    case KK: ssm_decode_k<KK, 4><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k); break;     \
-    case -KK: ssm_decode_k<KK, 1><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k); break;
+#define NK_CASE(KK)                                                                                        \
+    case KK: return pdl_launch(ssm_decode_k<KK, 4>, grid, dim3(128), 0, st, u, state, heads, conv_w, conv_b, g, \
+                               S, E, k);                                                                    \
+    case -KK: return pdl_launch(ssm_decode_k<KK, 1>, grid, dim3(128), 0, st, u, state, heads, conv_w, conv_b, \
+                                g, S, E, k);
         NK_CASE(1) NK_CASE(2) NK_CASE(3) NK_CASE(4) NK_CASE(5) NK_CASE(6) NK_CASE(7) NK_CASE(8)
 #undef NK_CASE
         default:
-            if (vec) ssm_decode_k<0, 4><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k);
-            else ssm_decode_k<0, 1><<<grid, 128, 0, st>>>(u, state, heads, conv_w, conv_b, g, S, E, k);
+            if (vec) return pdl_launch(ssm_decode_k<0, 4>, grid, dim3(128), 0, st, u, state, heads, conv_w, conv_b, g, S, E, k);
+            return pdl_launch(ssm_decode_k<0, 1>, grid, dim3(128), 0, st, u, state, heads, conv_w, conv_b, g, S, E, k);
     }
-    return cudaGetLastError();
 }
 
 cudaError_t ssm_prefill_seq(const float *u, float *state, const uint32_t *heads,
@@ -640,8 +648,7 @@ cudaError_t swiglu_rows(const float *up, RowOut s, int M, int H, cudaStream_t st
 cudaError_t argmax_partials(const float *val, const uint32_t *idx, int n_tiles, int M, uint32_t *out,
                             cudaStream_t st) {
     if (M == 0) return cudaSuccess;
-    argmax_partials_k<<<M, 256, 0, st>>>(val, idx, n_tiles, M, out);
-    return cudaGetLastError();
+    return pdl_launch(argmax_partials_k, dim3(M), dim3(256), 0, st, val, idx, n_tiles, M, out);
 }
 
 cudaError_t argmax_rows(const float *x, uint32_t *out, int M, int V, cudaStream_t st) {

@@ -32,8 +32,6 @@ namespace {
 constexpr int WARPS = 4;
 constexpr int THREADS = WARPS * 32;
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Bulk prefetch into L2 of the 16-byte aligned part of [p, p + bytes): the
 // start rounds up and the end rounds down, so no byte outside the range is
@@ -269,7 +267,7 @@ __global__ void __launch_bounds__(THREADS) in_ssm_k(const float *__restrict__ x,
         prefetch_rows(w_in, 3 * E, d, 2 * E + j0, min(WARPS, E - j0));
     }
     pdl_wait();
-    pdl_launch_next();
+    pdl_trigger();
     norm_rows_to_smem<MR>(x, gain, eps, M, d, xs);
     if (j >= E) return;
     float av[MR] = {}, az[MR] = {}, ao[MR] = {};
@@ -321,7 +319,7 @@ __global__ void __launch_bounds__(THREADS) proj_res_k(const float *__restrict__ 
     if (NW > 0) load_row<NW>(w + (size_t)(n < N ? n : N - 1) * K, K, wr);
     else if (threadIdx.x == 0) prefetch_rows(w, N, K, n0, WARPS);
     pdl_wait();
-    pdl_launch_next();
+    pdl_trigger();
     copy_rows_to_smem<MR>(act, M, K, as);
     if (n >= N) return;
     float acc[MR] = {};
@@ -356,7 +354,7 @@ __global__ void __launch_bounds__(THREADS) up_swiglu_k(const float *__restrict__
         prefetch_rows(w_up, 2 * H, d, H + j0, min(WARPS, H - j0));
     }
     pdl_wait();
-    pdl_launch_next();
+    pdl_trigger();
     norm_rows_to_smem<MR>(x, gain, eps, M, d, xs);
     if (j >= H) return;
     float aa[MR] = {}, ab[MR] = {};
@@ -399,7 +397,7 @@ __global__ void __launch_bounds__(THREADS) logits_k(const float *__restrict__ x,
         prefetch_rows(emb, V, d, v0, WARPS * LROWS);
     }
     pdl_wait();
-    pdl_launch_next();
+    pdl_trigger();
     norm_rows_to_smem<MR>(x, gain, eps, M, d, xs);
     float bv[MR];
     uint32_t bi[MR];
@@ -452,7 +450,7 @@ __global__ void embed_step_k(const uint32_t *__restrict__ tokens, const float *_
                              float *__restrict__ x, uint32_t *__restrict__ heads, int M, int d, int vocab, int k,
                              int *err) {
     pdl_wait();
-    pdl_launch_next();
+    pdl_trigger();
     for (int r = 0; r < M; ++r) {
         uint32_t t = tokens[r];
         if (t >= (uint32_t)vocab) {

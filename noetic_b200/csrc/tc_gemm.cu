@@ -525,6 +525,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // Prologue done: let the next kernel in the stream start its own, then
+    // wait until the previous one has finished writing this one's inputs.
+    pdl_trigger();
+    pdl_wait();
 
     if (warp == 0 && lane == 0) {
         // ---- TMA producer: runs ahead into the next piece's K-blocks while
@@ -833,6 +837,10 @@ tc_pair_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     pair_sync();  // both CTAs' barriers initialised before any cross-CTA signal
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // Prologue done: let the next kernel in the stream start its own, then
+    // wait until the previous one has finished writing this one's inputs.
+    pdl_trigger();
+    pdl_wait();
 
     if (warp == 0 && lane == 0) {
         // ---- TMA producer (both CTAs): this CTA's halves, completing on the
@@ -1162,9 +1170,8 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
         a.sk_t0 = (int)dp;
         grid = (unsigned)(dp > 0 ? slots : ctas);
     }
-    tc_gemm_kernel<BN><<<grid, THREADS, Tile<BN>::SMEM_BYTES, st>>>(mAh, mAl, *(const CUtensorMap *)mh,
-                                                                    *(const CUtensorMap *)ml, a);
-    return cudaGetLastError();
+    return pdl_launch(tc_gemm_kernel<BN>, dim3(grid), dim3(THREADS), Tile<BN>::SMEM_BYTES, st, mAh, mAl,
+                      *(const CUtensorMap *)mh, *(const CUtensorMap *)ml, a);
 }
 
 cudaError_t launch_pair(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, TcArgs a, int M,
