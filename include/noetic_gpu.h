@@ -188,7 +188,8 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * as one persistent cooperative kernel instead of the fused small-batch
  * kernels.  Bit 7: the CTA-pair projection kernel (256 x 256 tiles on two
  * SMs) wherever N >= 256.  Bit 8: whole tiles per CTA instead of stream-K
- * (equal K-block ranges per SM, partial tiles summed in a fixed order). */
+ * (equal K-block ranges per SM, partial tiles summed in a fixed order).
+ * Bit 9: no L2 cache policies on projection loads and stores. */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

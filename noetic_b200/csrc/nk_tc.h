@@ -62,6 +62,8 @@ struct TcEpilogue {
     size_t ws_floats = 0;
     int *flags = nullptr;
     int n_flags = 0;
+    // L2 policies: weights evict-last, staged outputs evict-first.
+    bool l2hints = true;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.

@@ -566,6 +566,7 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         ep.R = R;
         ep.ldr = N;
         ep.ws = (dec->engine & 256) ? nullptr : dec->ksplit_ws;
+        ep.l2hints = !(dec->engine & 512);
         ep.ws_floats = nk::tc_stream_k_ws_floats();
         ep.flags = dec->ksplit_flags;
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
@@ -595,6 +596,7 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
         ep.bias = bias;
         ep.ldc = H;
         ep.ws = (dec->engine & 256) ? nullptr : dec->ksplit_ws;
+        ep.l2hints = !(dec->engine & 512);
         ep.ws_floats = nk::tc_stream_k_ws_floats();
         ep.flags = dec->ksplit_flags;
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
@@ -629,6 +631,7 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
             nk::TcEpilogue ep;
             ep.best_val = dec->best_val;
             ep.best_idx = dec->best_idx;
+            ep.l2hints = false;  // the tied embedding (268 MB as hi + lo) does not fit L2
             cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, bn, dec->stream, dec->err), "tcgen05 projection");
             dec->launches += 1;
             dec->prof_tc = dec->prof_tc || dec->profiling;
@@ -1437,7 +1440,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 511) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 1023) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

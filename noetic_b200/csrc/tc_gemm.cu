@@ -107,6 +107,7 @@ struct TcArgs {
     int sk_t0;
     float *ws;
     int *flags;
+    int l2hints;  // 1: weights loaded evict-last, staged outputs stored evict-first
 };
 
 // One piece of a CTA's work: tile t, K-blocks [kb0, kb1).  np < 0: a partial
@@ -188,6 +189,31 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
+// The same load with an L2 cache policy (createpolicy) attached.
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap *map, uint32_t bar, int x, int y,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;"
+        ::"r"(dst), "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
+// L2 policies: weights are re-read by every row tile and should stay; the
+// epilogue's outputs stream out and should leave first.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void st_stream(float *p, float v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
+}
+
 // K-major operand with the 64-byte swizzle (layout type 4): rows of 64 bytes,
 // 8-row groups ATOM_BYTES apart.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -251,6 +277,7 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                                               int nparts = 0, float *part_out = nullptr) {
     const int row = m0 + q * 32 + lane;
     if (stg && !argmax_mode) {
+        const uint64_t pol_out = policy_evict_first();
         // Transpose each 32 x 32 chunk through this warp's shared buffer
         // (float4 slots XOR-swizzled by row: conflict-free both ways), then
         // lane = column, so every load and store is one 128-byte row segment.
@@ -306,10 +333,16 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                     if (grow < p.M) {
                         if (p.C_lo) {
                             const float h = tf32_round(sv);
-                            p.C[(size_t)grow * p.ldc + jc] = h;
-                            p.C_lo[(size_t)grow * p.ldc + jc] = tf32_round(sv - h);
+                            if (p.l2hints) {
+                                st_stream(p.C + (size_t)grow * p.ldc + jc, h, pol_out);
+                                st_stream(p.C_lo + (size_t)grow * p.ldc + jc, tf32_round(sv - h), pol_out);
+                            } else {
+                                p.C[(size_t)grow * p.ldc + jc] = h;
+                                p.C_lo[(size_t)grow * p.ldc + jc] = tf32_round(sv - h);
+                            }
                         } else {
-                            p.C[(size_t)grow * p.ldc + jc] = sv;
+                            if (p.l2hints) st_stream(p.C + (size_t)grow * p.ldc + jc, sv, pol_out);
+                            else p.C[(size_t)grow * p.ldc + jc] = sv;
                         }
                     }
                 }
@@ -369,7 +402,8 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                 if (grow < p.M && cok) {
                     if (p.bias) o = o + bcol;
                     if (p.R) o = rv[r] + o;
-                    p.C[(size_t)grow * p.ldc + col] = o;
+                    if (p.l2hints) st_stream(p.C + (size_t)grow * p.ldc + col, o, pol_out);
+                    else p.C[(size_t)grow * p.ldc + col] = o;
                 }
             }
             __syncwarp();
@@ -533,6 +567,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     if (warp == 0 && lane == 0) {
         // ---- TMA producer: runs ahead into the next piece's K-blocks while
         // the epilogue drains the current one.
+        const uint64_t pol_w = policy_evict_last();
         int stage = 0;
         uint32_t phase = 0;
         int issued = 0, cursor = 0;
@@ -552,8 +587,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 const int kx = kb * BK;
                 tma_load_2d(smem_u32(st), &mapAh, full, kx, m0);
                 tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, m0);
-                tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
-                tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
+                if (p.l2hints) {
+                    tma_load_2d_hint(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0, pol_w);
+                    tma_load_2d_hint(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0, pol_w);
+                } else {
+                    tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
+                    tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
+                }
                 ++issued;
                 if (++stage == STAGES) {
                     stage = 0;
@@ -1215,7 +1255,7 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     alignas(64) CUtensorMap mAh, mAl;
     if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
     TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err,
-              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 0, ep.ws, ep.flags};
+              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 0, ep.ws, ep.flags, ep.l2hints ? 1 : 0};
     if (a.ws) {
         // Stream-K needs one partial slot and one counter per SM.
         const int sms = sm_count_cached();
