@@ -112,6 +112,17 @@ nk_status nk_model_load_ckpt(const char *path, int device, nk_model **out);
  * cmd_gen needs.  Used to hand models between implementations. */
 nk_status nk_model_save_ckpt(const nk_model *model, const char *path);
 
+/* Lm::loss (model.rs:228-234): the batched forward Lm::logits (model.rs:209-226)
+ * of `batch` sequences of `t` tokens from the zero state, then the mean
+ * cross-entropy Graph::softmax_ce (autograd.rs:579-624) in nats over the
+ * positions whose target is not 0xFFFFFFFF (1 when there are none).  ids and
+ * targets: host [batch * t], sequence-major.  logits_out (host [batch * t,
+ * vocab]) is optional.  Tokens or targets out of range: NK_ERR_INVALID; a
+ * non-finite logit: NK_ERR_DEVICE.  Runs on a scratch decoder of `batch`
+ * streams; no other decoder's state is touched. */
+nk_status nk_model_loss(nk_model *model, const uint32_t *ids, const uint32_t *targets, uint32_t batch,
+                        uint32_t t, float *loss_out, float *logits_out);
+
 /* ---------------------------------------------------------------- decoder */
 
 /* Decoder::new (infer.rs:86-88) for n_streams independent streams, each

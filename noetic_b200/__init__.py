@@ -70,6 +70,7 @@ SIGNATURES = {
     "nk_model_get_tensor": (_i32, [_P, C.c_char_p, _P, _u64]),
     "nk_model_load_ckpt": (_i32, [C.c_char_p, _i32, C.POINTER(_P)]),
     "nk_model_save_ckpt": (_i32, [_P, C.c_char_p]),
+    "nk_model_loss": (_i32, [_P, _P, _P, _u32, _u32, C.POINTER(C.c_float), _P]),
     "nk_decoder_create": (_i32, [_P, _u32, C.POINTER(_P)]),
     "nk_decoder_destroy": (_i32, [_P]),
     "nk_decoder_streams": (_i32, [_P, C.POINTER(_u32)]),
@@ -251,6 +252,20 @@ class Model:
 
     def save(self, path: str):
         _check(lib().nk_model_save_ckpt(self.h, os.fsencode(path)))
+
+    def loss(self, ids, targets, batch: int, t: int, want_logits: bool = False):
+        """Lm::loss (model.rs:228-234): mean cross-entropy in nats of `batch`
+        sequences of `t` tokens (targets 0xFFFFFFFF ignored); returns the loss,
+        or (loss, logits [batch * t, vocab]) with want_logits."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32).reshape(-1)
+        targets = np.ascontiguousarray(targets, dtype=np.uint32).reshape(-1)
+        if ids.size != batch * t or targets.size != batch * t:
+            raise ValueError("ids and targets must hold batch * t entries")
+        out = np.empty((batch * t, self.cfg.vocab), dtype=np.float32) if want_logits else None
+        loss = C.c_float()
+        _check(lib().nk_model_loss(self.h, _ptr(ids), _ptr(targets), batch, t, C.byref(loss),
+                                   _ptr(out) if out is not None else None))
+        return (float(loss.value), out) if want_logits else float(loss.value)
 
     def close(self):
         if getattr(self, "h", None):

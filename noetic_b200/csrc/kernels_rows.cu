@@ -445,6 +445,85 @@ __global__ void argmax_partials_k(const float *__restrict__ val, const uint32_t 
     }
 }
 
+// Graph::softmax_ce forward per row (autograd.rs:579-624): the row maximum,
+// the f32 sum of exp(v - max), p = max(exp(v_t - max) / max(sum, 1e-30),
+// 1e-20), nll = -ln(p) in f64.  Row r of the block is logits row r of a
+// prompt chunk (stream-major, tcc positions per stream); its position in the
+// [batch, T] sequence layout is s * T + t0 + (r0 + r) % tcc with s = (r0 + r) / tcc.
+// A non-finite logit sets *err = 3 (the reference rejects it).
+__global__ void softmax_ce_rows_k(const float *__restrict__ logits, int V, int r0, int tcc, int T, int t0,
+                                  const uint32_t *__restrict__ targets, double *__restrict__ nll,
+                                  uint32_t *__restrict__ counted, int *err) {
+    const int r = blockIdx.x;
+    const float *row = logits + (size_t)r * V;
+    const int g = r0 + r, s = g / tcc;
+    const size_t pos = (size_t)s * T + t0 + (g - s * tcc);
+    __shared__ float red[32];
+    __shared__ int bad;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    if (threadIdx.x == 0) bad = 0;
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float v = row[j];
+        if (!isfinite(v)) bad = 1;
+        mx = fmaxf(mx, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = lane < nw ? red[lane] : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    __syncthreads();
+    float sum = 0.0f;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) sum += expf(row[j] - mx);
+    sum = warp_sum(sum);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float tot = 0.0f;
+        for (int w = 0; w < nw; ++w) tot += red[w];
+        const uint32_t t = targets[pos];
+        if (bad) atomicExch(err, 3);
+        if (t != 0xFFFFFFFFu && t < (uint32_t)V) {
+            const float inv = 1.0f / fmaxf(tot, 1e-30f);
+            const float pr = fmaxf(expf(row[t] - mx) * inv, 1e-20f);
+            nll[pos] = -log((double)pr);
+            counted[pos] = 1u;
+        } else {
+            nll[pos] = 0.0;
+            counted[pos] = 0u;
+        }
+    }
+}
+
+// Mean of nll over counted rows (1 when none), in a fixed order: thread i
+// sums rows i, i + blockDim, ... ascending, then a fixed tree.
+__global__ void ce_mean_k(const double *__restrict__ nll, const uint32_t *__restrict__ counted, size_t n,
+                          float *out) {
+    __shared__ double ssum[1024];
+    __shared__ unsigned long long scnt[1024];
+    double a = 0.0;
+    unsigned long long c = 0;
+    for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
+        a += nll[i];
+        c += counted[i];
+    }
+    ssum[threadIdx.x] = a;
+    scnt[threadIdx.x] = c;
+    __syncthreads();
+    for (int w = blockDim.x >> 1; w > 0; w >>= 1) {
+        if ((int)threadIdx.x < w) {
+            ssum[threadIdx.x] += ssum[threadIdx.x + w];
+            scnt[threadIdx.x] += scnt[threadIdx.x + w];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *out = (float)(ssum[0] / (scnt[0] ? (double)scnt[0] : 1.0));
+}
+
 // Block per row: first index of the maximum over non-NaN entries; 0 when
 // the maximum is -inf or every entry is NaN (tensor.rs:354-365).
 __global__ void argmax_rows_k(const float *__restrict__ x, uint32_t *__restrict__ out, int V) {
@@ -649,6 +728,18 @@ cudaError_t argmax_partials(const float *val, const uint32_t *idx, int n_tiles, 
                             cudaStream_t st) {
     if (M == 0) return cudaSuccess;
     return pdl_launch(argmax_partials_k, dim3(M), dim3(256), 0, st, val, idx, n_tiles, M, out);
+}
+
+cudaError_t softmax_ce_rows(const float *logits, int rows, int V, int r0, int tcc, int T, int t0,
+                            const uint32_t *targets, double *nll, uint32_t *counted, int *err, cudaStream_t st) {
+    if (rows == 0) return cudaSuccess;
+    softmax_ce_rows_k<<<rows, 256, 0, st>>>(logits, V, r0, tcc, T, t0, targets, nll, counted, err);
+    return cudaGetLastError();
+}
+
+cudaError_t ce_mean(const double *nll, const uint32_t *counted, size_t n, float *out, cudaStream_t st) {
+    ce_mean_k<<<1, 1024, 0, st>>>(nll, counted, n, out);
+    return cudaGetLastError();
 }
 
 cudaError_t argmax_rows(const float *x, uint32_t *out, int M, int V, cudaStream_t st) {

@@ -89,6 +89,14 @@ cudaError_t argmax_partials(const float *val, const uint32_t *idx, int n_tiles, 
 // out[m] = argmax(x[m,:]) (tensor.rs:354-365), first strict maximum, NaN skipped.
 cudaError_t argmax_rows(const float *x, uint32_t *out, int M, int V, cudaStream_t st);
 
+// Cross-entropy of one block of logits rows against targets (softmax_ce,
+// autograd.rs:579-624): rows r of the block sit at sequence position
+// s * T + t0 + (r0 + r) % tcc, s = (r0 + r) / tcc; nll / counted per position.
+cudaError_t softmax_ce_rows(const float *logits, int rows, int V, int r0, int tcc, int T, int t0,
+                            const uint32_t *targets, double *nll, uint32_t *counted, int *err, cudaStream_t st);
+// Mean nll over counted positions (1 when none) into *out, fixed order.
+cudaError_t ce_mean(const double *nll, const uint32_t *counted, size_t n, float *out, cudaStream_t st);
+
 // Gather rows x[s*tc + (lens[s]-1-t0)] for streams whose last prompt token lies
 // in [t0, t0+tc) into last[s].
 cudaError_t gather_last_rows(const float *x, const uint32_t *lens, int t0, int tc, float *last,

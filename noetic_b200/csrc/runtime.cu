@@ -6,6 +6,7 @@
 // Every entry point returns nk_status and records a thread-local message.
 
 #include <algorithm>
+#include <functional>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -690,7 +691,8 @@ void check_err_flag(nk_decoder *dec) {
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
                                 ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 105-108 CTA-pair pipeline wait expired, 111-113 "
-                                "persistent step wait expired, 121-123 stream-K hand-off wait expired)");
+                                "persistent step wait expired, 121-123 stream-K hand-off wait expired, 3 non-finite logit in "
+                                "softmax_ce)");
     }
 }
 
@@ -836,8 +838,12 @@ void validate_tokens(const nk_model *m, const uint32_t *t, size_t n) {
 
 // The prompt loop as a chunked scan (model.rs:148-165 over each prompt,
 // continuing from the current LmState).  ids/lens already on the device.
+// per_chunk(t0, tcc), when set, runs after the layers of each prompt chunk,
+// with the chunk's final hidden rows in p_x (row s * tcc + t is stream s,
+// position t0 + t).
 void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_lens,
-                    const std::vector<uint32_t> &lens, uint32_t max_t, float *last_logits_host) {
+                    const std::vector<uint32_t> &lens, uint32_t max_t, float *last_logits_host,
+                    const std::function<void(uint32_t, int)> &per_chunk = {}) {
     nk_model *m = dec->model;
     const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(),
               k = (int)m->k(), V = (int)m->cfg.vocab;
@@ -904,6 +910,7 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
                                              gated, t_dn);
             project(dec, t_dn, s_act, R, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->p_x, dec->p_x);
         }
+        if (per_chunk) per_chunk(t0, tcc);
         launch_ok(dec, nk::gather_last_rows(dec->p_x, d_lens, (int)t0, tcc, dec->p_last, S, d, st), "gather last");
         launch_ok(dec, nk::advance_heads_prompt(dec->heads, d_lens, (int)t0, tcc, S, k, st), "advance heads");
     }
@@ -1284,6 +1291,91 @@ nk_status nk_decoder_prefill(nk_decoder *dec, const uint32_t *ids, const uint32_
         prefill_device(dec, dec->p_ids, dec->p_lens, lv, max_t, last_logits);
         check_err_flag(dec);
     });
+}
+
+nk_status nk_model_loss(nk_model *model, const uint32_t *ids, const uint32_t *targets, uint32_t batch, uint32_t t,
+                        float *loss_out, float *logits_out) {
+    nk_decoder *tmp = nullptr;
+    nk_status st = guard([&] {
+        if (!model || !ids || !targets || !loss_out) fail(NK_ERR_INVALID, "null argument");
+        if (batch == 0 || t == 0) fail(NK_ERR_INVALID, "batch and sequence length must be positive");
+        const size_t n = (size_t)batch * t;
+        validate_tokens(model, ids, n);
+        const uint32_t V = (uint32_t)model->cfg.vocab;
+        for (size_t i = 0; i < n; ++i)
+            if (targets[i] != 0xFFFFFFFFu && targets[i] >= V) fail(NK_ERR_INVALID, "softmax_ce: target out of range");
+    });
+    if (st != NK_OK) return st;
+    // A scratch decoder of `batch` streams from the zero state (Lm::logits
+    // starts every sequence from zero padding and a zero scan carry).
+    st = nk_decoder_create(model, batch, &tmp);
+    if (st != NK_OK) return st;
+    st = guard([&] {
+        nk_decoder *dec = tmp;
+        nk_model *m = model;
+        const int S = (int)batch, d = (int)m->d();
+        const size_t n = (size_t)batch * t, V = m->cfg.vocab;
+        ensure_ready(dec);
+        std::vector<uint32_t> lv(batch, t);
+        upload_prompts(dec, ids, lv.data(), t);
+        uint32_t *d_tg = nullptr;
+        double *d_nll = nullptr;
+        uint32_t *d_cnt = nullptr;
+        float *d_lg = nullptr, *d_loss = nullptr;
+        struct Free {
+            std::vector<void *> p;
+            ~Free() {
+                for (void *q : p) cudaFree(q);
+            }
+        } fr;
+        dalloc(&d_tg, n, "targets");
+        fr.p.push_back(d_tg);
+        dalloc(&d_nll, n, "nll");
+        fr.p.push_back(d_nll);
+        dalloc(&d_cnt, n, "nll counted");
+        fr.p.push_back(d_cnt);
+        dalloc(&d_loss, 1, "loss");
+        fr.p.push_back(d_loss);
+        // Logits in blocks of at most 512 MiB.
+        const int block_rows = (int)std::max<size_t>(1, std::min<size_t>(((size_t)512 << 20) / (4 * V), 1u << 16));
+        dalloc(&d_lg, (size_t)block_rows * V, "logits block");
+        fr.p.push_back(d_lg);
+        cuda_check(cudaMemcpyAsync(d_tg, targets, n * sizeof(uint32_t), cudaMemcpyHostToDevice, dec->stream),
+                   "upload targets");
+        const nk::TcOperand *w_lg = tc_op(m, 4 * m->cfg.n_layer);
+        auto per_chunk = [&](uint32_t t0, int tcc) {
+            const int R = S * tcc;
+            for (int r0 = 0; r0 < R; r0 += block_rows) {
+                const int rr = std::min(block_rows, R - r0);
+                const bool t_lg = use_tc(dec, rr, (int)V, d, w_lg);
+                const Act nrm{dec->p_n, dec->p_ahi, dec->p_alo};
+                launch_ok(dec, nk::rmsnorm_rows(dec->p_x + (size_t)r0 * d, m->dp(m->norm_f), m->cfg.eps, nrm.out(t_lg),
+                                                rr, d, dec->stream),
+                          "rmsnorm");
+                project(dec, t_lg, nrm, rr, d, m->dp(m->emb), w_lg, (int)V, nullptr, d_lg, nullptr);
+                launch_ok(dec, nk::softmax_ce_rows(d_lg, rr, (int)V, r0, tcc, (int)t, (int)t0, d_tg, d_nll, d_cnt,
+                                                   dec->err, dec->stream),
+                          "softmax_ce");
+                if (logits_out) {
+                    // Rows of one stream are consecutive positions: one copy per run.
+                    for (int r = 0; r < rr;) {
+                        const int g = r0 + r, s = g / tcc, tt = g - s * tcc;
+                        const int run = std::min(rr - r, tcc - tt);
+                        cuda_check(cudaMemcpyAsync(logits_out + ((size_t)s * t + t0 + tt) * V, d_lg + (size_t)r * V,
+                                                   (size_t)run * V * sizeof(float), cudaMemcpyDeviceToHost, dec->stream),
+                                   "download logits");
+                        r += run;
+                    }
+                }
+            }
+        };
+        prefill_device(dec, dec->p_ids, dec->p_lens, lv, t, nullptr, per_chunk);
+        launch_ok(dec, nk::ce_mean(d_nll, d_cnt, n, d_loss, dec->stream), "loss mean");
+        cuda_check(cudaMemcpyAsync(loss_out, d_loss, sizeof(float), cudaMemcpyDeviceToHost, dec->stream), "download loss");
+        check_err_flag(dec);
+    });
+    nk_decoder_destroy(tmp);
+    return st;
 }
 
 nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uint32_t *history,

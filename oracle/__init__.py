@@ -113,6 +113,8 @@ def lib():
             "orc_model_tensor_numel": (_u64, [_P, _u64]),
             "orc_model_set_threads": (None, [_P, _u64]),
             "orc_lm_logits": (C.c_int, [_P, _U32, _u64, _u64, C.c_int, _F]),
+            "orc_softmax_ce": (C.c_int, [_F, _u64, _u64, _U32, C.POINTER(C.c_float)]),
+            "orc_lm_loss": (C.c_int, [_P, _U32, _U32, _u64, _u64, C.c_int, C.POINTER(C.c_float), C.c_void_p]),
             "orc_lm_prefill_state": (C.c_int, [_P, _U32, _u64, _u64, _F, _U32, _F]),
             "orc_state_new": (_P, [_P]),
             "orc_state_free": (None, [_P]),
@@ -257,6 +259,19 @@ class Model:
             raise ValueError(last_error())
         return out
 
+    def loss(self, ids: np.ndarray, targets: np.ndarray, batch: int, t: int, scan_policy: int = 1,
+             want_logits: bool = False):
+        """Lm::loss (model.rs:228-234): mean cross-entropy in nats over rows whose
+        target is not 0xFFFFFFFF; returns loss, or (loss, logits) with want_logits."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32).reshape(-1)
+        targets = np.ascontiguousarray(targets, dtype=np.uint32).reshape(-1)
+        out = np.empty((batch * t, self.cfg.vocab), dtype=np.float32) if want_logits else None
+        loss = C.c_float()
+        if lib().orc_lm_loss(self.ptr, ids, targets, batch, t, scan_policy, C.byref(loss),
+                             out.ctypes.data if out is not None else None) != 0:
+            raise ValueError(last_error())
+        return (float(loss.value), out) if want_logits else float(loss.value)
+
     def prefill_state(self, ids: np.ndarray, batch: int, t: int):
         """Batched forward; returns (state [batch, L, (k+1)E], heads [batch], last logits)."""
         c = self.cfg
@@ -358,6 +373,16 @@ def generate(model: Model, prompt, n: int, cfg: SampleCfg, rng: Rng) -> np.ndarr
 # ------------------------------------------------------------------ tensor.rs / scan.rs
 def worker_count(requested: int, jobs: int, total: int) -> int:
     return int(lib().orc_worker_count(requested, jobs, total))
+
+
+def softmax_ce(logits: np.ndarray, targets: np.ndarray) -> float:
+    """Graph::softmax_ce forward (autograd.rs:579-624) over logits [rows, vocab]."""
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    targets = np.ascontiguousarray(targets, dtype=np.uint32).reshape(-1)
+    loss = C.c_float()
+    if lib().orc_softmax_ce(logits, logits.shape[0], logits.shape[1], targets, C.byref(loss)) != 0:
+        raise ValueError(last_error())
+    return float(loss.value)
 
 
 def softmax_inplace(x: np.ndarray):

@@ -759,6 +759,42 @@ uint32_t sample_impl(float *logits, uint64_t vocab, const orc_sample_cfg *cfg,
     return chosen;
 }
 
+// Graph::softmax_ce forward (autograd.rs:579-624): per row the maximum, the
+// sequential f32 sum of exp(v - max), probabilities scaled by 1/max(sum,
+// 1e-30); the loss subtracts ln(max(p[target], 1e-20)) in f64 and is the mean
+// over rows whose target is not u32::MAX (1 when there are none).
+float softmax_ce(const float *logits, uint64_t rows, uint64_t vocab, const uint32_t *targets) {
+    if (vocab == 0) throw std::invalid_argument("softmax_ce: vocabulary must be positive");
+    std::vector<float> probs(vocab);
+    double loss = 0.0;
+    uint64_t cnt = 0;
+    for (uint64_t i = 0; i < rows; ++i) {
+        const float *row = logits + i * vocab;
+        float mx = -INFINITY;
+        for (uint64_t j = 0; j < vocab; ++j) {
+            if (!std::isfinite(row[j])) throw std::invalid_argument("softmax_ce: logits must be finite");
+            if (row[j] > mx) mx = row[j];
+        }
+        float s = 0.0f;
+        for (uint64_t j = 0; j < vocab; ++j) {
+            const float e = expf(row[j] - mx);
+            probs[j] = e;
+            s += e;
+        }
+        const float inv = 1.0f / std::max(s, 1e-30f);
+        for (uint64_t j = 0; j < vocab; ++j) probs[j] *= inv;
+        const uint32_t t = targets[i];
+        if (t != 0xFFFFFFFFu) {
+            if (t >= vocab) throw std::invalid_argument("softmax_ce: target out of range");
+            const float p = std::max(probs[t], 1e-20f);
+            loss -= std::log((double)p);
+            ++cnt;
+        }
+    }
+    const double denom = cnt == 0 ? 1.0 : (double)cnt;
+    return (float)(loss / denom);
+}
+
 template <class F>
 int guarded(F &&f) {
     try {
@@ -851,6 +887,25 @@ int orc_lm_logits(const orc_model *m, const uint32_t *ids, uint64_t batch, uint6
                   int scan_policy, float *logits_out) {
     return guarded([&] {
         lm_forward(m, ids, batch, t, scan_policy, logits_out, nullptr, nullptr, nullptr);
+    });
+}
+
+int orc_softmax_ce(const float *logits, uint64_t rows, uint64_t vocab, const uint32_t *targets, float *loss_out) {
+    return guarded([&] { *loss_out = softmax_ce(logits, rows, vocab, targets); });
+}
+
+int orc_lm_loss(const orc_model *m, const uint32_t *ids, const uint32_t *targets, uint64_t batch, uint64_t t,
+                int scan_policy, float *loss_out, float *logits_out) {
+    return guarded([&] {
+        const uint64_t rows = batch * t, V = m->cfg.vocab;
+        std::vector<float> own;
+        float *lg = logits_out;
+        if (!lg) {
+            own.resize(rows * V);
+            lg = own.data();
+        }
+        lm_forward(m, ids, batch, t, scan_policy, lg, nullptr, nullptr, nullptr);
+        *loss_out = softmax_ce(lg, rows, V, targets);
     });
 }
 

@@ -105,6 +105,12 @@ float *orc_model_tensor_data(orc_model *m, uint64_t i);
 uint64_t orc_model_tensor_numel(const orc_model *m, uint64_t i);
 void orc_model_set_threads(orc_model *m, uint64_t threads);
 
+/* Graph::softmax_ce forward (autograd.rs:579-624): mean cross-entropy in nats
+ * over rows whose target is not 0xFFFFFFFF. */
+int orc_softmax_ce(const float *logits, uint64_t rows, uint64_t vocab, const uint32_t *targets, float *loss_out);
+/* Lm::loss (model.rs:228-234): batched forward, then softmax_ce; logits_out nullable. */
+int orc_lm_loss(const orc_model *m, const uint32_t *ids, const uint32_t *targets, uint64_t batch, uint64_t t,
+                int scan_policy, float *loss_out, float *logits_out);
 /* Batched forward (model.rs:209-226): logits [batch*t, vocab]. */
 int orc_lm_logits(const orc_model *m, const uint32_t *ids, uint64_t batch, uint64_t t,
                   int scan_policy, float *logits_out);

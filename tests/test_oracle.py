@@ -260,3 +260,39 @@ def test_normal_moments(orc):
     u = np.array([r.f32_unit() for _ in range(20000)])
     assert u.min() >= 0.0 and u.max() < 1.0 and abs(u.mean() - 0.5) < 0.01
     assert math.isfinite(float(x.sum()))
+
+
+def test_softmax_ce_restatement(orc):
+    # Graph::softmax_ce forward (autograd.rs:579-624) against an f64 numpy
+    # statement of the same sums: ignored targets, an all-ignored batch, the
+    # 1e-20 probability floor and the non-finite / out-of-range rejections.
+    rng = np.random.default_rng(7)
+    lg = rng.normal(size=(9, 13)).astype(np.float32) * 3
+    lg[4, 5] = 90.0  # one row whose other probabilities underflow the floor
+    tg = rng.integers(0, 13, size=9).astype(np.uint32)
+    tg[2] = 0xFFFFFFFF
+    tg[4] = 0
+    x = lg.astype(np.float64)
+    p = np.exp(x - x.max(1, keepdims=True))
+    p /= p.sum(1, keepdims=True)
+    keep = tg != 0xFFFFFFFF
+    ref = -np.log(np.maximum(p[np.arange(9)[keep], tg[keep]], 1e-20)).mean()
+    assert abs(orc.softmax_ce(lg, tg) - ref) < 1e-5
+    assert orc.softmax_ce(lg, np.full(9, 0xFFFFFFFF, np.uint32)) == 0.0
+    bad = lg.copy()
+    bad[0, 0] = np.inf
+    with pytest.raises(ValueError, match="finite"):
+        orc.softmax_ce(bad, tg)
+    with pytest.raises(ValueError, match="range"):
+        orc.softmax_ce(lg, np.full(9, 13, np.uint32))
+
+
+def test_lm_loss_is_softmax_ce_of_lm_logits(orc):
+    cfg = orc.LmConfig(vocab=31, d_model=16, n_layer=2, expand=2, conv_k=3, mlp_mult=2, eps=1e-5, tau_max=8.0)
+    m = orc.Model(cfg, seed=11)
+    r = orc.Rng(4)
+    ids = np.array([r.below(31) for _ in range(3 * 7)], dtype=np.uint32)
+    tg = np.roll(ids, -1)
+    loss, lg = m.loss(ids, tg, 3, 7, want_logits=True)
+    assert np.array_equal(lg, m.logits(ids, 3, 7))
+    assert loss == orc.softmax_ce(lg, tg)
