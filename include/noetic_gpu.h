@@ -222,6 +222,16 @@ nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out);
 
 /* ---------------------------------------------------------------- ops */
 
+/* scan_adjoint (scan.rs:227-260), the reverse-mode gradient of the
+ * recurrence: c_t = g_t + a_{t+1} c_{t+1} with c_T = 0, over [batch, t, d]
+ * host arrays (layout (b*t + i)*d + j); chunked = 1 uses the three-pass
+ * time-parallel form (equal to the sequential one within f32 rounding).
+ * The _device form takes device pointers and a CUDA stream. */
+nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
+                          int chunked, int device);
+nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
+                                 int chunked, void *stream);
+
 /* scan_sequential / scan_chunked (scan.rs:35-57, 98-225):
  * h[b,t,j] = a[b,t,j] * h[b,t-1,j] + b[b,t,j], h[b,-1,j] = 0, layout
  * (b*T + t)*D + j.  Host pointers; runs on `device`.  chunked != 0 selects

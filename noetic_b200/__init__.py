@@ -91,6 +91,8 @@ SIGNATURES = {
     "nk_decoder_profile_end": (_i32, [_P, C.POINTER(NkProfile)]),
     "nk_scan": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
     "nk_scan_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _P]),
+    "nk_scan_adjoint": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
+    "nk_scan_adjoint_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _P]),
     "nk_scan_chunked_noalloc_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _P]),
     "nk_sample_token": (_i32, [_P, _u64, C.POINTER(NkSampleCfg), _P, _u64, _P, _P, _i32]),
 }
@@ -453,6 +455,19 @@ def scan_sequential(a, b, batch: int, t: int, d: int, device: int = 0) -> np.nda
 def scan_chunked(a, b, batch: int, t: int, d: int, device: int = 0) -> np.ndarray:
     """scan.rs:98-225 (time-chunked associative scan) on the GPU."""
     return _scan(a, b, batch, t, d, True, device)
+
+
+def scan_adjoint(a, g, batch: int, t: int, d: int, chunked: bool = False, device: int = 0) -> np.ndarray:
+    """scan.rs:227-260 on the GPU: c_t = g_t + a_{t+1} c_{t+1}, c_T = 0; returns c
+    (flat, layout (b*T + t)*D + j); chunked selects the time-parallel form."""
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    g = np.ascontiguousarray(g, dtype=np.float32).reshape(-1)
+    n = batch * t * d
+    if a.size != n or g.size != n:
+        raise ValueError("a and g must hold batch * t * d values")
+    c = np.empty(n, dtype=np.float32)
+    _check(lib().nk_scan_adjoint(_ptr(a), _ptr(g), _ptr(c), batch, t, d, int(chunked), device))
+    return c
 
 
 def sample_token(logits: np.ndarray, cfg: SampleCfg, history, rng: np.ndarray, device: int = 0) -> int:

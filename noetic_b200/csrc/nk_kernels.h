@@ -159,6 +159,12 @@ cudaError_t history_push(uint32_t *history, uint32_t *history_len, const uint32_
                          int window, cudaStream_t st);
 
 // ---- scans (scan.cu)
+// scan_adjoint (scan.rs:227-260): c_t = g_t + a_{t+1} c_{t+1}, c_T = 0; the
+// chunked form uses the same scratch as scan_chunked.
+cudaError_t scan_adjoint_sequential(const float *a, const float *g, float *c, int64_t batch, int64_t t, int64_t d,
+                                    cudaStream_t st);
+cudaError_t scan_adjoint_chunked(const float *a, const float *g, float *c, int64_t batch, int64_t t, int64_t d,
+                                 float *scratch, cudaStream_t st);
 cudaError_t scan_sequential(const float *a, const float *b, float *h, int64_t batch, int64_t t,
                             int64_t d, cudaStream_t st);
 cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch, int64_t t,

@@ -1601,6 +1601,48 @@ nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batc
     });
 }
 
+nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
+                                 int chunked, void *stream) {
+    return guard([&] {
+        if (batch * t * d == 0) return;
+        if (!a || !g || !c) fail(NK_ERR_INVALID, "null argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        if (!chunked) {
+            cuda_check(nk::scan_adjoint_sequential(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan adjoint");
+            return;
+        }
+        float *scratch = nullptr;
+        dalloc(&scratch, nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d), "scan scratch");
+        cudaError_t e = nk::scan_adjoint_chunked(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, scratch, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cudaFree(scratch);
+        cuda_check(e, "scan adjoint");
+        cuda_check(e2, "scan adjoint sync");
+    });
+}
+
+nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
+                          int chunked, int device) {
+    return guard([&] {
+        const size_t n = batch * t * d;
+        if (n == 0) return;
+        if (!a || !g || !c) fail(NK_ERR_INVALID, "null argument");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        float *da = nullptr, *dg = nullptr, *dc = nullptr;
+        dalloc(&da, n, "adjoint a");
+        std::unique_ptr<float, void (*)(float *)> oa(da, [](float *p) { cudaFree(p); });
+        dalloc(&dg, n, "adjoint g");
+        std::unique_ptr<float, void (*)(float *)> og(dg, [](float *p) { cudaFree(p); });
+        dalloc(&dc, n, "adjoint c");
+        std::unique_ptr<float, void (*)(float *)> oc(dc, [](float *p) { cudaFree(p); });
+        cuda_check(cudaMemcpy(da, a, n * 4, cudaMemcpyHostToDevice), "upload a");
+        cuda_check(cudaMemcpy(dg, g, n * 4, cudaMemcpyHostToDevice), "upload g");
+        nk_status s = nk_scan_adjoint_device(da, dg, dc, batch, t, d, chunked, nullptr);
+        if (s != NK_OK) fail(s, g_err);
+        cuda_check(cudaMemcpy(c, dc, n * 4, cudaMemcpyDeviceToHost), "download c");
+    });
+}
+
 nk_status nk_scan(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
                   int chunked, int device) {
     return guard([&] {

@@ -1,5 +1,6 @@
 // scan.cu -- the first-order linear recurrence h_t = a_t h_{t-1} + b_t over
-// [batch, T, D] (layout (b*T + t)*D + j), scan.rs:35-225.
+// [batch, T, D] (layout (b*T + t)*D + j), scan.rs:35-225, and its adjoint
+// c_t = g_t + a_{t+1} c_{t+1} (scan.rs:227-260) in the same two forms.
 //
 // scan_sequential: one thread per (b, j) walks time; loads are coalesced
 //   along j.  Optimal when batch * D fills the GPU.
@@ -109,6 +110,103 @@ __global__ void scan_fix_k(const float *__restrict__ a, float *__restrict__ h,
     }
 }
 
+// ---- the adjoint (scan.rs:227-260): c_t = g_t + a_{t+1} c_{t+1}, c_T = 0,
+// a reverse-time scan with the multiplier one step ahead.
+
+__global__ void adj_seq_k(const float *__restrict__ a, const float *__restrict__ g, float *__restrict__ c,
+                          int64_t batch, int64_t t, int64_t d) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * d) return;
+    const int64_t bi = i / d, j = i - bi * d;
+    const size_t base = (size_t)bi * t * d + j;
+    float carry = 0.0f;
+    int64_t ti = t;
+    for (; ti >= 4; ti -= 4) {
+        const size_t o = base + (size_t)(ti - 1) * d;
+        const float g0 = g[o], g1 = g[o - d], g2 = g[o - 2 * d], g3 = g[o - 3 * d];
+        const float a0 = a[o], a1 = a[o - d], a2 = a[o - 2 * d], a3 = a[o - 3 * d];
+        float cv = g0 + carry;
+        c[o] = cv;
+        carry = a0 * cv;
+        cv = g1 + carry;
+        c[o - d] = cv;
+        carry = a1 * cv;
+        cv = g2 + carry;
+        c[o - 2 * d] = cv;
+        carry = a2 * cv;
+        cv = g3 + carry;
+        c[o - 3 * d] = cv;
+        carry = a3 * cv;
+    }
+    for (; ti > 0; --ti) {
+        const size_t o = base + (size_t)(ti - 1) * d;
+        const float cv = g[o] + carry;
+        c[o] = cv;
+        carry = a[o] * cv;
+    }
+}
+
+// Pass 1: each time block from a zero carry, walking down; the block's map
+// from the carry entering at its top to the carry leaving below its bottom
+// is X_out = A X_in + B with A the product of the block's a and B the local
+// carry leaving it.
+__global__ void adj_local_k(const float *__restrict__ a, const float *__restrict__ g, float *__restrict__ c,
+                            float *__restrict__ blkA, float *__restrict__ blkB, int64_t batch, int64_t t, int64_t d,
+                            int64_t nblk) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * nblk * d) return;
+    const int64_t j = i % d, bc = i / d;
+    const int64_t k = bc % nblk, bi = bc / nblk;
+    const int64_t t0 = k * SCAN_TB, t1 = min(t, t0 + SCAN_TB);
+    float A = 1.0f, carry = 0.0f;
+    for (int64_t ti = t1 - 1; ti >= t0; --ti) {
+        const size_t o = ((size_t)bi * t + ti) * d + j;
+        const float av = a[o];
+        const float cv = g[o] + carry;
+        c[o] = cv;
+        carry = av * cv;
+        A = A * av;
+    }
+    blkA[i] = A;
+    blkB[i] = carry;
+}
+
+// Pass 2: compose the block maps from the last block down; carry[k] is the
+// carry entering block k at its top.
+__global__ void adj_carry_k(const float *__restrict__ blkA, const float *__restrict__ blkB, float *__restrict__ carry,
+                            int64_t batch, int64_t d, int64_t nblk) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * d) return;
+    const int64_t bi = i / d, j = i - bi * d;
+    float x = 0.0f;
+    for (int64_t k = nblk - 1; k >= 0; --k) {
+        const size_t o = ((size_t)bi * nblk + k) * d + j;
+        carry[o] = x;
+        x = blkA[o] * x + blkB[o];
+    }
+}
+
+// Pass 3: c_t += (prod of a strictly between t and the block top) * carry_in,
+// walking down, stopping once the product reaches zero.
+__global__ void adj_fix_k(const float *__restrict__ a, float *__restrict__ c, const float *__restrict__ carry,
+                          int64_t batch, int64_t t, int64_t d, int64_t nblk) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * nblk * d) return;
+    const int64_t j = i % d, bc = i / d;
+    const int64_t k = bc % nblk, bi = bc / nblk;
+    if (k == nblk - 1) return;
+    const float cin = carry[i];
+    if (cin == 0.0f) return;
+    const int64_t t0 = k * SCAN_TB, t1 = min(t, t0 + SCAN_TB);
+    float P = 1.0f;
+    for (int64_t ti = t1 - 1; ti >= t0; --ti) {
+        const size_t o = ((size_t)bi * t + ti) * d + j;
+        c[o] = c[o] + P * cin;
+        P = P * a[o];
+        if (P == 0.0f) break;
+    }
+}
+
 }  // namespace
 
 size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d) {
@@ -132,6 +230,25 @@ cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch
     scan_local_k<<<blocks_for(per, 128), 128, 0, st>>>(a, b, h, blkA, blkB, batch, t, d, nblk);
     scan_carry_k<<<blocks_for(batch * d, 128), 128, 0, st>>>(blkA, blkB, carry, batch, d, nblk);
     scan_fix_k<<<blocks_for(per, 128), 128, 0, st>>>(a, h, carry, batch, t, d, nblk);
+    return cudaGetLastError();
+}
+
+cudaError_t scan_adjoint_sequential(const float *a, const float *g, float *c, int64_t batch, int64_t t, int64_t d,
+                                    cudaStream_t st) {
+    if (batch * t * d == 0) return cudaSuccess;
+    adj_seq_k<<<blocks_for(batch * d, 128), 128, 0, st>>>(a, g, c, batch, t, d);
+    return cudaGetLastError();
+}
+
+cudaError_t scan_adjoint_chunked(const float *a, const float *g, float *c, int64_t batch, int64_t t, int64_t d,
+                                 float *scratch, cudaStream_t st) {
+    if (batch * t * d == 0) return cudaSuccess;
+    const int64_t nblk = (t + SCAN_TB - 1) / SCAN_TB;
+    const int64_t per = batch * nblk * d;
+    float *blkA = scratch, *blkB = scratch + per, *carry = scratch + 2 * per;
+    adj_local_k<<<blocks_for(per, 128), 128, 0, st>>>(a, g, c, blkA, blkB, batch, t, d, nblk);
+    adj_carry_k<<<blocks_for(batch * d, 128), 128, 0, st>>>(blkA, blkB, carry, batch, d, nblk);
+    adj_fix_k<<<blocks_for(per, 128), 128, 0, st>>>(a, c, carry, batch, t, d, nblk);
     return cudaGetLastError();
 }
 

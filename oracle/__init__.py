@@ -102,6 +102,7 @@ def lib():
             "orc_argmax": (_u64, [_F, _u64]),
             "orc_scan_sequential": (None, [_F, _F, _F, _u64, _u64, _u64, _u64]),
             "orc_scan_chunked": (None, [_F, _F, _F, _u64, _u64, _u64, _u64]),
+            "orc_scan_adjoint": (None, [_F, _F, _F, _u64, _u64, _u64]),
             "orc_config_check": (C.c_int, [C.POINTER(Config)]),
             "orc_model_new": (_P, [C.POINTER(Config), C.POINTER(RngState)]),
             "orc_model_free": (None, [_P]),
@@ -373,6 +374,15 @@ def generate(model: Model, prompt, n: int, cfg: SampleCfg, rng: Rng) -> np.ndarr
 # ------------------------------------------------------------------ tensor.rs / scan.rs
 def worker_count(requested: int, jobs: int, total: int) -> int:
     return int(lib().orc_worker_count(requested, jobs, total))
+
+
+def scan_adjoint(a: np.ndarray, g: np.ndarray, batch: int, t: int, d: int) -> np.ndarray:
+    """scan_adjoint (scan.rs:235-260): c_t = g_t + a_{t+1} c_{t+1}, c_T = 0."""
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    g = np.ascontiguousarray(g, dtype=np.float32).reshape(-1)
+    c = np.empty_like(a)
+    lib().orc_scan_adjoint(a, g, c, batch, t, d)
+    return c
 
 
 def softmax_ce(logits: np.ndarray, targets: np.ndarray) -> float:

@@ -890,6 +890,25 @@ int orc_lm_logits(const orc_model *m, const uint32_t *ids, uint64_t batch, uint6
     });
 }
 
+// scan_adjoint (scan.rs:235-260): per batch row, walking time down from a
+// zero carry: c = g + carry; carry = a * c.
+void orc_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d) {
+    std::vector<float> carry(d);
+    for (uint64_t bi = 0; bi < batch; ++bi) {
+        const uint64_t base = bi * t * d;
+        std::fill(carry.begin(), carry.end(), 0.0f);
+        for (uint64_t ti = t; ti > 0;) {
+            --ti;
+            const uint64_t idx = base + ti * d;
+            for (uint64_t j = 0; j < d; ++j) {
+                const float cv = g[idx + j] + carry[j];
+                c[idx + j] = cv;
+                carry[j] = a[idx + j] * cv;
+            }
+        }
+    }
+}
+
 int orc_softmax_ce(const float *logits, uint64_t rows, uint64_t vocab, const uint32_t *targets, float *loss_out) {
     return guarded([&] { *loss_out = softmax_ce(logits, rows, vocab, targets); });
 }

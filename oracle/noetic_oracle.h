@@ -105,6 +105,8 @@ float *orc_model_tensor_data(orc_model *m, uint64_t i);
 uint64_t orc_model_tensor_numel(const orc_model *m, uint64_t i);
 void orc_model_set_threads(orc_model *m, uint64_t threads);
 
+/* scan_adjoint (scan.rs:235-260): c_t = g_t + a_{t+1} c_{t+1}, c_T = 0. */
+void orc_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d);
 /* Graph::softmax_ce forward (autograd.rs:579-624): mean cross-entropy in nats
  * over rows whose target is not 0xFFFFFFFF. */
 int orc_softmax_ce(const float *logits, uint64_t rows, uint64_t vocab, const uint32_t *targets, float *loss_out);

@@ -142,3 +142,33 @@ def test_sampling_above_the_vocab_limit_is_refused(gpu):
     x = np.zeros(V, np.float32)
     x[12345] = 1.0
     assert gpu.sample_token(x, g, [], gpu.rng_state(1)) == 12345
+
+
+@pytest.mark.parametrize("chunked", [False, True])
+def test_scan_adjoint_matches_oracle(gpu, orc, chunked):
+    # The awkward-shape table of scan.rs:269-288 plus blocks crossing 256.
+    for batch, t, d in [(1, 1, 1), (3, 7, 5), (2, 129, 3), (5, 64, 1), (1, 1024, 9), (2, 1000, 4), (1, 777, 33)]:
+        n = batch * t * d
+        rng = orc.Rng(batch * 1000 + t)
+        a = np.array([rng.f32_unit() * np.float32(0.98) + np.float32(0.01) for _ in range(n)], dtype=np.float32)
+        g = np.array([rng.normal() for _ in range(n)], dtype=np.float32)
+        ref = orc.scan_adjoint(a, g, batch, t, d)
+        got = gpu.scan_adjoint(a, g, batch, t, d, chunked=chunked)
+        assert np.abs(got - ref).max() < 1e-4, (batch, t, d, chunked)
+
+
+def test_scan_adjoint_linearity_at_size(gpu):
+    # c is linear in g: c(g1 + g2) = c(g1) + c(g2) (to f32 rounding), and the
+    # two forms agree, on a C5-sized channel count over a long sequence.
+    batch, t, d = 2, 4096, 768
+    r = np.random.default_rng(3)
+    a = (r.random(batch * t * d, dtype=np.float32) * 0.98 + 0.01).astype(np.float32)
+    g1 = r.standard_normal(batch * t * d, dtype=np.float32)
+    g2 = r.standard_normal(batch * t * d, dtype=np.float32)
+    c1 = gpu.scan_adjoint(a, g1, batch, t, d, chunked=True)
+    c2 = gpu.scan_adjoint(a, g2, batch, t, d, chunked=True)
+    c12 = gpu.scan_adjoint(a, g1 + g2, batch, t, d, chunked=True)
+    scale = np.abs(c12).max()
+    assert np.abs(c12 - (c1 + c2)).max() <= 1e-5 * scale
+    cs = gpu.scan_adjoint(a, g1, batch, t, d, chunked=False)
+    assert np.abs(cs - c1).max() <= 1e-4 * np.abs(cs).max()

@@ -296,3 +296,23 @@ def test_lm_loss_is_softmax_ce_of_lm_logits(orc):
     loss, lg = m.loss(ids, tg, 3, 7, want_logits=True)
     assert np.array_equal(lg, m.logits(ids, 3, 7))
     assert loss == orc.softmax_ce(lg, tg)
+
+
+def test_scan_adjoint_closed_form(orc):
+    # scan.rs:291-315: c_t = sum_{s >= t} g_s prod_{r=t+1..s} a_r, with the
+    # reference's draws (Rng::new(5): a = f32_unit, then g = normal).
+    batch, t, d = 2, 6, 2
+    n = batch * t * d
+    rng = orc.Rng(5)
+    a = np.array([rng.f32_unit() for _ in range(n)], dtype=np.float32)
+    g = np.array([rng.normal() for _ in range(n)], dtype=np.float32)
+    c = orc.scan_adjoint(a, g, batch, t, d)
+    for bi in range(batch):
+        for j in range(d):
+            for ti in range(t):
+                exp, prod = np.float32(0.0), np.float32(1.0)
+                for s in range(ti, t):
+                    if s > ti:
+                        prod = np.float32(prod * a[(bi * t + s) * d + j])
+                    exp = np.float32(exp + g[(bi * t + s) * d + j] * prod)
+                assert abs(exp - c[(bi * t + ti) * d + j]) < 1e-4
