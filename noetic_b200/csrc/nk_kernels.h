@@ -133,12 +133,33 @@ int small_logit_tiles(int V);
 cudaError_t small_step(const SmallStepArgs &a, cudaStream_t st, int *launches);
 
 // ---- the whole decode step for 1..4 streams as one persistent cooperative
-// kernel (decode_persistent.cu).  layers_dev: device copy of a.layers;
-// sync: two device words, zeroed by the launch; a.best_val / best_idx hold
-// persistent_partials() entries per stream.
+// kernel (decode_persistent.cu): two grid barriers per layer, the out and
+// down projections read transposed (out_wT [E][d], down_wT [H][d]).
+struct PersistLayer {
+    const float *n1, *in_w, *in_b, *conv_w, *conv_b, *out_wT, *out_b, *n2, *up_w, *up_b, *down_wT, *down_b;
+};
+struct PersistStepArgs {
+    const uint32_t *tokens;  // device [M]
+    uint32_t *tokens_out;    // device [M] greedy choice, nullable
+    const float *emb, *norm_f;
+    float eps;
+    float *state;            // [L][M][k+1][E]
+    uint32_t *heads;
+    float *logits;           // [M,V] nullable
+    float *best_val;         // [M, persistent_partials()]
+    uint32_t *best_idx;
+    int *err;
+    void *ws;                // persistent_ws_bytes(d): zero before the first launch and after an
+                             // error; every completed launch leaves it zero
+    const PersistLayer *layers;  // device array [n_layer]
+    int M, d, E, H, k, V, n_layer;
+};
 bool persistent_step_supported(int M, int d, int E, int H, int k, int V, int n_layer);
 int persistent_partials();
-cudaError_t persistent_step(const SmallStepArgs &a, const SmallLayer *layers_dev, uint32_t *sync, cudaStream_t st);
+size_t persistent_ws_bytes(int d);
+cudaError_t persistent_step(const PersistStepArgs &a, cudaStream_t st);
+// out[c][r] = in[r][c] for in [rows, cols] row-major.
+cudaError_t transpose(const float *in, float *out, int rows, int cols, cudaStream_t st);
 
 // ---- sampler (sampler.cu): sample_token for every row.
 struct SampleParams {

@@ -167,6 +167,9 @@ struct nk_model {
     size_t arena_floats = 0;
     bool dirty = true;
     nk::TcWeights tc;  // tensor-core operand forms (built with the arena)
+    // out_w and down_w of every layer stored transposed ([E][d], [H][d] per
+    // layer) for the persistent step kernel, built on first use
+    float *wT = nullptr;
 
     uint64_t d() const { return cfg.d_model; }
     uint64_t e() const { return cfg.d_model * cfg.expand; }
@@ -263,14 +266,22 @@ struct nk_model {
                                   cudaMemcpyHostToDevice),
                        "cudaMemcpy(weights)");
         nk::tc_weights_free(tc);
+        free_transposed();
         dirty = false;
     }
+
+    void free_transposed() {
+        if (wT) cudaFree(wT);
+        wT = nullptr;
+    }
+    size_t wT_layer_floats() const { return (size_t)(e() + hidden()) * d(); }
 
     ~nk_model() {
         if (arena) {
             cudaSetDevice(device);
             cudaFree(arena);
         }
+        free_transposed();
         if (device < 0) return;
         nk::tc_weights_free(tc);
     }
@@ -445,14 +456,16 @@ struct nk_decoder {
     // small-batch engine: layer pointers and CUDA graphs of the greedy step,
     // one per (tokens in, tokens out) device buffer pair
     std::vector<nk::SmallLayer> small_layers;
-    // persistent step kernel: device copy of the layer pointers, barrier words
     // stream-K workspace of the tensor-core projections (counters zeroed)
     float *ksplit_ws = nullptr;
     int *ksplit_flags = nullptr;
     static constexpr int KSPLIT_FLAGS = 4096;
-    nk::SmallLayer *layers_dev = nullptr;
-    const float *layers_arena = nullptr;  // model arena the layer tables point into
-    uint32_t *sync = nullptr;
+    const float *layers_arena = nullptr;  // model arena the small-batch layer table points into
+    // persistent step kernel: device layer table (keyed on the model's
+    // transposed weights), accumulators and barrier words
+    nk::PersistLayer *players_dev = nullptr;
+    const float *players_key = nullptr;
+    uint8_t *pws = nullptr;
     struct StepGraph {
         const uint32_t *in;
         uint32_t *out;
@@ -483,7 +496,7 @@ struct nk_decoder {
                         (void *)p_lens})
             if (p) cudaFree(p);
         for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo,
-                        (void *)layers_dev, (void *)sync, (void *)ksplit_ws, (void *)ksplit_flags})
+                        (void *)players_dev, (void *)pws, (void *)ksplit_ws, (void *)ksplit_flags})
             if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         for (auto &gph : graphs) cudaGraphExecDestroy(gph.exec);
@@ -645,6 +658,8 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
     }
 }
 
+bool use_persistent(const nk_decoder *dec);
+
 void ensure_ready(nk_decoder *dec) {
     nk_model *m = dec->model;
     cuda_check(cudaSetDevice(m->device), "cudaSetDevice");
@@ -664,19 +679,47 @@ void ensure_ready(nk_decoder *dec) {
         cuda_check(nk::tc_weights_build(m->tc, srcs), "tensor-core weight split");
     }
     if (dec->layers_arena != m->arena) {
-        // Per-layer weight pointers for the few-stream engines, host and
-        // device copies; the arena exists only after the first upload.
+        // Per-layer weight pointers for the small-batch engine; the arena
+        // exists only after the first upload.
         dec->small_layers.clear();
         for (const LayerIx &L : m->layers)
             dec->small_layers.push_back({m->dp(L.n1), m->dp(L.in_w), m->dp(L.in_b), m->dp(L.conv_w), m->dp(L.conv_b),
                                          m->dp(L.out_w), m->dp(L.out_b), m->dp(L.n2), m->dp(L.up_w), m->dp(L.up_b),
                                          m->dp(L.down_w), m->dp(L.down_b)});
-        cuda_check(cudaMemcpyAsync(dec->layers_dev, dec->small_layers.data(),
-                                   dec->small_layers.size() * sizeof(nk::SmallLayer), cudaMemcpyHostToDevice,
-                                   dec->stream),
-                   "upload layer table");
-        cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         dec->layers_arena = m->arena;
+    }
+    if (use_persistent(dec)) {
+        // The persistent kernel reads out_w and down_w transposed: built once
+        // per weight upload, shared by every decoder of the model.
+        const size_t per = m->wT_layer_floats();
+        const int d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden();
+        if (!m->wT) {
+            cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+            cuda_check(cudaMalloc(&m->wT, std::max<size_t>(per * m->layers.size(), 1) * sizeof(float)),
+                       "cudaMalloc(transposed weights)");
+            for (size_t l = 0; l < m->layers.size(); ++l) {
+                const LayerIx &L = m->layers[l];
+                float *dst = m->wT + l * per;
+                cuda_check(nk::transpose(m->dp(L.out_w), dst, d, E, dec->stream), "transpose out_w");
+                cuda_check(nk::transpose(m->dp(L.down_w), dst + (size_t)E * d, d, H, dec->stream), "transpose down_w");
+            }
+            cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+        }
+        if (dec->players_key != m->wT) {
+            std::vector<nk::PersistLayer> tab;
+            for (size_t l = 0; l < m->layers.size(); ++l) {
+                const LayerIx &L = m->layers[l];
+                const float *t = m->wT + l * per;
+                tab.push_back({m->dp(L.n1), m->dp(L.in_w), m->dp(L.in_b), m->dp(L.conv_w), m->dp(L.conv_b), t,
+                               m->dp(L.out_b), m->dp(L.n2), m->dp(L.up_w), m->dp(L.up_b), t + (size_t)E * d,
+                               m->dp(L.down_b)});
+            }
+            cuda_check(cudaMemcpyAsync(dec->players_dev, tab.data(), tab.size() * sizeof(nk::PersistLayer),
+                                       cudaMemcpyHostToDevice, dec->stream),
+                       "upload layer table");
+            cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+            dec->players_key = m->wT;
+        }
     }
 }
 
@@ -688,6 +731,11 @@ void check_err_flag(nk_decoder *dec) {
     cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
     if (h) {
         cuda_check(cudaMemsetAsync(dec->err, 0, sizeof(int), dec->stream), "clear error flag");
+        // A persistent step that stopped early may leave its accumulators
+        // and barrier words set.
+        if (dec->pws)
+            cuda_check(cudaMemsetAsync(dec->pws, 0, nk::persistent_ws_bytes((int)dec->model->d()), dec->stream),
+                       "clear persistent workspace");
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
                                 ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 105-108 CTA-pair pipeline wait expired, 111-113 "
@@ -739,7 +787,28 @@ bool use_persistent(const nk_decoder *dec) {
 void small_step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
     const nk::SmallStepArgs a = small_args(dec, tokens, tokens_out, want_logits);
     if (use_persistent(dec)) {
-        cuda_check(nk::persistent_step(a, dec->layers_dev, dec->sync, dec->stream), "persistent decode step");
+        nk::PersistStepArgs pa{};
+        pa.tokens = a.tokens;
+        pa.tokens_out = a.tokens_out;
+        pa.emb = a.emb;
+        pa.norm_f = a.norm_f;
+        pa.eps = a.eps;
+        pa.state = a.state;
+        pa.heads = a.heads;
+        pa.logits = a.logits;
+        pa.best_val = a.best_val;
+        pa.best_idx = a.best_idx;
+        pa.err = a.err;
+        pa.ws = dec->pws;
+        pa.layers = dec->players_dev;
+        pa.M = a.M;
+        pa.d = a.d;
+        pa.E = a.E;
+        pa.H = a.H;
+        pa.k = a.k;
+        pa.V = a.V;
+        pa.n_layer = a.n_layer;
+        cuda_check(nk::persistent_step(pa, dec->stream), "persistent decode step");
         dec->launches += 1;
         return;
     }
@@ -1195,11 +1264,12 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         dalloc(&dec->tok_a, S, "tokens");
         dalloc(&dec->tok_b, S, "tokens");
         dalloc(&dec->err, 1, "error flag");
-        dalloc(&dec->sync, 2, "barrier words");
+        dalloc(&dec->pws, nk::persistent_ws_bytes((int)d), "persistent step workspace");
+        cuda_check(cudaMemset(dec->pws, 0, nk::persistent_ws_bytes((int)d)), "memset");
         dalloc(&dec->ksplit_ws, nk::tc_stream_k_ws_floats(), "stream-K workspace");
         dalloc(&dec->ksplit_flags, nk_decoder::KSPLIT_FLAGS, "stream-K counters");
         cuda_check(cudaMemset(dec->ksplit_flags, 0, nk_decoder::KSPLIT_FLAGS * sizeof(int)), "memset");
-        dalloc(&dec->layers_dev, model->cfg.n_layer, "layer table");
+        dalloc(&dec->players_dev, model->cfg.n_layer, "layer table");
         dalloc(&dec->rng, S * 4, "rng");
         cuda_check(cudaMemset(dec->err, 0, sizeof(int)), "memset");
         cuda_check(cudaMemset(dec->logits, 0, S * V * sizeof(float)), "memset");
