@@ -191,16 +191,17 @@ nk_status nk_decoder_cuda_stream(nk_decoder *dec, void **stream);
 nk_status nk_decoder_sync(nk_decoder *dec);
 
 /* Engine flags: 0 = automatic (tensor-core 3xTF32 projections where the
- * shape allows it; the fused small-batch step for <= 8 streams).  Bit 0: f32
+ * shape allows it; for 1-4 streams the whole step as one persistent
+ * cooperative kernel, for <= 8 streams the fused small-batch step).  Bit 0: f32
  * CUDA-core projections only.  Bit 1 / bit 2: force the time-chunked /
  * sequential prefill scan.  Bit 3: no fused small-batch step.  Bits 4 / 5:
  * tensor-core tiles 128 / 256 columns wide (default: 256 while the grid
- * covers every SM twice, else 128).  Bit 6: for 1-4 streams, the whole step
- * as one persistent cooperative kernel instead of the fused small-batch
- * kernels.  Bit 7: the CTA-pair projection kernel (256 x 256 tiles on two
+ * covers every SM twice, else 128).  Bit 6: the persistent step kernel for
+ * 1-4 streams (the default; kept for compatibility).  Bit 7: the CTA-pair projection kernel (256 x 256 tiles on two
  * SMs) wherever N >= 256.  Bit 8: whole tiles per CTA instead of stream-K
  * (equal K-block ranges per SM, partial tiles summed in a fixed order).
- * Bit 9: no L2 cache policies on projection loads and stores. */
+ * Bit 9: no L2 cache policies on projection loads and stores.  Bit 10: no
+ * persistent step kernel (1-4 streams take the fused small-batch kernels). */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

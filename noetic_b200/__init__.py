@@ -330,7 +330,9 @@ class Decoder:
 
     def set_engine(self, engine: int):
         """0 = automatic; bit 0 = f32 CUDA-core projections only; bit 1 / bit 2
-        force the time-chunked / sequential prefill scan."""
+        force the time-chunked / sequential prefill scan; bit 3 no fused
+        few-stream step; bit 10 no persistent step kernel (1-4 streams take
+        the fused small-batch kernels).  The C header lists every bit."""
         _check(lib().nk_decoder_set_engine(self.h, engine))
 
     def reset(self, first: int = 0, count: int | None = None):

@@ -779,7 +779,7 @@ nk::SmallStepArgs small_args(nk_decoder *dec, const uint32_t *tokens, uint32_t *
 
 bool use_persistent(const nk_decoder *dec) {
     const nk_model *m = dec->model;
-    return (dec->engine & 64) && !(dec->engine & 8) &&
+    return !(dec->engine & 1024) && !(dec->engine & 8) &&
            nk::persistent_step_supported((int)dec->S, (int)m->d(), (int)m->e(), (int)m->hidden(), (int)m->k(),
                                          (int)m->cfg.vocab, (int)m->cfg.n_layer);
 }
@@ -1602,7 +1602,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 1023) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 2047) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

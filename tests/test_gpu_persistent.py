@@ -1,6 +1,7 @@
-"""The single persistent decode-step kernel (engine bit 6, 1..4 streams:
-weights streamed through a shared-memory ring, grid barriers between
-phases) against the oracle and against the multi-kernel small-batch step."""
+"""The single persistent decode-step kernel (the default for 1..4 streams:
+weights streamed through a shared-memory ring, two grid barriers per layer,
+a fixed-point residual accumulator) against the oracle and against the
+multi-kernel small-batch step (engine bit 10)."""
 
 import numpy as np
 import pytest
@@ -9,7 +10,8 @@ from conftest import c1_cfg, same_model, state_rel_err, tiny_cfg
 
 pytestmark = pytest.mark.gpu
 
-PERSISTENT = 64  # engine bit: the whole step as one persistent kernel
+PERSISTENT = 64  # engine bit: the whole step as one persistent kernel (default)
+MULTI = 1024  # engine bit: no persistent kernel
 
 
 def _run_both(gpu, orc, kw, S, T, seed, base):
@@ -19,6 +21,7 @@ def _run_both(gpu, orc, kw, S, T, seed, base):
     ids = uniform_prompts(S, T, kw["vocab"], base)
     pers, multi = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
     pers.set_engine(PERSISTENT)
+    multi.set_engine(MULTI)
     ods = [orc.Decoder(om) for _ in range(S)]
     worst_o = worst_m = 0.0
     for t in range(T):
@@ -101,6 +104,7 @@ def test_persistent_matches_fused_greedy_tokens(gpu, orc):
     _, gm = same_model(orc, gpu, kw, seed=1)
     a, b = gpu.Decoder(gm, 4), gpu.Decoder(gm, 4)
     a.set_engine(PERSISTENT)
+    b.set_engine(MULTI)
     ta = tb = np.array([1, 2, 3, 4], dtype=np.uint32)
     agree = 0
     for _ in range(16):

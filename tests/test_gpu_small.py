@@ -10,6 +10,7 @@ from conftest import c1_cfg, same_model, state_rel_err, tiny_cfg
 pytestmark = pytest.mark.gpu
 
 UNFUSED = 8  # engine bit: no fused small-batch step
+SMALL = 1024  # engine bit: no persistent step kernel (the fused small-batch kernels)
 
 
 @pytest.mark.parametrize("S", [1, 3, 8])
@@ -20,6 +21,7 @@ def test_small_batch_step_matches_oracle_and_unfused(gpu, orc, S):
 
     ids = uniform_prompts(S, 6, kw["vocab"], 40)
     fused, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    fused.set_engine(SMALL)
     plain.set_engine(UNFUSED)
     ods = [orc.Decoder(om) for _ in range(S)]
     for t in range(6):
@@ -40,6 +42,7 @@ def test_graph_replayed_greedy_steps_follow_the_oracle(gpu, orc):
     om, gm = same_model(orc, gpu, kw, seed=0)
     S = 2
     dec = gpu.Decoder(gm, S)
+    dec.set_engine(SMALL)
     ods = [orc.Decoder(om) for _ in range(S)]
     toks = np.array([17, 900], dtype=np.uint32)
     checked = 0
@@ -63,6 +66,7 @@ def test_small_batch_awkward_shapes(gpu, orc):
         om, gm = same_model(orc, gpu, kw, seed=3)
         S = 3
         dec = gpu.Decoder(gm, S)
+        dec.set_engine(SMALL)
         ods = [orc.Decoder(om) for _ in range(S)]
         for t in range(5):
             tok = np.array([(t * 7 + s) % kw["vocab"] for s in range(S)], dtype=np.uint32)
