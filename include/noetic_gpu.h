@@ -233,6 +233,44 @@ nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t bat
 nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
                                  int chunked, void *stream);
 
+/* gemm_tn (tensor.rs:156-198): C[m, n] = A[p, m]^T B[p, n], the weight-
+ * gradient product; a zero element of A skips its product as kern_tn does.
+ * Host arrays, run on `device`; the _device form takes device pointers and a
+ * CUDA stream.  m < 2^22, n < 2^31. */
+nk_status nk_gemm_tn(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n, int device);
+nk_status nk_gemm_tn_device(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n,
+                            void *stream);
+
+/* Op::DwConv backward (autograd.rs:1050-1097) of y[b,t,j] = bias[j] +
+ * sum_{q < min(t+1, k)} w[q,j] x[b,t-q,j]: the gradients ADD into gx
+ * [batch*t*d], gw [k*d] and gb [d] (each nullable, as Graph::backward
+ * accumulates).  gx follows the reference's order bit for bit; gw and gb are
+ * sums over batch*t rows in a fixed blocked order (deterministic, equal to
+ * the sequential sums within f32 rounding).  k <= 16.  Host arrays on
+ * `device`; the _device form takes device pointers and a CUDA stream. */
+nk_status nk_dwconv_backward(const float *x, const float *w, const float *go, float *gx, float *gw, float *gb,
+                             uint64_t batch, uint64_t t, uint64_t d, uint64_t k, int device);
+nk_status nk_dwconv_backward_device(const float *x, const float *w, const float *go, float *gx, float *gw,
+                                    float *gb, uint64_t batch, uint64_t t, uint64_t d, uint64_t k, void *stream);
+
+/* AdamW::step (optim.rs:33-72) for one parameter tensor and its moments: t
+ * is the step counter after its increment (>= 1), decay the parameter's
+ * Param::decay.  Bit-identical to the reference's f32 arithmetic.  Invalid
+ * hyper-parameters are refused before any work; a non-finite gradient or
+ * parameter returns NK_ERR_INVALID (the reference asserts), with that
+ * element untouched and the others updated.  Host arrays on `device`; the
+ * _device form takes device pointers and a CUDA stream (synchronous: it
+ * reads the error flag). */
+typedef struct nk_adamw_cfg {
+    float lr, b1, b2, eps, wd; /* AdamW::new defaults: b1 0.9, b2 0.95, eps 1e-8 */
+    uint64_t t;
+    int decay;
+} nk_adamw_cfg;
+nk_status nk_adamw_step(float *val, const float *grad, float *m, float *v, uint64_t n, const nk_adamw_cfg *cfg,
+                        int device);
+nk_status nk_adamw_step_device(float *val, const float *grad, float *m, float *v, uint64_t n,
+                               const nk_adamw_cfg *cfg, void *stream);
+
 /* scan_sequential / scan_chunked (scan.rs:35-57, 98-225):
  * h[b,t,j] = a[b,t,j] * h[b,t-1,j] + b[b,t,j], h[b,-1,j] = 0, layout
  * (b*T + t)*D + j.  Host pointers; runs on `device`.  chunked != 0 selects

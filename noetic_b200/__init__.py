@@ -51,6 +51,11 @@ class NkSampleCfg(C.Structure):
                 ("rep_window", _u64), ("greedy", _u32)]
 
 
+class NkAdamwCfg(C.Structure):
+    _fields_ = [("lr", _f32), ("b1", _f32), ("b2", _f32), ("eps", _f32), ("wd", _f32), ("t", _u64),
+                ("decay", _i32)]
+
+
 class NkProfile(C.Structure):
     _fields_ = [("proj_ms", C.c_double), ("proj_launches", _u64), ("proj_flops", C.c_double),
                 ("proj_bytes", C.c_double), ("launches", _u64), ("tensor_core", _i32)]
@@ -92,6 +97,12 @@ SIGNATURES = {
     "nk_scan": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
     "nk_scan_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _P]),
     "nk_scan_adjoint": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
+    "nk_gemm_tn": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32]),
+    "nk_gemm_tn_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _P]),
+    "nk_dwconv_backward": (_i32, [_P, _P, _P, _P, _P, _P, _u64, _u64, _u64, _u64, _i32]),
+    "nk_dwconv_backward_device": (_i32, [_P, _P, _P, _P, _P, _P, _u64, _u64, _u64, _u64, _P]),
+    "nk_adamw_step": (_i32, [_P, _P, _P, _P, _u64, C.POINTER(NkAdamwCfg), _i32]),
+    "nk_adamw_step_device": (_i32, [_P, _P, _P, _P, _u64, C.POINTER(NkAdamwCfg), _P]),
     "nk_scan_adjoint_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _P]),
     "nk_scan_chunked_noalloc_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _P]),
     "nk_sample_token": (_i32, [_P, _u64, C.POINTER(NkSampleCfg), _P, _u64, _P, _P, _i32]),
@@ -470,6 +481,50 @@ def scan_adjoint(a, g, batch: int, t: int, d: int, chunked: bool = False, device
     c = np.empty(n, dtype=np.float32)
     _check(lib().nk_scan_adjoint(_ptr(a), _ptr(g), _ptr(c), batch, t, d, int(chunked), device))
     return c
+
+
+def gemm_tn(a, b, p: int, m: int, n: int, device: int = 0) -> np.ndarray:
+    """tensor.rs:156-198 on the GPU: C[m, n] = A[p, m]^T B[p, n]."""
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    b = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
+    if a.size != p * m or b.size != p * n:
+        raise ValueError("a must hold p * m values and b p * n")
+    c = np.empty(m * n, dtype=np.float32)
+    _check(lib().nk_gemm_tn(_ptr(a), _ptr(b), _ptr(c), p, m, n, device))
+    return c.reshape(m, n)
+
+
+def dwconv_backward(x, w, go, batch: int, t: int, d: int, k: int, gx=None, gw=None, gb=None, device: int = 0):
+    """Op::DwConv backward (autograd.rs:1050-1097) on the GPU: the gradients
+    add into copies of gx / gw / gb (zeros when None); returns (gx, gw, gb)."""
+    n = batch * t * d
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+    go = np.ascontiguousarray(go, dtype=np.float32).reshape(-1)
+    if x.size != n or go.size != n or w.size != k * d:
+        raise ValueError("x and go must hold batch * t * d values and w k * d")
+    gx = np.zeros(n, np.float32) if gx is None else np.array(gx, dtype=np.float32).reshape(-1)
+    gw = np.zeros(k * d, np.float32) if gw is None else np.array(gw, dtype=np.float32).reshape(-1)
+    gb = np.zeros(d, np.float32) if gb is None else np.array(gb, dtype=np.float32).reshape(-1)
+    _check(lib().nk_dwconv_backward(_ptr(x), _ptr(w), _ptr(go), _ptr(gx), _ptr(gw), _ptr(gb), batch, t, d, k,
+                                    device))
+    return gx, gw, gb
+
+
+def adamw_step(val, grad, m, v, lr: float, t: int, decay: bool = True, b1: float = 0.9, b2: float = 0.95,
+               eps: float = 1e-8, wd: float = 0.0, device: int = 0):
+    """AdamW::step (optim.rs:33-72) on the GPU for copies of one parameter
+    tensor and its moments; t is the step counter after the increment.
+    Returns (val, m, v)."""
+    val = np.array(val, dtype=np.float32).reshape(-1)
+    m = np.array(m, dtype=np.float32).reshape(-1)
+    v = np.array(v, dtype=np.float32).reshape(-1)
+    grad = np.ascontiguousarray(grad, dtype=np.float32).reshape(-1)
+    if not (grad.size == val.size == m.size == v.size):
+        raise ValueError("val, grad, m and v must have the same size")
+    cfg = NkAdamwCfg(lr, b1, b2, eps, wd, t, int(decay))
+    _check(lib().nk_adamw_step(_ptr(val), _ptr(grad), _ptr(m), _ptr(v), val.size, C.byref(cfg), device))
+    return val, m, v
 
 
 def sample_token(logits: np.ndarray, cfg: SampleCfg, history, rng: np.ndarray, device: int = 0) -> int:

@@ -192,6 +192,25 @@ cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch
                          int64_t d, float *scratch, cudaStream_t st);
 size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d);
 
+// ---- training-side ops (train.cu)
+// gemm_tn (tensor.rs:156-198): C[m, n] = A[p, m]^T B[p, n].
+cudaError_t gemm_tn(const float *a, const float *b, float *c, int64_t p, int m, int n, cudaStream_t st);
+// Op::DwConv backward (autograd.rs:1050-1097): accumulates into gx [batch*t, d],
+// gw [k, d], gb [d] (each nullable); scratch holds
+// dwconv_backward_scratch_floats() floats when gw or gb is given; k <= dwconv_max_k().
+cudaError_t dwconv_backward(const float *x, const float *w, const float *go, float *gx, float *gw, float *gb,
+                            int64_t batch, int64_t t, int d, int k, float *scratch, cudaStream_t st);
+size_t dwconv_backward_scratch_floats(int64_t rows, int d, int k);
+int dwconv_max_k();
+// AdamW::step (optim.rs:33-72) for one parameter tensor; the bias corrections
+// 1 / (1 - b^t) come from the host.  A non-finite gradient or parameter sets *err = 4.
+struct AdamwParams {
+    float lr, b1, b2, eps, wd, inv_bc1, inv_bc2;
+    int decay;
+};
+cudaError_t adamw_step(float *val, const float *grad, float *m, float *v, int64_t n, const AdamwParams &a, int *err,
+                       cudaStream_t st);
+
 // Sets the thread-local message that nk_last_error() returns.
 void set_last_error(const std::string &msg);
 

@@ -1691,6 +1691,159 @@ nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint6
     });
 }
 
+// ---------------------------------------------------------------- training-side ops
+
+nk_status nk_gemm_tn_device(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n,
+                            void *stream) {
+    return guard([&] {
+        if (m == 0 || n == 0) return;
+        if (!c || (p && (!a || !b))) fail(NK_ERR_INVALID, "null argument");
+        if (m >= (1ull << 22) || n >= (1ull << 31) || p >= (1ull << 62)) fail(NK_ERR_INVALID, "gemm_tn shape too large");
+        cuda_check(nk::gemm_tn(a, b, c, (int64_t)p, (int)m, (int)n, (cudaStream_t)stream), "gemm_tn");
+    });
+}
+
+nk_status nk_gemm_tn(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n, int device) {
+    return guard([&] {
+        if (m == 0 || n == 0) return;
+        if (!c || (p && (!a || !b))) fail(NK_ERR_INVALID, "null argument");
+        if (m >= (1ull << 22) || n >= (1ull << 31) || p >= (1ull << 62)) fail(NK_ERR_INVALID, "gemm_tn shape too large");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        float *da = nullptr, *db = nullptr, *dc = nullptr;
+        dalloc(&da, p * m, "gemm_tn a");
+        std::unique_ptr<float, void (*)(float *)> oa(da, [](float *q) { cudaFree(q); });
+        dalloc(&db, p * n, "gemm_tn b");
+        std::unique_ptr<float, void (*)(float *)> ob(db, [](float *q) { cudaFree(q); });
+        dalloc(&dc, m * n, "gemm_tn c");
+        std::unique_ptr<float, void (*)(float *)> oc(dc, [](float *q) { cudaFree(q); });
+        if (p) {
+            cuda_check(cudaMemcpy(da, a, p * m * 4, cudaMemcpyHostToDevice), "upload a");
+            cuda_check(cudaMemcpy(db, b, p * n * 4, cudaMemcpyHostToDevice), "upload b");
+        }
+        nk_status st = nk_gemm_tn_device(da, db, dc, p, m, n, nullptr);
+        if (st != NK_OK) fail(st, g_err);
+        cuda_check(cudaMemcpy(c, dc, m * n * 4, cudaMemcpyDeviceToHost), "download c");
+    });
+}
+
+nk_status nk_dwconv_backward_device(const float *x, const float *w, const float *go, float *gx, float *gw,
+                                    float *gb, uint64_t batch, uint64_t t, uint64_t d, uint64_t k, void *stream) {
+    return guard([&] {
+        if (d == 0 || k == 0) fail(NK_ERR_INVALID, "dwconv: width and kernel width must be positive");
+        if (k > (uint64_t)nk::dwconv_max_k()) fail(NK_ERR_INVALID, "dwconv backward: kernel width above 16");
+        if (d >= (1ull << 21)) fail(NK_ERR_INVALID, "dwconv backward: width too large");
+        const uint64_t rows = batch * t;
+        if (rows == 0 || (!gx && !gw && !gb)) return;
+        if (!go || (gx && !w) || (gw && !x)) fail(NK_ERR_INVALID, "null argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        float *scratch = nullptr;
+        if (gw || gb) dalloc(&scratch, nk::dwconv_backward_scratch_floats((int64_t)rows, (int)d, (int)k), "dwconv scratch");
+        cudaError_t e = nk::dwconv_backward(x, w, go, gx, gw, gb, (int64_t)batch, (int64_t)t, (int)d, (int)k, scratch, st);
+        cudaError_t e2 = scratch ? cudaStreamSynchronize(st) : cudaSuccess;
+        if (scratch) cudaFree(scratch);
+        cuda_check(e, "dwconv backward");
+        cuda_check(e2, "dwconv backward sync");
+    });
+}
+
+nk_status nk_dwconv_backward(const float *x, const float *w, const float *go, float *gx, float *gw, float *gb,
+                             uint64_t batch, uint64_t t, uint64_t d, uint64_t k, int device) {
+    return guard([&] {
+        if (d == 0 || k == 0) fail(NK_ERR_INVALID, "dwconv: width and kernel width must be positive");
+        if (k > (uint64_t)nk::dwconv_max_k()) fail(NK_ERR_INVALID, "dwconv backward: kernel width above 16");
+        if (d >= (1ull << 21)) fail(NK_ERR_INVALID, "dwconv backward: width too large");
+        const uint64_t n = batch * t * d;
+        if (n == 0 || (!gx && !gw && !gb)) return;
+        if (!go || (gx && !w) || (gw && !x)) fail(NK_ERR_INVALID, "null argument");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        std::vector<std::unique_ptr<float, void (*)(float *)>> own;
+        auto up = [&](const float *h, size_t cnt, const char *what) -> float * {
+            if (!h) return nullptr;
+            float *dp = nullptr;
+            dalloc(&dp, cnt, what);
+            own.emplace_back(dp, [](float *q) { cudaFree(q); });
+            cuda_check(cudaMemcpy(dp, h, cnt * 4, cudaMemcpyHostToDevice), what);
+            return dp;
+        };
+        float *dx = gw ? up(x, n, "dwconv x") : nullptr;
+        float *dw = gx ? up(w, k * d, "dwconv w") : nullptr;
+        float *dgo = up(go, n, "dwconv go");
+        float *dgx = up(gx, n, "dwconv gx"), *dgw = up(gw, k * d, "dwconv gw"), *dgb = up(gb, d, "dwconv gb");
+        nk_status st = nk_dwconv_backward_device(dx, dw, dgo, dgx, dgw, dgb, batch, t, d, k, nullptr);
+        if (st != NK_OK) fail(st, g_err);
+        if (gx) cuda_check(cudaMemcpy(gx, dgx, n * 4, cudaMemcpyDeviceToHost), "download gx");
+        if (gw) cuda_check(cudaMemcpy(gw, dgw, k * d * 4, cudaMemcpyDeviceToHost), "download gw");
+        if (gb) cuda_check(cudaMemcpy(gb, dgb, d * 4, cudaMemcpyDeviceToHost), "download gb");
+    });
+}
+
+namespace {
+// AdamW::step's checks and bias corrections (optim.rs:35-47), on the host.
+nk::AdamwParams adamw_params(const nk_adamw_cfg *cfg) {
+    if (!cfg) fail(NK_ERR_INVALID, "null AdamW configuration");
+    const nk_adamw_cfg &c = *cfg;
+    if (!(std::isfinite(c.lr) && c.lr >= 0.0f)) fail(NK_ERR_INVALID, "AdamW learning rate must be finite and non-negative");
+    if (!(std::isfinite(c.b1) && c.b1 >= 0.0f && c.b1 < 1.0f)) fail(NK_ERR_INVALID, "AdamW beta1 must be in [0, 1)");
+    if (!(std::isfinite(c.b2) && c.b2 >= 0.0f && c.b2 < 1.0f)) fail(NK_ERR_INVALID, "AdamW beta2 must be in [0, 1)");
+    if (!(std::isfinite(c.eps) && c.eps > 0.0f)) fail(NK_ERR_INVALID, "AdamW epsilon must be finite and positive");
+    if (!(std::isfinite(c.wd) && c.wd >= 0.0f)) fail(NK_ERR_INVALID, "AdamW weight decay must be finite and non-negative");
+    if (c.t == 0) fail(NK_ERR_INVALID, "AdamW step counter must be at least 1");
+    const float tf = (float)c.t;
+    const float bc1 = 1.0f - powf(c.b1, tf), bc2 = 1.0f - powf(c.b2, tf);
+    return nk::AdamwParams{c.lr, c.b1, c.b2, c.eps, c.wd, 1.0f / bc1, 1.0f / bc2, c.decay ? 1 : 0};
+}
+}  // namespace
+
+nk_status nk_adamw_step_device(float *val, const float *grad, float *m, float *v, uint64_t n,
+                               const nk_adamw_cfg *cfg, void *stream) {
+    return guard([&] {
+        const nk::AdamwParams a = adamw_params(cfg);
+        if (n == 0) return;
+        if (!val || !grad || !m || !v) fail(NK_ERR_INVALID, "null argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        int *de = nullptr;
+        dalloc(&de, 1, "error flag");
+        std::unique_ptr<int, void (*)(int *)> oe(de, [](int *q) { cudaFree(q); });
+        cuda_check(cudaMemsetAsync(de, 0, sizeof(int), st), "memset");
+        cuda_check(nk::adamw_step(val, grad, m, v, (int64_t)n, a, de, st), "adamw");
+        int e = 0;
+        cuda_check(cudaMemcpyAsync(&e, de, sizeof(int), cudaMemcpyDeviceToHost, st), "download error flag");
+        cuda_check(cudaStreamSynchronize(st), "adamw sync");
+        if (e) fail(NK_ERR_INVALID, "AdamW received a non-finite gradient or parameter");
+    });
+}
+
+nk_status nk_adamw_step(float *val, const float *grad, float *m, float *v, uint64_t n, const nk_adamw_cfg *cfg,
+                        int device) {
+    return guard([&] {
+        adamw_params(cfg);
+        if (n == 0) return;
+        if (!val || !grad || !m || !v) fail(NK_ERR_INVALID, "null argument");
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        float *dv = nullptr, *dg = nullptr, *dm = nullptr, *dvv = nullptr;
+        dalloc(&dv, n, "adamw val");
+        std::unique_ptr<float, void (*)(float *)> o1(dv, [](float *q) { cudaFree(q); });
+        dalloc(&dg, n, "adamw grad");
+        std::unique_ptr<float, void (*)(float *)> o2(dg, [](float *q) { cudaFree(q); });
+        dalloc(&dm, n, "adamw m");
+        std::unique_ptr<float, void (*)(float *)> o3(dm, [](float *q) { cudaFree(q); });
+        dalloc(&dvv, n, "adamw v");
+        std::unique_ptr<float, void (*)(float *)> o4(dvv, [](float *q) { cudaFree(q); });
+        cuda_check(cudaMemcpy(dv, val, n * 4, cudaMemcpyHostToDevice), "upload val");
+        cuda_check(cudaMemcpy(dg, grad, n * 4, cudaMemcpyHostToDevice), "upload grad");
+        cuda_check(cudaMemcpy(dm, m, n * 4, cudaMemcpyHostToDevice), "upload m");
+        cuda_check(cudaMemcpy(dvv, v, n * 4, cudaMemcpyHostToDevice), "upload v");
+        const nk_status st = nk_adamw_step_device(dv, dg, dm, dvv, n, cfg, nullptr);
+        // Copy back what the kernel wrote even after a non-finite element,
+        // then report it.
+        const std::string msg = st != NK_OK ? g_err : std::string();
+        cuda_check(cudaMemcpy(val, dv, n * 4, cudaMemcpyDeviceToHost), "download val");
+        cuda_check(cudaMemcpy(m, dm, n * 4, cudaMemcpyDeviceToHost), "download m");
+        cuda_check(cudaMemcpy(v, dvv, n * 4, cudaMemcpyDeviceToHost), "download v");
+        if (st != NK_OK) fail(st, msg);
+    });
+}
+
 nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
                           int chunked, int device) {
     return guard([&] {

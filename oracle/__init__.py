@@ -103,6 +103,10 @@ def lib():
             "orc_scan_sequential": (None, [_F, _F, _F, _u64, _u64, _u64, _u64]),
             "orc_scan_chunked": (None, [_F, _F, _F, _u64, _u64, _u64, _u64]),
             "orc_scan_adjoint": (None, [_F, _F, _F, _u64, _u64, _u64]),
+            "orc_gemm_tn": (None, [_F, _F, _F, _u64, _u64, _u64]),
+            "orc_dwconv_backward": (None, [_F, _F, _F, _P, _P, _P, _u64, _u64, _u64, _u64]),
+            "orc_adamw_step": (C.c_int, [_F, _F, _F, _F, _u64, C.c_float, C.c_float, C.c_float, C.c_float,
+                                         C.c_float, _u64, C.c_int]),
             "orc_config_check": (C.c_int, [C.POINTER(Config)]),
             "orc_model_new": (_P, [C.POINTER(Config), C.POINTER(RngState)]),
             "orc_model_free": (None, [_P]),
@@ -383,6 +387,41 @@ def scan_adjoint(a: np.ndarray, g: np.ndarray, batch: int, t: int, d: int) -> np
     c = np.empty_like(a)
     lib().orc_scan_adjoint(a, g, c, batch, t, d)
     return c
+
+
+def gemm_tn(a: np.ndarray, b: np.ndarray, p: int, m: int, n: int) -> np.ndarray:
+    """gemm_tn (tensor.rs:156-198): C[m,n] = A[p,m]^T B[p,n]."""
+    a = np.ascontiguousarray(a, dtype=np.float32).reshape(-1)
+    b = np.ascontiguousarray(b, dtype=np.float32).reshape(-1)
+    c = np.empty(m * n, dtype=np.float32)
+    lib().orc_gemm_tn(a, b, c, p, m, n)
+    return c.reshape(m, n)
+
+
+def dwconv_backward(x, w, go, batch: int, t: int, d: int, k: int, gx=None, gw=None, gb=None):
+    """Op::DwConv backward (autograd.rs:1050-1097).  Gradients accumulate
+    into copies of gx / gw / gb (zeros when None); returns (gx, gw, gb)."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    w = np.ascontiguousarray(w, dtype=np.float32).reshape(-1)
+    go = np.ascontiguousarray(go, dtype=np.float32).reshape(-1)
+    gx = np.zeros(batch * t * d, np.float32) if gx is None else np.array(gx, dtype=np.float32).reshape(-1)
+    gw = np.zeros(k * d, np.float32) if gw is None else np.array(gw, dtype=np.float32).reshape(-1)
+    gb = np.zeros(d, np.float32) if gb is None else np.array(gb, dtype=np.float32).reshape(-1)
+    lib().orc_dwconv_backward(x, w, go, gx.ctypes.data, gw.ctypes.data, gb.ctypes.data, batch, t, d, k)
+    return gx, gw, gb
+
+
+def adamw_step(val, grad, m, v, lr: float, t: int, decay: bool = True, b1: float = 0.9, b2: float = 0.95,
+               eps: float = 1e-8, wd: float = 0.0):
+    """AdamW::step (optim.rs:33-72) on copies of one parameter tensor and its
+    moments; t is the step counter after the increment.  Returns (val, m, v)."""
+    val = np.array(val, dtype=np.float32).reshape(-1)
+    m = np.array(m, dtype=np.float32).reshape(-1)
+    v = np.array(v, dtype=np.float32).reshape(-1)
+    grad = np.ascontiguousarray(grad, dtype=np.float32).reshape(-1)
+    if lib().orc_adamw_step(val, grad, m, v, val.size, lr, b1, b2, eps, wd, t, int(decay)) != 0:
+        raise ValueError(last_error())
+    return val, m, v
 
 
 def softmax_ce(logits: np.ndarray, targets: np.ndarray) -> float:

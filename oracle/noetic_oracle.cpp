@@ -909,6 +909,88 @@ void orc_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, 
     }
 }
 
+// ---- training-side ops (the backward pass and the optimiser around the scan)
+
+// kern_tn (tensor.rs:179-198): C[m,n] = sum_q A[q,m] * B[q,n], one row of C
+// at a time, q ascending, a product then an add (no fused multiply-add), and
+// a zero A element skips its row of B.
+void orc_gemm_tn(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n) {
+    for (uint64_t i = 0; i < m; ++i) {
+        float *cr = c + i * n;
+        for (uint64_t j = 0; j < n; ++j) cr[j] = 0.0f;
+        for (uint64_t q = 0; q < p; ++q) {
+            const float av = a[q * m + i];
+            if (av == 0.0f) continue;
+            const float *br = b + q * n;
+            for (uint64_t j = 0; j < n; ++j) cr[j] += av * br[j];
+        }
+    }
+}
+
+// Op::DwConv backward (autograd.rs:1050-1097): the three gradients
+// accumulate into gx / gw / gb (each nullable) in the reference's loop order.
+void orc_dwconv_backward(const float *x, const float *w, const float *go, float *gx, float *gw, float *gb,
+                         uint64_t batch, uint64_t t, uint64_t d, uint64_t k) {
+    if (gx)
+        for (uint64_t bi = 0; bi < batch; ++bi) {
+            const uint64_t base = bi * t * d;
+            for (uint64_t ti = 0; ti < t; ++ti) {
+                const uint64_t o = base + ti * d, qmax = ti + 1 < k ? ti + 1 : k;
+                for (uint64_t q = 0; q < qmax; ++q) {
+                    const uint64_t src = base + (ti - q) * d;
+                    for (uint64_t j = 0; j < d; ++j) gx[src + j] += go[o + j] * w[q * d + j];
+                }
+            }
+        }
+    if (gw)
+        for (uint64_t bi = 0; bi < batch; ++bi) {
+            const uint64_t base = bi * t * d;
+            for (uint64_t ti = 0; ti < t; ++ti) {
+                const uint64_t o = base + ti * d, qmax = ti + 1 < k ? ti + 1 : k;
+                for (uint64_t q = 0; q < qmax; ++q) {
+                    const uint64_t src = base + (ti - q) * d;
+                    for (uint64_t j = 0; j < d; ++j) gw[q * d + j] += go[o + j] * x[src + j];
+                }
+            }
+        }
+    if (gb)
+        for (uint64_t i = 0; i < batch * t; ++i)
+            for (uint64_t j = 0; j < d; ++j) gb[j] += go[i * d + j];
+}
+
+// AdamW::step (optim.rs:33-72) for one parameter tensor.  t is the step
+// counter after its increment; decay is the parameter's Param::decay.  The
+// bias corrections use powf exactly as the reference; every update is a
+// product or a sum in f32 (no fused multiply-add).  A non-finite gradient
+// or parameter stops the pass with an error, as the reference's assertion.
+int orc_adamw_step(float *val, const float *grad, float *m, float *v, uint64_t n, float lr, float b1, float b2,
+                   float eps, float wd, uint64_t t, int decay) {
+    return guarded([&] {
+        if (!(std::isfinite(lr) && lr >= 0.0f)) throw std::runtime_error("AdamW learning rate must be finite and non-negative");
+        if (!(std::isfinite(b1) && b1 >= 0.0f && b1 < 1.0f)) throw std::runtime_error("AdamW beta1 must be in [0, 1)");
+        if (!(std::isfinite(b2) && b2 >= 0.0f && b2 < 1.0f)) throw std::runtime_error("AdamW beta2 must be in [0, 1)");
+        if (!(std::isfinite(eps) && eps > 0.0f)) throw std::runtime_error("AdamW epsilon must be finite and positive");
+        if (!(std::isfinite(wd) && wd >= 0.0f)) throw std::runtime_error("AdamW weight decay must be finite and non-negative");
+        if (t == 0) throw std::runtime_error("AdamW step counter must be at least 1");
+        const float tf = (float)t;
+        const float bc1 = 1.0f - powf(b1, tf), bc2 = 1.0f - powf(b2, tf);
+        const float inv_bc1 = 1.0f / bc1, inv_bc2 = 1.0f / bc2;
+        for (uint64_t i = 0; i < n; ++i) {
+            const float gr = grad[i];
+            if (!std::isfinite(gr)) throw std::runtime_error("AdamW received a non-finite gradient");
+            if (!std::isfinite(val[i])) throw std::runtime_error("AdamW received a non-finite parameter");
+            const float mi = b1 * m[i] + (1.0f - b1) * gr;
+            const float vi = b2 * v[i] + (1.0f - b2) * gr * gr;
+            m[i] = mi;
+            v[i] = vi;
+            const float mh = mi * inv_bc1, vh = vi * inv_bc2;
+            float upd = mh / (sqrtf(vh) + eps);
+            if (decay && wd != 0.0f) upd += wd * val[i];
+            val[i] -= lr * upd;
+        }
+    });
+}
+
 int orc_softmax_ce(const float *logits, uint64_t rows, uint64_t vocab, const uint32_t *targets, float *loss_out) {
     return guarded([&] { *loss_out = softmax_ce(logits, rows, vocab, targets); });
 }

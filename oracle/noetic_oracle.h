@@ -107,6 +107,17 @@ void orc_model_set_threads(orc_model *m, uint64_t threads);
 
 /* scan_adjoint (scan.rs:235-260): c_t = g_t + a_{t+1} c_{t+1}, c_T = 0. */
 void orc_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d);
+/* gemm_tn (tensor.rs:156-198): C[m,n] = A[p,m]^T B[p,n], q ascending, zero A skipped. */
+void orc_gemm_tn(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n);
+/* Op::DwConv backward (autograd.rs:1050-1097): accumulates into gx [batch*t*d],
+ * gw [k*d], gb [d]; each nullable. */
+void orc_dwconv_backward(const float *x, const float *w, const float *go, float *gx, float *gw, float *gb,
+                         uint64_t batch, uint64_t t, uint64_t d, uint64_t k);
+/* AdamW::step (optim.rs:33-72) for one parameter tensor; t = step counter after
+ * the increment.  Returns nonzero (message in orc_last_error) on invalid
+ * hyper-parameters or a non-finite gradient / parameter. */
+int orc_adamw_step(float *val, const float *grad, float *m, float *v, uint64_t n, float lr, float b1, float b2,
+                   float eps, float wd, uint64_t t, int decay);
 /* Graph::softmax_ce forward (autograd.rs:579-624): mean cross-entropy in nats
  * over rows whose target is not 0xFFFFFFFF. */
 int orc_softmax_ce(const float *logits, uint64_t rows, uint64_t vocab, const uint32_t *targets, float *loss_out);

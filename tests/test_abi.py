@@ -142,3 +142,24 @@ def test_host_only_model_cannot_run_a_decoder(nb):
 def test_rng_state_helper_matches_oracle(nb, orc):
     for seed in [0, 3000, 2**64 - 1]:
         assert [int(v) for v in nb.rng_state(seed)] == orc.Rng(seed).s
+
+
+def test_training_ops_refuse_bad_arguments_before_any_device_work(nb):
+    # AdamW's assertions (optim.rs:34-38) and the shape limits are checked on
+    # the host, so these refusals need no GPU.
+    z = np.zeros(4, np.float32)
+    for kw in [dict(lr=-1.0), dict(lr=float("inf")), dict(lr=0.1, b1=1.0), dict(lr=0.1, b2=-0.5),
+               dict(lr=0.1, eps=0.0), dict(lr=0.1, wd=-1.0), dict(lr=0.1, t=0)]:
+        args = dict(t=1)
+        args.update(kw)
+        with pytest.raises(nb.NoeticError) as e:
+            nb.adamw_step(z, z, z, z, **args)
+        assert e.value.status == nb.NK_ERR_INVALID
+    with pytest.raises(nb.NoeticError) as e:  # kernel width above the weight-gradient kernel's 16
+        nb.dwconv_backward(np.zeros(34), np.zeros(17 * 2), np.zeros(34), 1, 17, 2, 17)
+    assert e.value.status == nb.NK_ERR_INVALID
+    with pytest.raises(nb.NoeticError) as e:
+        nb.dwconv_backward(np.zeros(0), np.zeros(0), np.zeros(0), 1, 0, 0, 4)
+    assert e.value.status == nb.NK_ERR_INVALID
+    # Empty products need no device either.
+    assert nb.gemm_tn(np.zeros(0), np.zeros(0), 0, 0, 5).shape == (0, 5)

@@ -316,3 +316,111 @@ def test_scan_adjoint_closed_form(orc):
                         prod = np.float32(prod * a[(bi * t + s) * d + j])
                     exp = np.float32(exp + g[(bi * t + s) * d + j] * prod)
                 assert abs(exp - c[(bi * t + ti) * d + j]) < 1e-4
+
+
+def _dwconv_forward64(x, w, b, batch, t, d, k):
+    """autograd.rs:550-575 in float64: y = bias + sum_{q < min(t+1, k)} w[q] x[t-q]."""
+    x = x.reshape(batch, t, d).astype(np.float64)
+    w = w.reshape(k, d).astype(np.float64)
+    y = np.broadcast_to(b.astype(np.float64), (batch, t, d)).copy()
+    for ti in range(t):
+        for q in range(min(ti + 1, k)):
+            y[:, ti] += w[q] * x[:, ti - q]
+    return y
+
+
+def test_gemm_tn_restatement(orc):
+    # selftest.rs:35-75: gemm_tn of the transposed A against a naive product, 2e-3.
+    rng = np.random.default_rng(7)
+    for p, m, n in [(33, 17, 29), (1, 5, 3), (64, 64, 64)]:
+        a = rng.standard_normal((p, m)).astype(np.float32)
+        b = rng.standard_normal((p, n)).astype(np.float32)
+        c = orc.gemm_tn(a, b, p, m, n)
+        assert np.abs(c - a.T.astype(np.float64) @ b.astype(np.float64)).max() < 2e-3
+    # p = 0: C = 0; a zero A element skips its (non-finite) row of B (tensor.rs:188-190).
+    assert not orc.gemm_tn(np.zeros(0), np.zeros(0), 0, 3, 4).any()
+    a = np.array([[0.0, 1.0]], np.float32)
+    b = np.array([[np.inf, 2.0]], np.float32)
+    assert np.array_equal(orc.gemm_tn(a, b, 1, 2, 2), np.array([[0.0, 0.0], [np.inf, 2.0]], np.float32))
+
+
+def test_dwconv_backward_restatement(orc):
+    # selftest.rs:722-784: the three gradients of sum(dwconv(x, w, b) * m)
+    # against central differences, with a kernel longer than the sequence.
+    for batch, t, d, k in [(2, 3, 2, 6), (3, 7, 4, 3)]:
+        rng = np.random.default_rng(batch * 100 + k)
+        x = rng.standard_normal(batch * t * d).astype(np.float32)
+        w = (rng.standard_normal(k * d) * 0.5).astype(np.float32)
+        b = (rng.standard_normal(d) * 0.1).astype(np.float32)
+        m = rng.standard_normal(batch * t * d).astype(np.float32)
+        gx, gw, gb = orc.dwconv_backward(x, w, m, batch, t, d, k)
+
+        def loss(xs, ws, bs):
+            return float((_dwconv_forward64(xs, ws, bs, batch, t, d, k).reshape(-1) * m).sum())
+
+        eps = 1e-3
+        for arr, grad, which in [(x, gx, 0), (w, gw, 1), (b, gb, 2)]:
+            for i in range(arr.size):
+                plus, minus = arr.astype(np.float64).copy(), arr.astype(np.float64).copy()
+                plus[i] += eps
+                minus[i] -= eps
+                args_p = [x.astype(np.float64), w.astype(np.float64), b.astype(np.float64)]
+                args_m = list(args_p)
+                args_p[which], args_m[which] = plus, minus
+                fd = (loss(*args_p) - loss(*args_m)) / (2 * eps)
+                assert abs(fd - grad[i]) / (1 + abs(fd)) < 5e-3, (batch, t, d, k, which, i)
+    # The gradients add into what the buffers held (Graph::backward accumulates).
+    gx0 = np.full(batch * t * d, 0.5, np.float32)
+    gx2, gw2, gb2 = orc.dwconv_backward(x, w, m, batch, t, d, k, gx=gx0, gw=np.ones(k * d), gb=np.ones(d))
+    assert np.allclose(gx2, gx + 0.5, atol=1e-6) and np.allclose(gw2, gw + 1, atol=1e-5)
+    assert np.allclose(gb2, gb + 1, atol=1e-6)
+
+
+def _powf(x, y):
+    """The C library's powf, which Rust's f32::powf calls (numpy's float32
+    power rounds differently in the last place for some arguments)."""
+    import ctypes
+
+    libm = ctypes.CDLL("libm.so.6")
+    libm.powf.restype = ctypes.c_float
+    libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
+    return np.float32(libm.powf(float(x), float(y)))
+
+
+def _adamw_numpy(val, grad, m, v, lr, t, decay, b1=0.9, b2=0.95, eps=1e-8, wd=0.0):
+    """optim.rs:43-71 in numpy float32 (every operation rounded to f32)."""
+    f = np.float32
+    b1, b2, eps, wd, lr = f(b1), f(b2), f(eps), f(wd), f(lr)
+    inv_bc1 = f(1) / (f(1) - _powf(b1, t))
+    inv_bc2 = f(1) / (f(1) - _powf(b2, t))
+    mi = b1 * m + (f(1) - b1) * grad
+    vi = b2 * v + (f(1) - b2) * grad * grad
+    upd = (mi * inv_bc1) / (np.sqrt(vi * inv_bc2) + eps)
+    if decay and wd != 0:
+        upd = upd + wd * val
+    return val - lr * upd, mi, vi
+
+
+def test_adamw_restatement(orc):
+    rng = np.random.default_rng(11)
+    n = 1000
+    val = rng.standard_normal(n).astype(np.float32)
+    m = np.zeros(n, np.float32)
+    v = np.zeros(n, np.float32)
+    ev, em, ev2 = val.copy(), m.copy(), v.copy()
+    for t in range(1, 8):
+        g = rng.standard_normal(n).astype(np.float32)
+        decay = t % 2 == 0
+        val, m, v = orc.adamw_step(val, g, m, v, lr=1e-2, t=t, decay=decay, wd=0.1)
+        ev, em, ev2 = _adamw_numpy(ev, g, em, ev2, 1e-2, t, decay, wd=0.1)
+        assert np.array_equal(val, ev) and np.array_equal(m, em) and np.array_equal(v, ev2), t
+    # The first step moves every weight by lr * sign(g) (m_hat / sqrt(v_hat) = +-1).
+    v1, _, _ = orc.adamw_step(np.zeros(3), np.array([2.0, -0.5, 0.0]), np.zeros(3), np.zeros(3), lr=0.1, t=1)
+    assert np.allclose(v1, [-0.1, 0.1, 0.0], atol=1e-6)
+    # The reference's assertions (optim.rs:34-38, 55-56).
+    for kw in [dict(lr=-1.0), dict(lr=0.1, b1=1.0), dict(lr=0.1, b2=-0.1), dict(lr=0.1, eps=0.0),
+               dict(lr=0.1, wd=float("nan"))]:
+        with pytest.raises(ValueError):
+            orc.adamw_step(np.zeros(2), np.zeros(2), np.zeros(2), np.zeros(2), t=1, **kw)
+    with pytest.raises(ValueError):
+        orc.adamw_step(np.zeros(2), np.array([0.0, np.nan]), np.zeros(2), np.zeros(2), lr=0.1, t=1)
