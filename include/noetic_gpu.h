@@ -233,6 +233,37 @@ nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t bat
 nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
                                  int chunked, void *stream);
 
+/* ---------------------------------------------------------------- BPE text I/O
+ * Byte-level BPE (bpe.rs), host only: tokens 0..255 are bytes, merge i makes
+ * token 256 + i.  Prompts are encoded to ids before prefill, generated ids
+ * decoded to bytes after. */
+typedef struct nk_bpe nk_bpe;
+/* Bpe::bytes_only (bpe.rs:47-53): 256 byte tokens, no merges. */
+nk_status nk_bpe_create_bytes_only(nk_bpe **out);
+/* Bpe::load (bpe.rs:309-380): the "noetic-bpe 1" merges file, with the
+ * reference's limits (64 MiB file, 1,000,000 merges, 1 MiB per token, 128
+ * MiB of token bytes) and checks; a bad file is NK_ERR_IO. */
+nk_status nk_bpe_load(const char *path, nk_bpe **out);
+/* Bpe::save (bpe.rs:288-307): temporary file, then rename. */
+nk_status nk_bpe_save(const nk_bpe *bpe, const char *path);
+nk_status nk_bpe_destroy(nk_bpe *bpe);
+nk_status nk_bpe_vocab_size(const nk_bpe *bpe, uint64_t *out);
+/* The pair that merge i joins. */
+nk_status nk_bpe_merge(const nk_bpe *bpe, uint64_t i, uint32_t *a, uint32_t *b);
+/* Bpe::encode (bpe.rs:252-258): UTF-8 text (len bytes; invalid UTF-8 is
+ * NK_ERR_INVALID) split by Bpe::pretokenize (bpe.rs:77-115, char::is_alphabetic
+ * = the Unicode 15.0 Alphabetic property), each chunk merged lowest rank
+ * first.  *n_out = the id count; NK_ERR_INVALID when it exceeds cap. */
+nk_status nk_bpe_encode(const nk_bpe *bpe, const char *text, uint64_t len, uint32_t *ids, uint64_t cap,
+                        uint64_t *n_out);
+/* Bpe::encode_bytes (bpe.rs:262-266): any bytes, no pre-token boundaries. */
+nk_status nk_bpe_encode_bytes(const nk_bpe *bpe, const uint8_t *bytes, uint64_t len, uint32_t *ids, uint64_t cap,
+                              uint64_t *n_out);
+/* Bpe::decode_bytes (bpe.rs:268-279): an out-of-range id is NK_ERR_INVALID
+ * (the reference returns None).  *n_out = the byte count. */
+nk_status nk_bpe_decode_bytes(const nk_bpe *bpe, const uint32_t *ids, uint64_t n, uint8_t *out, uint64_t cap,
+                              uint64_t *n_out);
+
 /* gemm_tn (tensor.rs:156-198): C[m, n] = A[p, m]^T B[p, n], the weight-
  * gradient product; a zero element of A skips its product as kern_tn does.
  * Host arrays, run on `device`; the _device form takes device pointers and a

@@ -14,6 +14,11 @@ reference (noetic crate)               here
 ``sample_token`` (infer.rs:228-305)    :func:`sample_token`, :meth:`Decoder.sample`
 ``cli.rs:generate`` (cli.rs:470-518)   :meth:`Decoder.generate`
 ``scan_sequential`` / ``scan_chunked`` :func:`scan_sequential`, :func:`scan_chunked`
+``scan_adjoint`` (scan.rs:235-260)     :func:`scan_adjoint`
+``gemm_tn`` (tensor.rs:156-198)        :func:`gemm_tn`
+``Op::DwConv`` backward                :func:`dwconv_backward`
+``AdamW::step`` (optim.rs:33-72)       :func:`adamw_step`
+``Lm::loss`` (model.rs:228-234)        :meth:`Model.loss`
 =====================================  ===========================================
 
 Every computation runs on the GPU through hand-written sm_100a kernels.  There
@@ -97,6 +102,15 @@ SIGNATURES = {
     "nk_scan": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
     "nk_scan_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _P]),
     "nk_scan_adjoint": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32, _i32]),
+    "nk_bpe_create_bytes_only": (_i32, [C.POINTER(_P)]),
+    "nk_bpe_load": (_i32, [C.c_char_p, C.POINTER(_P)]),
+    "nk_bpe_save": (_i32, [_P, C.c_char_p]),
+    "nk_bpe_destroy": (_i32, [_P]),
+    "nk_bpe_vocab_size": (_i32, [_P, C.POINTER(_u64)]),
+    "nk_bpe_merge": (_i32, [_P, _u64, C.POINTER(_u32), C.POINTER(_u32)]),
+    "nk_bpe_encode": (_i32, [_P, _P, _u64, _P, _u64, C.POINTER(_u64)]),
+    "nk_bpe_encode_bytes": (_i32, [_P, _P, _u64, _P, _u64, C.POINTER(_u64)]),
+    "nk_bpe_decode_bytes": (_i32, [_P, _P, _u64, _P, _u64, C.POINTER(_u64)]),
     "nk_gemm_tn": (_i32, [_P, _P, _P, _u64, _u64, _u64, _i32]),
     "nk_gemm_tn_device": (_i32, [_P, _P, _P, _u64, _u64, _u64, _P]),
     "nk_dwconv_backward": (_i32, [_P, _P, _P, _P, _P, _P, _u64, _u64, _u64, _u64, _i32]),
@@ -481,6 +495,95 @@ def scan_adjoint(a, g, batch: int, t: int, d: int, chunked: bool = False, device
     c = np.empty(n, dtype=np.float32)
     _check(lib().nk_scan_adjoint(_ptr(a), _ptr(g), _ptr(c), batch, t, d, int(chunked), device))
     return c
+
+
+class Bpe:
+    """Byte-level BPE (bpe.rs) over ``nk_bpe_*``: tokens 0..255 are bytes,
+    merge i makes token 256 + i.  Host only (no device needed)."""
+
+    def __init__(self, handle):
+        self.h = handle
+
+    @staticmethod
+    def bytes_only() -> "Bpe":
+        """Bpe::bytes_only (bpe.rs:47-53)."""
+        h = _P()
+        _check(lib().nk_bpe_create_bytes_only(C.byref(h)))
+        return Bpe(h)
+
+    @staticmethod
+    def load(path: str) -> "Bpe":
+        """Bpe::load (bpe.rs:309-380); a bad file raises NoeticError (NK_ERR_IO)."""
+        h = _P()
+        _check(lib().nk_bpe_load(os.fsencode(path), C.byref(h)))
+        return Bpe(h)
+
+    def save(self, path: str):
+        """Bpe::save (bpe.rs:288-307)."""
+        _check(lib().nk_bpe_save(self.h, os.fsencode(path)))
+
+    def vocab_size(self) -> int:
+        n = _u64(0)
+        _check(lib().nk_bpe_vocab_size(self.h, C.byref(n)))
+        return n.value
+
+    def merges(self) -> list:
+        out = []
+        for i in range(self.vocab_size() - 256):
+            a, b = _u32(0), _u32(0)
+            _check(lib().nk_bpe_merge(self.h, i, C.byref(a), C.byref(b)))
+            out.append((a.value, b.value))
+        return out
+
+    def _ids(self, fn, data: bytes) -> np.ndarray:
+        buf = C.create_string_buffer(data, len(data))
+        n = _u64(0)
+        cap = max(len(data), 1)
+        out = np.empty(cap, dtype=np.uint32)
+        _check(fn(self.h, buf, len(data), _ptr(out), cap, C.byref(n)))
+        return out[: n.value].copy()
+
+    def encode(self, text: str) -> np.ndarray:
+        """Bpe::encode (bpe.rs:252-258): pre-token chunks, then merges."""
+        return self._ids(lib().nk_bpe_encode, text.encode("utf-8"))
+
+    def encode_bytes(self, data: bytes) -> np.ndarray:
+        """Bpe::encode_bytes (bpe.rs:262-266): no pre-token boundaries."""
+        return self._ids(lib().nk_bpe_encode_bytes, bytes(data))
+
+    def decode_bytes(self, ids) -> bytes:
+        """Bpe::decode_bytes (bpe.rs:268-279); an out-of-range id raises
+        NoeticError (NK_ERR_INVALID) where the reference returns None."""
+        ids = _u32a(ids).reshape(-1)
+        n = _u64(0)
+        # Sized first: with no room the call reports the byte count it needs
+        # (an out-of-range id fails before that, leaving the count at 0).
+        st = lib().nk_bpe_decode_bytes(self.h, _ptr(ids), ids.size, None, 0, C.byref(n))
+        if st == NK_OK:
+            return b""
+        if n.value == 0:
+            _check(st)
+        out = C.create_string_buffer(n.value)
+        _check(lib().nk_bpe_decode_bytes(self.h, _ptr(ids), ids.size, out, n.value, C.byref(n)))
+        return out.raw[: n.value]
+
+    def decode(self, ids) -> str:
+        """Bpe::decode (bpe.rs:281-286): lossy UTF-8; "" when an id is out of range."""
+        try:
+            return self.decode_bytes(ids).decode("utf-8", errors="replace")
+        except NoeticError:
+            return ""
+
+    def close(self):
+        if self.h:
+            lib().nk_bpe_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def gemm_tn(a, b, p: int, m: int, n: int, device: int = 0) -> np.ndarray:

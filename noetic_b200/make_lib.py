@@ -30,7 +30,7 @@ def _sources():
 
 
 def _headers():
-    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh"))]
+    hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".h", ".cuh", ".inc"))]
     hs.append(os.path.join(ROOT, "include", "noetic_gpu.h"))
     return hs
 
