@@ -180,6 +180,71 @@ def run_reference(args, rank):
 
 
 # ---------------------------------------------------------------- our arm
+def run_train_ops(args):
+    """The training-side ops at training shapes of the headline model, inputs
+    resident on the device, timed with CUDA events on the launching stream
+    (every call includes its own synchronisation): gemm_tn (the weight
+    gradient of up_proj over 64 sequences of 1024 tokens: p = 65536 rows,
+    m = 1024, n = 3072), the depthwise-conv backward of one layer over 8
+    sequences of 32768 tokens (d = 768, k = 4), and AdamW over the 361.15 M
+    parameters of the headline model.  Prints one JSON line."""
+    import ctypes as C
+
+    import torch
+
+    import noetic_b200 as nb
+
+    L = nb.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    st = stream.cuda_stream
+    peaks, basis = load_peaks()
+    tf_peak = peaks["bf16_tflops_sustained"] / 2 / 3
+    reps = max(3, args.steps)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    out = {"metric": "training-side ops (gemm_tn, dwconv backward, AdamW)", "data": "synthetic (torch.randn)",
+           "peak_basis": basis}
+    p, m, n = 65536, 1024, 3072
+    a, b = torch.randn(p, m, device="cuda"), torch.randn(p, n, device="cuda")
+    c = torch.empty(m, n, device="cuda")
+    ms = timed(lambda: nb._check(L.nk_gemm_tn_device(a.data_ptr(), b.data_ptr(), c.data_ptr(), p, m, n, st)))
+    out["gemm_tn"] = {"shape": [p, m, n], "ms": ms, "tflops": 2.0 * p * m * n / ms / 1e9,
+                      "frac": 2.0 * p * m * n / ms / 1e9 / tf_peak, "peak_tflops": tf_peak,
+                      "engine": "tcgen05 3xTF32 + transposing operand splits"}
+    del a, b, c
+    batch, t, d, k = 8, 32768, 768, 4
+    x = torch.randn(batch * t * d, device="cuda")
+    go, gx = torch.randn_like(x), torch.zeros_like(x)
+    w, gw, gb = torch.randn(k * d, device="cuda"), torch.zeros(k * d, device="cuda"), torch.zeros(d, device="cuda")
+    ms = timed(lambda: nb._check(L.nk_dwconv_backward_device(x.data_ptr(), w.data_ptr(), go.data_ptr(), gx.data_ptr(),
+                                                             gw.data_ptr(), gb.data_ptr(), batch, t, d, k, st)))
+    nbytes = batch * t * d * 20.0  # gx pass: go + gx read, gx written; weight pass: go + x read
+    out["dwconv_backward"] = {"shape": [batch, t, d, k], "ms": ms, "gbs": nbytes / ms / 1e6,
+                              "frac": nbytes / ms / 1e6 / peaks["hbm_gbs"], "bytes": nbytes}
+    del x, go, gx
+    nn = 361_150_000
+    val, g = torch.randn(nn, device="cuda"), torch.randn(nn, device="cuda") * 1e-3
+    mm, v = torch.zeros(nn, device="cuda"), torch.zeros(nn, device="cuda")
+    cfg = nb.NkAdamwCfg(1e-3, 0.9, 0.95, 1e-8, 0.01, 1, 1)
+    ms = timed(lambda: nb._check(L.nk_adamw_step_device(val.data_ptr(), g.data_ptr(), mm.data_ptr(), v.data_ptr(), nn,
+                                                        C.byref(cfg), st)))
+    out["adamw"] = {"params": nn, "ms": ms, "gbs": nn * 28.0 / ms / 1e6, "frac": nn * 28.0 / ms / 1e6 / peaks["hbm_gbs"],
+                    "bytes_per_param": 28}
+    print(json.dumps(out), flush=True)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
 
@@ -427,6 +492,8 @@ def main():
                     help="profiling knob: fewer layers than the headline model (for small ncu captures)")
     ap.add_argument("--vocab", type=int, default=None,
                     help="profiling knob: a smaller vocabulary than the headline model")
+    ap.add_argument("--train-ops", action="store_true",
+                    help="time the training-side ops (gemm_tn, dwconv backward, AdamW) instead")
     args = ap.parse_args()
     rank = _env_int("RANK", 0)
     world = _env_int("WORLD_SIZE", 1)
@@ -441,6 +508,9 @@ def main():
         global WORKLOAD
         WORKLOAD = (f"profiling case: d1024 L{MODEL['n_layer']} V{MODEL['vocab']}, {args.streams} streams x "
                     f"64-token prompts, greedy decode (not the headline configuration)")
+    if args.train_ops:
+        run_train_ops(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank)
         return

@@ -195,6 +195,15 @@ size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d);
 // ---- training-side ops (train.cu)
 // gemm_tn (tensor.rs:156-198): C[m, n] = A[p, m]^T B[p, n].
 cudaError_t gemm_tn(const float *a, const float *b, float *c, int64_t p, int m, int n, cudaStream_t st);
+// The same product on the tcgen05 3xTF32 engine: scratch holds
+// gemm_tn_tc_scratch_floats() floats, flags gemm_tn_tc_flag_ints() ints, zero
+// before the call ([0] non-finite operand -> exact recompute, [1] kernel
+// error code, the rest stream-K counters, left zero).
+bool gemm_tn_tc_eligible(int64_t p, int m, int n);
+size_t gemm_tn_tc_scratch_floats(int64_t p, int m, int n);
+int gemm_tn_tc_flag_ints();
+cudaError_t gemm_tn_tc(const float *a, const float *b, float *c, int64_t p, int m, int n, float *scratch, int *flags,
+                       cudaStream_t st);
 // Op::DwConv backward (autograd.rs:1050-1097): accumulates into gx [batch*t, d],
 // gw [k, d], gb [d] (each nullable); scratch holds
 // dwconv_backward_scratch_floats() floats when gw or gb is given; k <= dwconv_max_k().

@@ -83,6 +83,14 @@ size_t tc_stream_k_ws_floats();
 int tc_argmax_parts(int N, int bn);
 
 cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs);
+// hi / lo [cols, ld_out] = the operand pair of the transpose of src [rows,
+// cols], output columns rows .. ld_out - 1 zero; *nonfinite (nullable) = 1
+// when src holds inf or NaN.  ld_out < 2^21 * 32 rows of tiles.
+cudaError_t tc_split_transposed(const float *src, int rows, int cols, int ld_out, float *hi, float *lo,
+                                int *nonfinite, cudaStream_t st);
+// A TcOperand over an already split [N, K] pair (K % 4 == 0); false if the
+// tensor maps cannot be encoded.
+bool tc_operand_from(const float *hi, const float *lo, int N, int K, TcOperand &op);
 void tc_weights_free(TcWeights &w);
 
 // hi = tf32(A), lo = tf32(A - hi) for an f32 operand [rows, cols] (row stride lda).

@@ -13,6 +13,7 @@
 #include <fstream>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1693,13 +1694,79 @@ nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint6
 
 // ---------------------------------------------------------------- training-side ops
 
+namespace {
+// Scratch for the synchronous stand-alone ops, kept per device between calls
+// (grown on demand up to 8 GiB; larger requests allocate for the call).
+// The lock is held from the request until the op has synchronised, so calls
+// from several host threads take turns on it.
+struct OpScratch {
+    std::mutex mu;
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+OpScratch &op_scratch(int device) {
+    static std::mutex table_mu;
+    static std::map<int, OpScratch *> table;
+    std::lock_guard<std::mutex> g(table_mu);
+    OpScratch *&e = table[device];
+    if (!e) e = new OpScratch();
+    return *e;
+}
+constexpr size_t OP_SCRATCH_CAP = size_t(8) << 30;
+
+// Holds the device's scratch (or a private allocation) for one call.
+struct ScratchLease {
+    std::unique_lock<std::mutex> lock;
+    void *own = nullptr;
+    void *ptr = nullptr;
+    ScratchLease(size_t bytes, const char *what) {
+        int dev = 0;
+        cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+        if (bytes > OP_SCRATCH_CAP) {
+            cuda_check(cudaMalloc(&own, bytes), what);
+            ptr = own;
+            return;
+        }
+        OpScratch &sc = op_scratch(dev);
+        lock = std::unique_lock<std::mutex>(sc.mu);
+        if (sc.bytes < bytes) {
+            if (sc.ptr) cudaFree(sc.ptr);
+            sc.ptr = nullptr;
+            sc.bytes = 0;
+            cuda_check(cudaMalloc(&sc.ptr, bytes), what);
+            sc.bytes = bytes;
+        }
+        ptr = sc.ptr;
+    }
+    ~ScratchLease() {
+        if (own) cudaFree(own);
+    }
+};
+}  // namespace
+
 nk_status nk_gemm_tn_device(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n,
                             void *stream) {
     return guard([&] {
         if (m == 0 || n == 0) return;
         if (!c || (p && (!a || !b))) fail(NK_ERR_INVALID, "null argument");
         if (m >= (1ull << 22) || n >= (1ull << 31) || p >= (1ull << 62)) fail(NK_ERR_INVALID, "gemm_tn shape too large");
-        cuda_check(nk::gemm_tn(a, b, c, (int64_t)p, (int)m, (int)n, (cudaStream_t)stream), "gemm_tn");
+        cudaStream_t st = (cudaStream_t)stream;
+        if (!nk::gemm_tn_tc_eligible((int64_t)p, (int)m, (int)n)) {
+            cuda_check(nk::gemm_tn(a, b, c, (int64_t)p, (int)m, (int)n, st), "gemm_tn");
+            return;
+        }
+        const int nflags = nk::gemm_tn_tc_flag_ints();
+        const size_t fbytes = ((size_t)nflags * sizeof(int) + 255) & ~size_t(255);
+        ScratchLease lease(fbytes + nk::gemm_tn_tc_scratch_floats((int64_t)p, (int)m, (int)n) * sizeof(float),
+                           "gemm_tn operands");
+        int *flags = (int *)lease.ptr;
+        float *scratch = (float *)((char *)lease.ptr + fbytes);
+        cuda_check(cudaMemsetAsync(flags, 0, nflags * sizeof(int), st), "memset");
+        cuda_check(nk::gemm_tn_tc(a, b, c, (int64_t)p, (int)m, (int)n, scratch, flags, st), "gemm_tn (tensor cores)");
+        int h[2] = {0, 0};
+        cuda_check(cudaMemcpyAsync(h, flags, sizeof(h), cudaMemcpyDeviceToHost, st), "read gemm_tn flags");
+        cuda_check(cudaStreamSynchronize(st), "gemm_tn sync");
+        if (h[1]) fail(NK_ERR_DEVICE, "gemm_tn: a tensor-core pipeline wait expired (code " + std::to_string(h[1]) + ")");
     });
 }
 
@@ -1736,11 +1803,13 @@ nk_status nk_dwconv_backward_device(const float *x, const float *w, const float 
         if (rows == 0 || (!gx && !gw && !gb)) return;
         if (!go || (gx && !w) || (gw && !x)) fail(NK_ERR_INVALID, "null argument");
         cudaStream_t st = (cudaStream_t)stream;
-        float *scratch = nullptr;
-        if (gw || gb) dalloc(&scratch, nk::dwconv_backward_scratch_floats((int64_t)rows, (int)d, (int)k), "dwconv scratch");
+        std::unique_ptr<ScratchLease> lease;
+        if (gw || gb)
+            lease.reset(new ScratchLease(nk::dwconv_backward_scratch_floats((int64_t)rows, (int)d, (int)k) * sizeof(float),
+                                         "dwconv scratch"));
+        float *scratch = lease ? (float *)lease->ptr : nullptr;
         cudaError_t e = nk::dwconv_backward(x, w, go, gx, gw, gb, (int64_t)batch, (int64_t)t, (int)d, (int)k, scratch, st);
         cudaError_t e2 = scratch ? cudaStreamSynchronize(st) : cudaSuccess;
-        if (scratch) cudaFree(scratch);
         cuda_check(e, "dwconv backward");
         cuda_check(e2, "dwconv backward sync");
     });
@@ -1801,9 +1870,8 @@ nk_status nk_adamw_step_device(float *val, const float *grad, float *m, float *v
         if (n == 0) return;
         if (!val || !grad || !m || !v) fail(NK_ERR_INVALID, "null argument");
         cudaStream_t st = (cudaStream_t)stream;
-        int *de = nullptr;
-        dalloc(&de, 1, "error flag");
-        std::unique_ptr<int, void (*)(int *)> oe(de, [](int *q) { cudaFree(q); });
+        ScratchLease lease(sizeof(int), "error flag");
+        int *de = (int *)lease.ptr;
         cuda_check(cudaMemsetAsync(de, 0, sizeof(int), st), "memset");
         cuda_check(nk::adamw_step(val, grad, m, v, (int64_t)n, a, de, st), "adamw");
         int e = 0;

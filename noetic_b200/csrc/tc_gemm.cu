@@ -1035,6 +1035,41 @@ __global__ void split_tf32_k(const float *__restrict__ src, int ld, float *__res
     lo[(size_t)rd * cols + c] = tf32_round(x - h);
 }
 
+// hi / lo [cols, ld_out] = the split of the transpose of src [rows, cols]
+// (row stride cols), columns rows .. ld_out - 1 of the output zero (K
+// padding to a multiple of 4).  32 x 32 tiles through shared memory keep
+// both the reads and the writes coalesced.  *nonfinite = 1 if any element
+// is inf or NaN.
+__global__ void split_tf32_t_k(const float *__restrict__ src, int rows, int cols, int ld_out,
+                               float *__restrict__ hi, float *__restrict__ lo, int *nonfinite) {
+    __shared__ float tile[32][33];
+    const int c0 = blockIdx.x * 32;
+    const int64_t r0 = (int64_t)blockIdx.y * 32;
+    bool bad = false;
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int64_t r = r0 + i;
+        const int c = c0 + threadIdx.x;
+        float x = 0.0f;
+        if (r < rows && c < cols) {
+            x = src[(size_t)r * cols + c];
+            bad |= !isfinite(x);
+        }
+        tile[i][threadIdx.x] = x;
+    }
+    if (bad && nonfinite) atomicExch(nonfinite, 1);
+    __syncthreads();
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+        const int c = c0 + i;
+        const int64_t r = r0 + threadIdx.x;
+        if (c < cols && r < ld_out) {
+            const float x = tile[threadIdx.x][i];
+            const float h = tf32_round(x);
+            hi[(size_t)c * ld_out + r] = h;
+            lo[(size_t)c * ld_out + r] = tf32_round(x - h);
+        }
+    }
+}
+
 // ---- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1120,6 +1155,26 @@ int tc_argmax_parts(int N, int bn) { return 2 * tc_tiles_n(N, bn); }
 
 cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
     return split(A, lda, hi, lo, rows, cols, st);
+}
+
+cudaError_t tc_split_transposed(const float *src, int rows, int cols, int ld_out, float *hi, float *lo,
+                                int *nonfinite, cudaStream_t st) {
+    if (ld_out < rows || cols <= 0 || ld_out <= 0) return cols <= 0 ? cudaSuccess : cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((ld_out + 31) / 32));
+    if (grid.y > 65535u) return cudaErrorInvalidValue;
+    split_tf32_t_k<<<grid, dim3(32, 8), 0, st>>>(src, rows, cols, ld_out, hi, lo, nonfinite);
+    return cudaGetLastError();
+}
+
+bool tc_operand_from(const float *hi, const float *lo, int N, int K, TcOperand &op) {
+    if (K % 4 != 0 || N <= 0 || K <= 0) return false;
+    op.hi = hi;
+    op.lo = lo;
+    op.N = op.N_pad = N;
+    op.K = op.K_pad = K;
+    op.pair_half = 0;
+    return make_map((CUtensorMap *)op.map_hi, hi, N, K, 256) && make_map((CUtensorMap *)op.map_lo, lo, N, K, 256) &&
+           make_map((CUtensorMap *)op.map_hi128, hi, N, K, 128) && make_map((CUtensorMap *)op.map_lo128, lo, N, K, 128);
 }
 
 cudaError_t tc_weights_build(TcWeights &w, const std::vector<TcSource> &srcs) {

@@ -128,3 +128,30 @@ def test_adamw_non_finite_gradient_is_refused(gpu):
     assert e.value.status == gpu.NK_ERR_INVALID
     with pytest.raises(gpu.NoeticError):
         gpu.adamw_step(np.array([1.0, np.nan]), np.zeros(2), np.zeros(2), np.zeros(2), lr=0.1, t=1)
+
+
+def test_gemm_tn_tensor_core_path_with_non_finite_operands(gpu, orc):
+    # Shapes the tcgen05 path takes (m, n >= 128); a non-finite element in B
+    # (or A) sends the product to the exact kernel, which keeps kern_tn's
+    # zero-skip semantics; p not a multiple of 4 exercises the K padding.
+    rng = np.random.default_rng(21)
+    p, m, n = 258, 130, 200
+    a = rng.standard_normal((p, m)).astype(np.float32)
+    b = rng.standard_normal((p, n)).astype(np.float32)
+    a[5, :] = 0.0
+    a[5, 3] = 2.0
+    b[5, 7] = np.inf
+    b[9, 11] = np.nan
+    a[9, :] = 0.0
+    got = gpu.gemm_tn(a, b, p, m, n)
+    ref = orc.gemm_tn(a, b, p, m, n)
+    assert np.array_equal(np.isnan(got), np.isnan(ref)) and np.array_equal(np.isinf(got), np.isinf(ref))
+    fin = np.isfinite(ref)
+    bound = 1e-5 * (np.abs(a).T.astype(np.float64) @ np.where(np.isfinite(b), np.abs(b), 0).astype(np.float64))
+    assert (np.abs(got - ref)[fin] <= bound[fin] + 1e-6).all()
+    # All finite at the same shape: the tensor-core result within the sum bound.
+    b[5, 7], b[9, 11] = 1.0, -1.0
+    got = gpu.gemm_tn(a, b, p, m, n)
+    ref = orc.gemm_tn(a, b, p, m, n)
+    bound = 1e-5 * (np.abs(a).T.astype(np.float64) @ np.abs(b).astype(np.float64)) + 1e-6
+    assert (np.abs(got - ref) <= bound).all()
