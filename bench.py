@@ -245,6 +245,55 @@ def run_train_ops(args):
     print(json.dumps(out), flush=True)
 
 
+def run_ckpt_load(args):
+    """Checkpoint -> device load of the headline model (1.445 GB of f32
+    weights): the direct loader (headers scanned, payload streamed through
+    pinned buffers on several host threads with the CRC on the host and
+    async copies, finiteness checked on the device) against reading the whole
+    file into host memory and uploading it.  The file is written once to a
+    temporary directory and read warm from the page cache (the first load is
+    untimed); prints one JSON line."""
+    import tempfile
+
+    import noetic_b200 as nb
+
+    cfg = nb.LmConfig(**MODEL)
+    gm = nb.Model.new(cfg, MODEL_SEED, device=-1)
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "headline.ckpt")
+        gm.save(path)
+        size = os.path.getsize(path)
+        nb.Model.load(path, device=0).close()
+        direct, direct_first = [], []
+        for _ in range(max(3, args.steps)):
+            t0 = time.perf_counter()
+            m = nb.Model.load(path, device=0)
+            direct.append(time.perf_counter() - t0)
+            dec = nb.Decoder(m, 1)
+            dec.step([0])
+            direct_first.append(time.perf_counter() - t0)
+            dec.close()
+            m.close()
+        host = []
+        for _ in range(2):
+            t0 = time.perf_counter()
+            m = nb.Model.load(path, device=-1)
+            m2 = nb.Model(cfg, device=0)
+            for name, _ in m.tensor_names():
+                m2.set_tensor(name, m.get_tensor(name))
+            dec = nb.Decoder(m2, 1)
+            dec.step([0])  # the host copies reach the device with the first step
+            host.append(time.perf_counter() - t0)
+            dec.close()
+            m.close()
+            m2.close()
+    td, tf, th = statistics.median(direct), statistics.median(direct_first), statistics.median(host)
+    print(json.dumps({"metric": "checkpoint -> device load (d1024 L24 V32768, f32)", "bytes": size,
+                      "direct_load_s": td, "direct_gbs": size / td / 1e9,
+                      "direct_load_to_first_step_s": tf,
+                      "host_read_set_tensor_first_step_s": th, "reads": "page cache (warm)"}), flush=True)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
 
@@ -494,6 +543,8 @@ def main():
                     help="profiling knob: a smaller vocabulary than the headline model")
     ap.add_argument("--train-ops", action="store_true",
                     help="time the training-side ops (gemm_tn, dwconv backward, AdamW) instead")
+    ap.add_argument("--ckpt-load", action="store_true",
+                    help="time the checkpoint -> device load of the headline model instead")
     args = ap.parse_args()
     rank = _env_int("RANK", 0)
     world = _env_int("WORLD_SIZE", 1)
@@ -510,6 +561,9 @@ def main():
                     f"64-token prompts, greedy decode (not the headline configuration)")
     if args.train_ops:
         run_train_ops(args)
+        return
+    if args.ckpt_load:
+        run_ckpt_load(args)
         return
     if args.impl == "reference":
         run_reference(args, rank)

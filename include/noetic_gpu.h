@@ -102,10 +102,20 @@ nk_status nk_model_set_tensor(nk_model *model, const char *name, const float *da
 nk_status nk_model_get_tensor(const nk_model *model, const char *name, float *out,
                               uint64_t numel);
 
+/* ckpt::crc32 (ckpt.rs:35-54): the checkpoint format's CRC-32 (IEEE,
+ * reflected 0xEDB88320), computed the way the loader does it: 16 MiB pieces
+ * CRC'd separately and combined. */
+nk_status nk_crc32(const uint8_t *data, uint64_t n, uint32_t *out);
+
 /* ckpt::load (ckpt.rs:299-383) + the config rules of cmd_gen
  * (cli.rs:909-920) + apply_exact (ckpt.rs:410-436), into a new model on
  * `device`.  Rejects corrupt, truncated, inconsistent or mismatched files
- * with NK_ERR_IO before creating anything. */
+ * with NK_ERR_IO; nothing of a rejected file is returned.  For a device
+ * model the file goes straight to device memory: headers are scanned first,
+ * then the payload is streamed in 16 MiB chunks through pinned buffers by
+ * several host threads (CRC on the host, copies async), the CRC checked at
+ * the end and every value checked finite on the device.  device == -1 reads
+ * the file into a host-only model. */
 nk_status nk_model_load_ckpt(const char *path, int device, nk_model **out);
 
 /* ckpt::save (ckpt.rs:125-200) of the model tensors with the metadata keys

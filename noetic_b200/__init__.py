@@ -79,6 +79,7 @@ SIGNATURES = {
     "nk_model_set_tensor": (_i32, [_P, C.c_char_p, _P, _P, _u32]),
     "nk_model_get_tensor": (_i32, [_P, C.c_char_p, _P, _u64]),
     "nk_model_load_ckpt": (_i32, [C.c_char_p, _i32, C.POINTER(_P)]),
+    "nk_crc32": (_i32, [_P, _u64, C.POINTER(_u32)]),
     "nk_model_save_ckpt": (_i32, [_P, C.c_char_p]),
     "nk_model_loss": (_i32, [_P, _P, _P, _u32, _u32, C.POINTER(C.c_float), _P]),
     "nk_decoder_create": (_i32, [_P, _u32, C.POINTER(_P)]),

@@ -779,4 +779,28 @@ cudaError_t history_push(uint32_t *history, uint32_t *history_len, const uint32_
     return cudaGetLastError();
 }
 
+// *flag = 1 if any of x[0, n) is inf or NaN (checkpoint validation).
+__global__ void any_nonfinite_k(const float *__restrict__ x, size_t n, int *flag) {
+    bool bad = false;
+    const size_t n4 = n / 4;
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = x4[i];
+        bad |= !isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w);
+    }
+    for (size_t i = 4 * n4 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        bad |= !isfinite(x[i]);
+    if (__syncthreads_or(bad) && threadIdx.x == 0) atomicExch(flag, 1);
+}
+
+cudaError_t any_nonfinite(const float *x, size_t n, int *flag, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const size_t blocks = std::min<size_t>((n / 4 + 255) / 256 + 1, (size_t)sms * 8);
+    any_nonfinite_k<<<(unsigned)blocks, 256, 0, st>>>(x, n, flag);
+    return cudaGetLastError();
+}
+
 }  // namespace nk

@@ -220,6 +220,9 @@ struct AdamwParams {
 cudaError_t adamw_step(float *val, const float *grad, float *m, float *v, int64_t n, const AdamwParams &a, int *err,
                        cudaStream_t st);
 
+// *flag = 1 if x[0, n) (16-byte aligned) holds inf or NaN; *flag is not cleared.
+cudaError_t any_nonfinite(const float *x, size_t n, int *flag, cudaStream_t st);
+
 // Sets the thread-local message that nk_last_error() returns.
 void set_last_error(const std::string &msg);
 

@@ -14,10 +14,14 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <thread>
+#include <atomic>
 #include <string>
 #include <vector>
 
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <unistd.h>
 
 #include "../../include/noetic_gpu.h"
 #include "nk_kernels.h"
@@ -167,6 +171,9 @@ struct nk_model {
     float *arena = nullptr;
     size_t arena_floats = 0;
     bool dirty = true;
+    // false after a direct checkpoint load: the device arena holds the
+    // weights and the host copies are filled on demand (ensure_host)
+    bool host_valid = true;
     nk::TcWeights tc;  // tensor-core operand forms (built with the arena)
     // out_w and down_w of every layer stored transposed ([E][d], [H][d] per
     // layer) for the persistent step kernel, built on first use
@@ -182,7 +189,7 @@ struct nk_model {
         Tensor t;
         t.name = name;
         t.shape = std::move(shape);
-        t.host.assign(t.numel(), 0.0f);
+        if (host_valid) t.host.assign(t.numel(), 0.0f);
         tensors.push_back(std::move(t));
         by_name[name] = (int)tensors.size() - 1;
         return (int)tensors.size() - 1;
@@ -217,6 +224,10 @@ struct nk_model {
     // reference's model: emb N(0,1)*0.02; per layer in_proj.w, conv taps
     // q>=1, out_proj.w, up.w, down.w; deterministic gains/biases).
     void init_random(HostRng &rng) {
+        if (!host_valid) {  // every tensor is rewritten below
+            for (auto &t : tensors) t.host.assign(t.numel(), 0.0f);
+            host_valid = true;
+        }
         const uint64_t d = this->d(), e = this->e(), hd = hidden(), k = this->k();
         for (auto &t : tensors) std::fill(t.host.begin(), t.host.end(), 0.0f);
         for (auto &x : tensors[emb].host) x = rng.normal() * 0.02f;
@@ -250,18 +261,35 @@ struct nk_model {
         dirty = true;
     }
 
+    void ensure_arena() {
+        if (arena) return;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        size_t off = 0;
+        for (auto &t : tensors) {
+            t.dev_off = off;
+            off += (t.numel() + 63) & ~size_t(63);  // 256-byte aligned tensors
+        }
+        arena_floats = off;
+        cuda_check(cudaMalloc(&arena, arena_floats * sizeof(float)), "cudaMalloc(weights)");
+    }
+
+    // Host copies of every tensor from the device arena (after a direct load).
+    void ensure_host() {
+        if (host_valid) return;
+        cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        for (auto &t : tensors) {
+            t.host.resize(t.numel());
+            cuda_check(cudaMemcpy(t.host.data(), arena + t.dev_off, t.numel() * sizeof(float), cudaMemcpyDeviceToHost),
+                       "download weights");
+        }
+        host_valid = true;
+    }
+
     void upload() {
         if (!dirty) return;
+        if (!host_valid) fail(NK_ERR_INVALID, "model host copies are stale");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
-        if (!arena) {
-            size_t off = 0;
-            for (auto &t : tensors) {
-                t.dev_off = off;
-                off += (t.numel() + 63) & ~size_t(63);  // 256-byte aligned tensors
-            }
-            arena_floats = off;
-            cuda_check(cudaMalloc(&arena, arena_floats * sizeof(float)), "cudaMalloc(weights)");
-        }
+        ensure_arena();
         for (auto &t : tensors)
             cuda_check(cudaMemcpy(arena + t.dev_off, t.host.data(), t.numel() * sizeof(float),
                                   cudaMemcpyHostToDevice),
@@ -308,6 +336,60 @@ uint32_t crc32(const uint8_t *p, size_t n) {  // ckpt.rs:35-54
     uint32_t crc = 0xFFFFFFFFu;
     for (size_t i = 0; i < n; ++i) crc = table[(crc ^ p[i]) & 0xFF] ^ (crc >> 8);
     return crc ^ 0xFFFFFFFFu;
+}
+
+// ---- the same CRC-32, fast: slicing by 8 (eight table lookups per 8
+// bytes), and the CRC of a concatenation from the CRCs of its parts.
+struct Crc8Tables {
+    uint32_t t[8][256];
+    Crc8Tables() {
+        for (uint32_t i = 0; i < 256; ++i) {
+            uint32_t c = i;
+            for (int b = 0; b < 8; ++b) c = (c & 1) ? (0xEDB88320u ^ (c >> 1)) : (c >> 1);
+            t[0][i] = c;
+        }
+        for (int k = 1; k < 8; ++k)
+            for (uint32_t i = 0; i < 256; ++i) t[k][i] = (t[k - 1][i] >> 8) ^ t[0][t[k - 1][i] & 0xFF];
+    }
+};
+
+uint32_t crc32_fast(const uint8_t *p, size_t n) {
+    static const Crc8Tables T;
+    uint32_t crc = 0xFFFFFFFFu;
+    while (n >= 8) {
+        uint32_t lo, hi;
+        std::memcpy(&lo, p, 4);
+        std::memcpy(&hi, p + 4, 4);
+        lo ^= crc;
+        crc = T.t[7][lo & 0xFF] ^ T.t[6][(lo >> 8) & 0xFF] ^ T.t[5][(lo >> 16) & 0xFF] ^ T.t[4][lo >> 24] ^
+              T.t[3][hi & 0xFF] ^ T.t[2][(hi >> 8) & 0xFF] ^ T.t[1][(hi >> 16) & 0xFF] ^ T.t[0][hi >> 24];
+        p += 8;
+        n -= 8;
+    }
+    while (n--) crc = T.t[0][(crc ^ *p++) & 0xFF] ^ (crc >> 8);
+    return crc ^ 0xFFFFFFFFu;
+}
+
+// Product of two polynomials modulo the CRC polynomial, in the reflected
+// representation the CRC uses (bit 31 is x^0).
+uint32_t crc_mulmod(uint32_t a, uint32_t b) {
+    uint32_t prod = 0;
+    for (uint32_t m = 1u << 31; m; m >>= 1) {
+        if (a & m) prod ^= b;
+        b = (b & 1) ? (b >> 1) ^ 0xEDB88320u : b >> 1;  // b * x
+    }
+    return prod;
+}
+
+// CRC(A || B) from CRC(A), CRC(B) and |B| bytes: CRC(A) times x^(8 |B|), plus
+// CRC(B) (the initial and final inversions cancel in this form).
+uint32_t crc32_combine(uint32_t crc_a, uint32_t crc_b, uint64_t len_b) {
+    uint32_t xp = 1u << 31, base = 1u << 23;  // x^0 and x^8
+    for (; len_b; len_b >>= 1) {
+        if (len_b & 1) xp = crc_mulmod(xp, base);
+        base = crc_mulmod(base, base);
+    }
+    return crc_mulmod(xp, crc_a) ^ crc_b;
 }
 
 struct CkptData {
@@ -1141,6 +1223,7 @@ nk_status nk_model_set_tensor(nk_model *model, const char *name, const float *da
         const uint64_t n = t.numel();
         for (uint64_t i = 0; i < n; ++i)
             if (!std::isfinite(data[i])) fail(NK_ERR_INVALID, std::string("tensor '") + name + "' contains a non-finite value");
+        model->ensure_host();  // the next upload copies every tensor from the host
         std::memcpy(t.host.data(), data, n * sizeof(float));
         model->dirty = true;
     });
@@ -1153,7 +1236,341 @@ nk_status nk_model_get_tensor(const nk_model *model, const char *name, float *ou
         if (it == model->by_name.end()) fail(NK_ERR_INVALID, std::string("unknown tensor '") + name + "'");
         const Tensor &t = model->tensors[it->second];
         if (numel != t.numel()) fail(NK_ERR_INVALID, "wrong element count");
+        const_cast<nk_model *>(model)->ensure_host();
         std::memcpy(out, t.host.data(), numel * sizeof(float));
+    });
+}
+
+namespace {
+
+// Where one tensor's f32 payload sits in a checkpoint file.
+struct CkptTensorRec {
+    std::string name;
+    std::vector<uint64_t> shape;
+    uint64_t numel = 0, file_off = 0;
+};
+
+struct CkptIndex {
+    CkptData meta;  // metadata only (no tensor payloads)
+    std::vector<CkptTensorRec> tensors;  // file order
+    uint64_t body = 0;                   // bytes covered by the CRC
+    uint32_t want_crc = 0;
+};
+
+// ckpt.rs:299-383 without reading the payloads: the header, metadata and
+// every tensor's name / shape / count are parsed with small reads, each
+// payload is skipped; the same structural checks as read_ckpt.
+CkptIndex scan_ckpt(int fd, uint64_t size) {
+    if (size > MAX_CKPT_BYTES) fail(NK_ERR_IO, "checkpoint file exceeds the supported size limit");
+    if (size < 24) fail(NK_ERR_IO, "checkpoint too small");
+    CkptIndex ix;
+    ix.body = size - 4;
+    std::vector<uint8_t> buf(1 << 20);
+    uint64_t buf_pos = 0, buf_len = 0, off = 0;
+    auto fill = [&](uint64_t at, uint64_t want) {
+        const uint64_t len = std::min<uint64_t>(std::max<uint64_t>(want, buf.size()), size - at);
+        if (len > buf.size()) buf.resize(len);
+        uint64_t got = 0;
+        while (got < len) {
+            const ssize_t r = pread(fd, buf.data() + got, len - got, (off_t)(at + got));
+            if (r <= 0) fail(NK_ERR_IO, "checkpoint read failed");
+            got += (uint64_t)r;
+        }
+        buf_pos = at;
+        buf_len = len;
+    };
+    auto take = [&](uint64_t n) -> const uint8_t * {
+        if (n > ix.body - off) fail(NK_ERR_IO, "checkpoint truncated");
+        if (off < buf_pos || off + n > buf_pos + buf_len) fill(off, n);
+        const uint8_t *p = buf.data() + (off - buf_pos);
+        off += n;
+        return p;
+    };
+    auto u32 = [&]() -> uint32_t {
+        const uint8_t *p = take(4);
+        return p[0] | (p[1] << 8) | (p[2] << 16) | ((uint32_t)p[3] << 24);
+    };
+    auto str = [&]() {
+        const uint32_t n = u32();
+        const uint8_t *p = take(n);
+        return std::string((const char *)p, n);
+    };
+    {
+        uint8_t t[4];
+        if (pread(fd, t, 4, (off_t)ix.body) != 4) fail(NK_ERR_IO, "checkpoint read failed");
+        ix.want_crc = t[0] | (t[1] << 8) | (t[2] << 16) | ((uint32_t)t[3] << 24);
+    }
+    if (std::memcmp(take(8), MAGIC, 8) != 0) fail(NK_ERR_IO, "not a noetic checkpoint");
+    if (u32() != 1) fail(NK_ERR_IO, "unsupported checkpoint version");
+    const uint32_t n_meta = u32();
+    if (n_meta > 1000000) fail(NK_ERR_IO, "checkpoint contains too many metadata entries");
+    for (uint32_t i = 0; i < n_meta; ++i) {
+        std::string k = str(), v = str();
+        if (k.empty() || ix.meta.meta.count(k)) fail(NK_ERR_IO, "checkpoint metadata contains an empty or duplicate key");
+        ix.meta.meta[k] = v;
+    }
+    const uint32_t n_t = u32();
+    if (n_t > 1000000) fail(NK_ERR_IO, "checkpoint contains too many tensors");
+    std::map<std::string, int> seen;
+    for (uint32_t i = 0; i < n_t; ++i) {
+        CkptTensorRec r;
+        r.name = str();
+        if (r.name.empty() || seen.count(r.name)) fail(NK_ERR_IO, "checkpoint contains an empty or duplicate tensor name");
+        seen[r.name] = 1;
+        const uint32_t rank = u32();
+        if (rank > 32 || rank > (ix.body - off) / 4) fail(NK_ERR_IO, "checkpoint tensor rank is invalid");
+        r.shape.resize(rank);
+        uint64_t expect = 1;
+        bool overflow = false;
+        for (auto &d : r.shape) {
+            d = u32();
+            if (d != 0 && expect > UINT64_MAX / d) overflow = true;
+            expect *= d;
+        }
+        const uint32_t numel = u32();
+        if (numel > (ix.body - off) / 4) fail(NK_ERR_IO, "checkpoint tensor payload is truncated");
+        if (overflow || expect != numel) fail(NK_ERR_IO, "checkpoint tensor shape does not match its element count");
+        r.numel = numel;
+        r.file_off = off;
+        off += 4ull * numel;  // the payload, read by the streaming pass
+        ix.tensors.push_back(std::move(r));
+    }
+    if (off != ix.body) fail(NK_ERR_IO, "checkpoint has trailing data");
+    return ix;
+}
+
+// The checkpoint body streamed from the file straight into device memory:
+// worker threads take CKPT_CHUNK-byte chunks in turn, read each into one of
+// two pinned buffers, CRC it, and copy the payload bytes it holds to their
+// device destinations with cudaMemcpyAsync on the thread's own stream; the
+// chunk CRCs are combined in file order at the end.  dest[i] is tensor i's
+// device address (every tensor, aux.* included, has one).
+constexpr uint64_t CKPT_CHUNK = 16ull << 20;
+constexpr unsigned CKPT_THREADS = 16;
+
+// Pinned staging buffers (two per loader thread), allocated on the first
+// load and kept for later ones: pinning memory costs more than reading it.
+struct PinnedPool {
+    std::mutex mu;
+    std::vector<uint8_t *> free;
+    uint8_t *take() {
+        std::lock_guard<std::mutex> g(mu);
+        if (!free.empty()) {
+            uint8_t *p = free.back();
+            free.pop_back();
+            return p;
+        }
+        uint8_t *p = nullptr;
+        return cudaHostAlloc((void **)&p, CKPT_CHUNK, cudaHostAllocPortable) == cudaSuccess ? p : nullptr;
+    }
+    void give(uint8_t *p) {
+        if (!p) return;
+        std::lock_guard<std::mutex> g(mu);
+        free.push_back(p);
+    }
+};
+PinnedPool &pinned_pool() {
+    static PinnedPool *pool = new PinnedPool();
+    return *pool;
+}
+
+uint32_t stream_ckpt_to_device(int fd, int device, const CkptIndex &ix, const std::vector<char *> &dest) {
+    const uint64_t n_chunks = (ix.body + CKPT_CHUNK - 1) / CKPT_CHUNK;
+    std::vector<uint32_t> crc(n_chunks, 0);
+    std::atomic<uint64_t> next{0};
+    std::mutex err_mu;
+    std::string err;
+    auto worker = [&]() {
+        cudaStream_t st = nullptr;
+        uint8_t *pin[2] = {nullptr, nullptr};
+        cudaEvent_t ev[2] = {nullptr, nullptr};
+        auto set_err = [&](const std::string &m) {
+            std::lock_guard<std::mutex> g(err_mu);
+            if (err.empty()) err = m;
+        };
+        if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess ||
+            !(pin[0] = pinned_pool().take()) || !(pin[1] = pinned_pool().take()) ||
+            cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming) != cudaSuccess) {
+            set_err("checkpoint staging buffers could not be allocated");
+        } else {
+            int b = 0;
+            for (;;) {
+                {
+                    std::lock_guard<std::mutex> g(err_mu);
+                    if (!err.empty()) break;
+                }
+                const uint64_t c = next.fetch_add(1);
+                if (c >= n_chunks) break;
+                const uint64_t c0 = c * CKPT_CHUNK, len = std::min(CKPT_CHUNK, ix.body - c0);
+                if (cudaEventSynchronize(ev[b]) != cudaSuccess) {  // the buffer's previous copies are done
+                    set_err("checkpoint upload failed");
+                    break;
+                }
+                uint64_t got = 0;
+                while (got < len) {
+                    const ssize_t r = pread(fd, pin[b] + got, len - got, (off_t)(c0 + got));
+                    if (r <= 0) break;
+                    got += (uint64_t)r;
+                }
+                if (got != len) {
+                    set_err("checkpoint read failed");
+                    break;
+                }
+                crc[c] = crc32_fast(pin[b], len);
+                // Payloads overlapping [c0, c0 + len): the first one ending after c0.
+                size_t lo = 0, hi = ix.tensors.size();
+                while (lo < hi) {
+                    const size_t mid = (lo + hi) / 2;
+                    const CkptTensorRec &t = ix.tensors[mid];
+                    if (t.file_off + 4 * t.numel <= c0)
+                        lo = mid + 1;
+                    else
+                        hi = mid;
+                }
+                bool ok = true;
+                for (size_t i = lo; i < ix.tensors.size() && ix.tensors[i].file_off < c0 + len; ++i) {
+                    const CkptTensorRec &t = ix.tensors[i];
+                    const uint64_t s0 = std::max(t.file_off, c0), s1 = std::min(t.file_off + 4 * t.numel, c0 + len);
+                    if (s1 <= s0) continue;
+                    ok &= cudaMemcpyAsync(dest[i] + (s0 - t.file_off), pin[b] + (s0 - c0), s1 - s0,
+                                          cudaMemcpyHostToDevice, st) == cudaSuccess;
+                }
+                ok &= cudaEventRecord(ev[b], st) == cudaSuccess;
+                if (!ok) {
+                    set_err("checkpoint upload failed");
+                    break;
+                }
+                b ^= 1;
+            }
+        }
+        if (st) cudaStreamSynchronize(st);
+        for (int k = 0; k < 2; ++k) {
+            if (ev[k]) cudaEventDestroy(ev[k]);
+            pinned_pool().give(pin[k]);
+        }
+        if (st) cudaStreamDestroy(st);
+    };
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const unsigned n_threads = (unsigned)std::min<uint64_t>({CKPT_THREADS, hw, std::max<uint64_t>(n_chunks, 1)});
+    std::vector<std::thread> pool;
+    for (unsigned i = 0; i < n_threads; ++i) pool.emplace_back(worker);
+    for (auto &t : pool) t.join();
+    if (!err.empty()) fail(NK_ERR_IO, err);
+    uint32_t total = n_chunks ? crc[0] : crc32_fast(nullptr, 0);
+    for (uint64_t c = 1; c < n_chunks; ++c)
+        total = crc32_combine(total, crc[c], std::min(CKPT_CHUNK, ix.body - c * CKPT_CHUNK));
+    return total;
+}
+
+nk_config ckpt_config(const CkptData &c) {
+    nk_config cfg{};  // cmd_gen's metadata rules (cli.rs:909-920)
+    cfg.vocab = meta_usize(c, "vocab");
+    cfg.d_model = meta_usize(c, "d_model");
+    cfg.n_layer = meta_usize(c, "n_layer");
+    cfg.expand = meta_usize(c, "expand");
+    cfg.conv_k = meta_usize(c, "conv_k");
+    cfg.mlp_mult = meta_usize(c, "mlp_mult");
+    cfg.eps = meta_f32(c, "eps", false, 1e-5f);
+    cfg.tau_max = meta_f32(c, "tau_max", true, 0.0f);
+    std::string e = config_error(cfg);
+    if (!e.empty()) fail(NK_ERR_IO, "checkpoint model configuration is invalid: " + e);
+    return cfg;
+}
+
+// The direct loader (device models): scan, create the model and its device
+// arena, stream the payloads into it, then check the CRC and that every
+// value is finite on the device.  Nothing of a rejected file is returned.
+nk_model *load_ckpt_direct(const char *path, int device) {
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) fail(NK_ERR_IO, std::string("cannot open checkpoint ") + path);
+    std::unique_ptr<int, void (*)(int *)> ofd(new int(fd), [](int *f) {
+        close(*f);
+        delete f;
+    });
+    const off_t size = lseek(fd, 0, SEEK_END);
+    if (size < 0) fail(NK_ERR_IO, "cannot size the checkpoint file");
+    const CkptIndex ix = scan_ckpt(fd, (uint64_t)size);
+    nk_config cfg = ckpt_config(ix.meta);
+    nk_model *m = nullptr;
+    {
+        std::string e = config_error(cfg);
+        if (!e.empty()) fail(NK_ERR_IO, "checkpoint model configuration is invalid: " + e);
+        e = device_limits_error(cfg);
+        if (!e.empty()) fail(NK_ERR_UNSUPPORTED, e);
+        int n = 0;
+        cuda_check(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+        if (device < 0 || device >= n) fail(NK_ERR_INVALID, "device index out of range");
+        m = new nk_model();
+        m->cfg = cfg;
+        m->device = device;
+        m->host_valid = false;  // no host copies: the arena is filled directly
+        m->build_layout();
+    }
+    std::unique_ptr<nk_model> own(m);
+    // apply_exact (ckpt.rs:410-436): the exact model tensor set; aux.* is
+    // checked (CRC, finite) but not kept.
+    size_t model_tensors = 0;
+    uint64_t aux_bytes = 0;
+    for (const auto &t : ix.tensors) {
+        if (t.name.rfind("aux.", 0) == 0)
+            aux_bytes += (4 * t.numel + 255) & ~uint64_t(255);
+        else
+            ++model_tensors;
+    }
+    if (model_tensors != own->tensors.size()) fail(NK_ERR_IO, "checkpoint tensor set does not exactly match the model");
+    std::map<std::string, const CkptTensorRec *> by_name;
+    for (const auto &t : ix.tensors) by_name[t.name] = &t;
+    for (auto &t : own->tensors) {
+        auto it = by_name.find(t.name);
+        if (it == by_name.end()) fail(NK_ERR_IO, "checkpoint is missing tensor '" + t.name + "'");
+        if (it->second->shape != t.shape) fail(NK_ERR_IO, "checkpoint tensor '" + t.name + "' has the wrong shape");
+    }
+    own->ensure_arena();
+    cuda_check(cudaMemset(own->arena, 0, own->arena_floats * sizeof(float)), "memset");  // padding stays finite
+    char *aux = nullptr;
+    if (aux_bytes) cuda_check(cudaMalloc(&aux, aux_bytes), "cudaMalloc(aux tensors)");
+    std::unique_ptr<char, void (*)(char *)> oaux(aux, [](char *q) {
+        if (q) cudaFree(q);
+    });
+    if (aux) cuda_check(cudaMemset(aux, 0, aux_bytes), "memset");
+    std::vector<char *> dest;
+    uint64_t aux_off = 0;
+    for (const auto &t : ix.tensors) {
+        if (t.name.rfind("aux.", 0) == 0) {
+            dest.push_back(aux + aux_off);
+            aux_off += (4 * t.numel + 255) & ~uint64_t(255);
+        } else {
+            dest.push_back((char *)(own->arena + own->tensors[own->by_name.at(t.name)].dev_off));
+        }
+    }
+    const uint32_t got = stream_ckpt_to_device(fd, device, ix, dest);
+    if (got != ix.want_crc) fail(NK_ERR_IO, "checkpoint CRC mismatch (corrupt file)");
+    int *flag = nullptr;
+    dalloc(&flag, 1, "flag");
+    std::unique_ptr<int, void (*)(int *)> oflag(flag, [](int *q) { cudaFree(q); });
+    cuda_check(cudaMemset(flag, 0, sizeof(int)), "memset");
+    cuda_check(nk::any_nonfinite(own->arena, own->arena_floats, flag, nullptr), "finite check");
+    if (aux) cuda_check(nk::any_nonfinite((const float *)aux, aux_bytes / 4, flag, nullptr), "finite check");
+    int h = 0;
+    cuda_check(cudaMemcpy(&h, flag, sizeof(int), cudaMemcpyDeviceToHost), "finite check");
+    if (h) fail(NK_ERR_IO, "checkpoint tensor contains a non-finite value");
+    own->dirty = false;
+    return own.release();
+}
+
+}  // namespace
+
+nk_status nk_crc32(const uint8_t *data, uint64_t n, uint32_t *out) {
+    return guard([&] {
+        if (!out || (n && !data)) fail(NK_ERR_INVALID, "null argument");
+        // The loader's form: CKPT_CHUNK pieces, CRC'd separately, combined.
+        uint32_t total = crc32_fast(data, std::min(n, CKPT_CHUNK));
+        for (uint64_t c0 = CKPT_CHUNK; c0 < n; c0 += CKPT_CHUNK) {
+            const uint64_t len = std::min(CKPT_CHUNK, n - c0);
+            total = crc32_combine(total, crc32_fast(data + c0, len), len);
+        }
+        *out = total;
     });
 }
 
@@ -1161,6 +1578,10 @@ nk_status nk_model_load_ckpt(const char *path, int device, nk_model **out) {
     return guard([&] {
         if (!path || !out) fail(NK_ERR_INVALID, "null argument");
         *out = nullptr;
+        if (device >= 0) {
+            *out = load_ckpt_direct(path, device);
+            return;
+        }
         CkptData c = read_ckpt(path);
         nk_config cfg{};  // cmd_gen's metadata rules (cli.rs:909-920)
         cfg.vocab = meta_usize(c, "vocab");
@@ -1196,6 +1617,7 @@ nk_status nk_model_load_ckpt(const char *path, int device, nk_model **out) {
 nk_status nk_model_save_ckpt(const nk_model *model, const char *path) {
     return guard([&] {
         if (!model || !path) fail(NK_ERR_INVALID, "null argument");
+        const_cast<nk_model *>(model)->ensure_host();
         const nk_config &c = model->cfg;
         std::vector<std::pair<std::string, std::string>> meta = {
             {"vocab", std::to_string(c.vocab)},       {"d_model", std::to_string(c.d_model)},

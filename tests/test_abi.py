@@ -163,3 +163,17 @@ def test_training_ops_refuse_bad_arguments_before_any_device_work(nb):
     assert e.value.status == nb.NK_ERR_INVALID
     # Empty products need no device either.
     assert nb.gemm_tn(np.zeros(0), np.zeros(0), 0, 0, 5).shape == (0, 5)
+
+
+def test_crc32_pieces_combine_to_the_reference_crc(nb):
+    # ckpt::crc32 (ckpt.rs:35-54) is zlib's CRC-32; the library computes it in
+    # 16 MiB pieces combined by polynomial arithmetic, as the loader does.
+    import ctypes
+    import zlib
+
+    rng = np.random.default_rng(4)
+    for n in [0, 1, 7, 8, 9, 1000, (16 << 20) - 1, 16 << 20, (16 << 20) + 1, (40 << 20) + 12345]:
+        data = rng.integers(0, 256, n, dtype=np.uint8)
+        out = ctypes.c_uint32(0)
+        nb._check(nb.lib().nk_crc32(data.ctypes.data_as(ctypes.c_void_p), n, ctypes.byref(out)))
+        assert out.value == zlib.crc32(data.tobytes()), n
