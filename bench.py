@@ -294,6 +294,100 @@ def run_ckpt_load(args):
                       "host_read_set_tensor_first_step_s": th, "reads": "page cache (warm)"}), flush=True)
 
 
+LONG_MODEL = dict(vocab=16384, d_model=768, n_layer=12, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+LONG_SEED, LONG_STREAMS, LONG_PROMPT, LONG_DECODE = 3, 64, 32768, 64
+
+
+def run_long_prefill(args, rank, world, local_rank):
+    """The long-prompt prefill workload: d768 L12 V16384 (seed 3), 64 streams
+    x 32768-token uniform-random prompts (stream s: Rng::new(6000 + s)) through
+    the time-chunked associative scan fused with the causal conv, then 64
+    greedy decode tokens; streams sharded over the ranks.  Prefill is timed on
+    the device (max over ranks) after one untimed full run; the projections'
+    share comes from the decoder's own per-launch CUDA events.  Prints one
+    JSON line on rank 0."""
+    import torch
+
+    import noetic_b200 as nb
+    from noetic_b200.prompts import uniform_prompts
+    from noetic_b200.shard import shard_range
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    first, count = shard_range(LONG_STREAMS, world, rank)
+    cfg = nb.LmConfig(**LONG_MODEL)
+    gm = nb.Model.new(cfg, LONG_SEED, device=local_rank)
+    ids = uniform_prompts(count, LONG_PROMPT, cfg.vocab, 6000, first)
+    dec = nb.Decoder(gm, count)
+    stream = torch.cuda.ExternalStream(dec.cuda_stream())
+    dec.prefill(ids, want_logits=False)  # sizes buffers, builds operands
+    dec.reset()
+    barrier()
+    torch.cuda.synchronize()
+    dec.profile_begin()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    dec.prefill(ids, want_logits=False)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prof = dec.profile_end()
+    prefill_ms = max_over_ranks(e0.elapsed_time(e1))
+    barrier()
+    greedy = nb.SampleCfg(greedy=True, rep_penalty=1.0)
+    tok = torch.from_numpy(dec.sample(greedy, np.zeros((count, 4), np.uint64)).astype(np.int32)).cuda()
+    nxt = torch.empty_like(tok)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(LONG_DECODE):
+        dec.step_greedy_device(tok.data_ptr(), nxt.data_ptr())
+        tok, nxt = nxt, tok
+    e1.record(stream)
+    torch.cuda.synchronize()
+    decode_ms = max_over_ranks(e0.elapsed_time(e1))
+    if rank == 0:
+        peaks, basis = load_peaks()
+        tokens = LONG_STREAMS * LONG_PROMPT
+        E, H, d, L = cfg.d_model * cfg.expand, cfg.d_model * cfg.mlp_mult, cfg.d_model, cfg.n_layer
+        flops = 2.0 * tokens * L * (3 * E * d + d * E + 2 * H * d + d * H)  # no logits until the last position
+        proj_s = prof["proj_ms"] / 1000.0
+        rest_ms = max(prefill_ms - prof["proj_ms"], 1e-6)
+        scan_bytes = 16.0 * E * L * tokens  # per layer and token: u[3E] read, y[E] written (f32)
+        print(json.dumps({
+            "metric": "long-prompt prefill tokens/s (d768 L12 V16384, 64 streams x 32768 tokens)",
+            "value": tokens / (prefill_ms / 1000.0), "unit": "tokens/s", "n_gpus": world, "ms": prefill_ms,
+            "data": "synthetic (seeded random-init weights Lm::new seed 3, prompt ids Rng::new(6000+s).below(16384))",
+            "projections": {"ms": prof["proj_ms"], "tflops": flops / proj_s / 1e12 if proj_s > 0 else None,
+                            "frac": (flops / proj_s / 1e12) / (peaks["bf16_tflops_sustained"] / 2 / 3)
+                            if proj_s > 0 else None, "launches": prof["proj_launches"],
+                            "engine": "tcgen05 3xTF32" if prof["tensor_core"] else "f32 CUDA cores"},
+            "outside_projections": {"ms": rest_ms, "gbs_scan_conv_lower_bound": scan_bytes / rest_ms / 1e6,
+                                    "note": "scan + conv + norms + gathers; bytes counted for the scan and conv only"},
+            "decode": {"tokens_per_s": LONG_STREAMS * LONG_DECODE / (decode_ms / 1000.0), "ms": decode_ms,
+                       "tokens": LONG_DECODE},
+            "peak_basis": basis}), flush=True)
+    dec.close()
+    gm.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
 
@@ -545,6 +639,8 @@ def main():
                     help="time the training-side ops (gemm_tn, dwconv backward, AdamW) instead")
     ap.add_argument("--ckpt-load", action="store_true",
                     help="time the checkpoint -> device load of the headline model instead")
+    ap.add_argument("--long-prefill", action="store_true",
+                    help="time the long-prompt prefill workload (d768 L12, 64 x 32768 tokens) instead")
     args = ap.parse_args()
     rank = _env_int("RANK", 0)
     world = _env_int("WORLD_SIZE", 1)
@@ -564,6 +660,9 @@ def main():
         return
     if args.ckpt_load:
         run_ckpt_load(args)
+        return
+    if args.long_prefill:
+        run_long_prefill(args, rank, world, local_rank)
         return
     if args.impl == "reference":
         run_reference(args, rank)

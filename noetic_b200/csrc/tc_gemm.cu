@@ -1109,8 +1109,11 @@ cudaError_t split(const float *src, int ld, float *hi, float *lo, int rows, int 
 
 }  // namespace
 
+// Any M: a tile past the last row reads zeros (the A map's rows beyond M
+// are filled, never read) and the epilogues mask rows >= M, so 9..127
+// streams take one 128-row tile instead of the CUDA-core GEMM.
 bool tc_eligible(int M, int N, int K) {
-    return M >= BM && N >= 128 && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
+    return M >= 1 && N >= 128 && K >= 8 && K % 4 == 0 && encode_fn() != nullptr;
 }
 
 int sm_count_cached() {

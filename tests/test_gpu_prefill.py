@@ -139,3 +139,40 @@ def test_prefill_rejects_bad_input(gpu, orc):
         dec.prefill(np.array([[1, 2], [3, 19]], dtype=np.uint32))
     with pytest.raises(gpu.NoeticError):
         dec.prefill(np.array([[1, 2], [3, 4]], dtype=np.uint32), lens=[3, 1])
+
+
+def test_long_prompt_prefill_at_full_length(gpu):
+    """The long-prompt prefill shape (d768, 12 layers, vocab 16384, 32768-token
+    prompts, stream s from Rng::new(6000 + s)): the time-chunked scan prefill
+    leaves the state the sequential scan prefill leaves (scan.rs:286, 1e-4)
+    and the state that stepping every token through the decoder leaves (the
+    decoder is pinned to the oracle by the streaming tests), with the same
+    last-position logits.  Size-independent checks at the full length, where
+    the oracle would take hours."""
+    import torch
+
+    from noetic_b200.prompts import uniform_prompts
+
+    kw = dict(vocab=16384, d_model=768, n_layer=12, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    gm = gpu.Model.new(gpu.LmConfig(**kw), 3)
+    S, T = 2, 32768
+    ids = uniform_prompts(S, T, kw["vocab"], 6000)
+    a, b = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    a.set_engine(CHUNKED)
+    b.set_engine(SEQ)
+    la, lb = a.prefill(ids).copy(), b.prefill(ids).copy()
+    # Stepping: the prompt columns already on the device, one step per token.
+    c = gpu.Decoder(gm, S)
+    cols = torch.from_numpy(np.ascontiguousarray(ids.T).astype(np.int32)).cuda()
+    out = torch.empty(S, dtype=torch.int32, device="cuda")
+    for t in range(T - 1):
+        c.step_greedy_device(cols[t].data_ptr(), out.data_ptr())
+    torch.cuda.synchronize()
+    lc = c.step(ids[:, T - 1]).copy()
+    sa, ha = a.get_state()
+    sb, hb = b.get_state()
+    sc, hc = c.get_state()
+    assert np.array_equal(ha, hb) and np.array_equal(ha, hc)
+    assert state_rel_err(sa, sb) <= STATE_TOL
+    assert state_rel_err(sa, sc) <= STATE_TOL
+    assert np.abs(la - lb).max() <= LOGIT_TOL and np.abs(la - lc).max() <= LOGIT_TOL
