@@ -176,3 +176,45 @@ def test_long_prompt_prefill_at_full_length(gpu):
     assert state_rel_err(sa, sb) <= STATE_TOL
     assert state_rel_err(sa, sc) <= STATE_TOL
     assert np.abs(la - lb).max() <= LOGIT_TOL and np.abs(la - lc).max() <= LOGIT_TOL
+
+
+def test_prefill_then_decode_at_the_4096_stream_shape(gpu, orc):
+    """d512 L8 V8192 (seed 1), 4096 streams x 512-token prompts (stream s from
+    Rng::new(4000 + s)), the scan prefill then greedy steps: streams spread
+    over the batch against the oracle's batched forward and its decoder,
+    teacher-forced with the oracle's tokens."""
+    from noetic_b200.prompts import uniform_prompts
+
+    kw = dict(vocab=8192, d_model=512, n_layer=8, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=1)
+    S, T = 4096, 512
+    ids = uniform_prompts(S, T, kw["vocab"], 4000)
+    dec = gpu.Decoder(gm, S)
+    last = dec.prefill(ids).copy()
+    st, heads = dec.get_state()
+    probe = [0, 1365, 2730, 4095]
+    ods = []
+    for s in probe:
+        ost, oh, olast = om.prefill_state(ids[s], 1, T)
+        assert heads[s] == oh[0], s
+        assert state_rel_err(st[s], ost[0]) <= STATE_TOL, s
+        assert np.abs(last[s] - olast[0]).max() <= LOGIT_TOL, s
+        od = orc.Decoder(om)
+        od.set_state(ost[0], int(oh[0]))
+        ods.append((od, olast[0].copy()))
+    # Greedy steps, the probed streams fed the oracle's own tokens.
+    toks = np.array([orc.argmax(row) for row in last], dtype=np.uint32)
+    checked = 0
+    for step in range(4):
+        for i, s in enumerate(probe):
+            toks[s] = orc.argmax(ods[i][1])
+        nxt = dec.step_greedy(toks).copy()
+        for i, s in enumerate(probe):
+            lg = ods[i][0].step(int(toks[s])).copy()
+            top2 = np.sort(lg)[-2:]
+            if top2[1] - top2[0] > LOGIT_TOL:
+                assert int(nxt[s]) == orc.argmax(lg), (step, s)
+                checked += 1
+            ods[i] = (ods[i][0], lg)
+        toks = nxt
+    assert checked >= 12
