@@ -264,6 +264,7 @@ __global__ void ssm_prefill_seq_k(const float *__restrict__ u, float *__restrict
 
 // ---- time-parallel prefill: blocks of TB positions per (stream, channel)
 constexpr int TB = 64;
+constexpr int PB = 8;  // positions whose operands are loaded ahead of use
 
 __device__ __forceinline__ float raw_v(const float *ur, const float *ring, uint32_t head0, int k,
                                        int p, int E, int j) {
@@ -275,7 +276,9 @@ __device__ __forceinline__ float raw_v(const float *ur, const float *ring, uint3
 }
 
 // Pass 1: local scan of one time block from h = 0; writes h_local into y and
-// the block's (decay product, final local h).
+// the block's (decay product, final local h).  KW > 0: conv widths k <= KW,
+// the window of raw v in registers; KW == 0: any width, every tap loaded.
+template <int KW>
 __global__ void ssm_chunk_local_k(const float *__restrict__ u, const float *__restrict__ state,
                                   const uint32_t *__restrict__ heads, const uint32_t *__restrict__ lens,
                                   int t0, int tc, const float *__restrict__ conv_w,
@@ -297,15 +300,48 @@ __global__ void ssm_chunk_local_k(const float *__restrict__ u, const float *__re
         const uint32_t head0 = heads[s];
         const float bias = conv_b[j];
         float *yr = y + (size_t)s * tc * E;
-        for (int p = p0; p < p1; ++p) {
-            float sum = bias;
-            for (int q = 0; q < k; ++q)
-                sum = sum + conv_w[(size_t)q * E + j] * raw_v(ur, ring, head0, k, p - q, E, j);
-            const float value = silu(sum);
-            const float decay = sigmoid(ur[(size_t)p * 3 * E + E + j]);
-            h = decay * h + (1.0f - decay) * value;
-            A = A * decay;
-            yr[(size_t)p * E + j] = h;
+        // Conv taps and the window of raw v in registers: before position p
+        // is shifted in, win[q] = v at p - 1 - q (so after the shift win[q] =
+        // v at p - q).  The operands of PB positions are loaded ahead of
+        // their use, so the loads overlap instead of waiting one round trip
+        // per position.
+        constexpr int W = KW > 0 ? KW : 1;
+        float cw[W], win[W];
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+            cw[q] = q < k ? conv_w[(size_t)q * E + j] : 0.0f;
+            win[q] = (KW > 0 && q + 1 < k) ? raw_v(ur, ring, head0, k, p0 - 1 - q, E, j) : 0.0f;
+        }
+        for (int pb = p0; pb < p1; pb += PB) {
+            float vv[PB], zz[PB];
+#pragma unroll
+            for (int e = 0; e < PB; ++e) {
+                const int p = pb + e;
+                vv[e] = p < p1 ? ur[(size_t)p * 3 * E + j] : 0.0f;
+                zz[e] = p < p1 ? ur[(size_t)p * 3 * E + E + j] : 0.0f;
+            }
+#pragma unroll
+            for (int e = 0; e < PB; ++e) {
+                const int p = pb + e;
+                if (p >= p1) break;
+                float sum = bias;
+                if constexpr (KW > 0) {
+#pragma unroll
+                    for (int q = W - 1; q > 0; --q) win[q] = win[q - 1];
+                    win[0] = vv[e];
+#pragma unroll
+                    for (int q = 0; q < W; ++q)
+                        if (q < k) sum = sum + cw[q] * win[q];
+                } else {
+                    for (int q = 0; q < k; ++q)
+                        sum = sum + conv_w[(size_t)q * E + j] * (q == 0 ? vv[e] : raw_v(ur, ring, head0, k, p - q, E, j));
+                }
+                const float value = silu(sum);
+                const float decay = sigmoid(zz[e]);
+                h = decay * h + (1.0f - decay) * value;
+                A = A * decay;
+                yr[(size_t)p * E + j] = h;
+            }
         }
     }
     blkA[i] = A;
@@ -352,11 +388,24 @@ __global__ void ssm_chunk_fix_k(const float *__restrict__ u, float *__restrict__
     const float *ur = u + (size_t)s * tc * 3 * E;
     const float cin = carry[i];
     float P = 1.0f, h = 0.0f;
-    for (int p = p0; p < p1; ++p) {
-        const float decay = sigmoid(ur[(size_t)p * 3 * E + E + j]);
-        P = P * decay;
-        h = yr[(size_t)p * E + j] + P * cin;
-        put(yout, ybase + (size_t)p * E, h * silu(ur[(size_t)p * 3 * E + 2 * E + j]));
+    for (int pb = p0; pb < p1; pb += PB) {
+        float zz[PB], oo[PB], yl[PB];  // loaded PB positions ahead
+#pragma unroll
+        for (int e = 0; e < PB; ++e) {
+            const int p = pb + e;
+            zz[e] = p < p1 ? ur[(size_t)p * 3 * E + E + j] : 0.0f;
+            oo[e] = p < p1 ? ur[(size_t)p * 3 * E + 2 * E + j] : 0.0f;
+            yl[e] = p < p1 ? yr[(size_t)p * E + j] : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < PB; ++e) {
+            const int p = pb + e;
+            if (p >= p1) break;
+            const float decay = sigmoid(zz[e]);
+            P = P * decay;
+            h = yl[e] + P * cin;
+            put(yout, ybase + (size_t)p * E, h * silu(oo[e]));
+        }
     }
     for (int p = p1; p < min(tc, p0 + TB); ++p) put(yout, ybase + (size_t)p * E, 0.0f);
     if (p1 == nv) {
@@ -705,8 +754,15 @@ cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *he
     const size_t per = (size_t)S * nblk * E;
     float *blkA = scratch, *blkH = scratch + per, *carry = scratch + 2 * per;
     const int64_t n = (int64_t)per;
-    ssm_chunk_local_k<<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, conv_w,
-                                                          conv_b, y, blkA, blkH, S, E, k, nblk);
+    if (k <= 4)
+        ssm_chunk_local_k<4><<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, y,
+                                                                 blkA, blkH, S, E, k, nblk);
+    else if (k <= 8)
+        ssm_chunk_local_k<8><<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, y,
+                                                                 blkA, blkH, S, E, k, nblk);
+    else
+        ssm_chunk_local_k<0><<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, y,
+                                                                 blkA, blkH, S, E, k, nblk);
     ssm_chunk_carry_k<<<blocks_for((int64_t)S * E, 128), 128, 0, st>>>(state, lens, t0, tc, blkA,
                                                                        blkH, carry, S, E, k, nblk);
     ssm_chunk_fix_k<<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, y, yout, carry,
