@@ -294,6 +294,55 @@ def run_ckpt_load(args):
                       "host_read_set_tensor_first_step_s": th, "reads": "page cache (warm)"}), flush=True)
 
 
+def run_scan(args):
+    """The stand-alone scans (scan.rs:35-260) on device-resident f32 arrays:
+    the sequential and time-chunked forms of h_t = a_t h_{t-1} + b_t and of the
+    adjoint c_t = g_t + a_{t+1} c_{t+1}, at the long-prompt prefill's scan shape
+    (64 x 32768 x 768: one layer of 64 prompts of 32768 tokens) and at a
+    many-streams shape (4096 x 512 x 512).  Algorithmic bytes: a and b read, h
+    written, 12 per element.  Prints one JSON line."""
+    import torch
+
+    import noetic_b200 as nb
+
+    L = nb.lib()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    st = stream.cuda_stream
+    peaks, basis = load_peaks()
+    reps = max(3, args.steps)
+    out = {"metric": "stand-alone scans (scan.rs), GB/s of algorithmic bytes", "peak_gbs": peaks["hbm_gbs"],
+           "peak_basis": basis}
+    for name, (B, T, D) in [("long_prompt", (64, 32768, 768)), ("many_streams", (4096, 512, 512))]:
+        n = B * T * D
+        a = torch.rand(n, device="cuda")
+        b = torch.randn(n, device="cuda")
+        h = torch.empty(n, device="cuda")
+        res = {}
+        for label, fn in [
+            ("sequential", lambda: L.nk_scan_device(a.data_ptr(), b.data_ptr(), h.data_ptr(), B, T, D, 0, st)),
+            ("chunked", lambda: L.nk_scan_device(a.data_ptr(), b.data_ptr(), h.data_ptr(), B, T, D, 1, st)),
+            ("adjoint_sequential",
+             lambda: L.nk_scan_adjoint_device(a.data_ptr(), b.data_ptr(), h.data_ptr(), B, T, D, 0, st)),
+            ("adjoint_chunked",
+             lambda: L.nk_scan_adjoint_device(a.data_ptr(), b.data_ptr(), h.data_ptr(), B, T, D, 1, st)),
+        ]:
+            for _ in range(args.warmup):
+                nb._check(fn())
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                nb._check(fn())
+            e1.record(stream)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            res[label] = {"ms": ms, "gbs": 12.0 * n / ms / 1e6, "frac": 12.0 * n / ms / 1e6 / peaks["hbm_gbs"]}
+        out[name] = {"shape": [B, T, D], **res}
+        del a, b, h
+    print(json.dumps(out), flush=True)
+
+
 LONG_MODEL = dict(vocab=16384, d_model=768, n_layer=12, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
 LONG_SEED, LONG_STREAMS, LONG_PROMPT, LONG_DECODE = 3, 64, 32768, 64
 
@@ -639,6 +688,7 @@ def main():
                     help="time the training-side ops (gemm_tn, dwconv backward, AdamW) instead")
     ap.add_argument("--ckpt-load", action="store_true",
                     help="time the checkpoint -> device load of the headline model instead")
+    ap.add_argument("--scan", action="store_true", help="time the stand-alone scans instead")
     ap.add_argument("--long-prefill", action="store_true",
                     help="time the long-prompt prefill workload (d768 L12, 64 x 32768 tokens) instead")
     args = ap.parse_args()
@@ -663,6 +713,9 @@ def main():
         return
     if args.long_prefill:
         run_long_prefill(args, rank, world, local_rank)
+        return
+    if args.scan:
+        run_scan(args)
         return
     if args.impl == "reference":
         run_reference(args, rank)

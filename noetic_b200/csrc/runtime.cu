@@ -2074,48 +2074,6 @@ nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out) {
     });
 }
 
-nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
-                         int chunked, void *stream) {
-    return guard([&] {
-        if (batch * t * d == 0) return;
-        if (!a || !b || !h) fail(NK_ERR_INVALID, "null argument");
-        cudaStream_t st = (cudaStream_t)stream;
-        if (!chunked) {
-            cuda_check(nk::scan_sequential(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan");
-            return;
-        }
-        float *scratch = nullptr;
-        dalloc(&scratch, nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d), "scan scratch");
-        cudaError_t e = nk::scan_chunked(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, scratch, st);
-        cudaError_t e2 = cudaStreamSynchronize(st);
-        cudaFree(scratch);
-        cuda_check(e, "scan");
-        cuda_check(e2, "scan sync");
-    });
-}
-
-nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
-                                 int chunked, void *stream) {
-    return guard([&] {
-        if (batch * t * d == 0) return;
-        if (!a || !g || !c) fail(NK_ERR_INVALID, "null argument");
-        cudaStream_t st = (cudaStream_t)stream;
-        if (!chunked) {
-            cuda_check(nk::scan_adjoint_sequential(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan adjoint");
-            return;
-        }
-        float *scratch = nullptr;
-        dalloc(&scratch, nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d), "scan scratch");
-        cudaError_t e = nk::scan_adjoint_chunked(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, scratch, st);
-        cudaError_t e2 = cudaStreamSynchronize(st);
-        cudaFree(scratch);
-        cuda_check(e, "scan adjoint");
-        cuda_check(e2, "scan adjoint sync");
-    });
-}
-
-// ---------------------------------------------------------------- training-side ops
-
 namespace {
 // Scratch for the synchronous stand-alone ops, kept per device between calls
 // (grown on demand up to 8 GiB; larger requests allocate for the call).
@@ -2165,6 +2123,47 @@ struct ScratchLease {
     }
 };
 }  // namespace
+
+nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
+                         int chunked, void *stream) {
+    return guard([&] {
+        if (batch * t * d == 0) return;
+        if (!a || !b || !h) fail(NK_ERR_INVALID, "null argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        if (!chunked) {
+            cuda_check(nk::scan_sequential(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan");
+            return;
+        }
+        ScratchLease lease(nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d) * sizeof(float),
+                           "scan scratch");
+        cudaError_t e = nk::scan_chunked(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, (float *)lease.ptr, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cuda_check(e, "scan");
+        cuda_check(e2, "scan sync");
+    });
+}
+
+nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
+                                 int chunked, void *stream) {
+    return guard([&] {
+        if (batch * t * d == 0) return;
+        if (!a || !g || !c) fail(NK_ERR_INVALID, "null argument");
+        cudaStream_t st = (cudaStream_t)stream;
+        if (!chunked) {
+            cuda_check(nk::scan_adjoint_sequential(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan adjoint");
+            return;
+        }
+        ScratchLease lease(nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d) * sizeof(float),
+                           "scan scratch");
+        cudaError_t e = nk::scan_adjoint_chunked(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, (float *)lease.ptr, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cuda_check(e, "scan adjoint");
+        cuda_check(e2, "scan adjoint sync");
+    });
+}
+
+// ---------------------------------------------------------------- training-side ops
+
 
 nk_status nk_gemm_tn_device(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n,
                             void *stream) {

@@ -24,6 +24,7 @@ namespace nk {
 namespace {
 
 constexpr int SCAN_TB = 256;  // time steps per block in the chunked scan
+constexpr int SCAN_PB = 8;    // steps whose operands the chunked passes load ahead of use
 
 inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }
 
@@ -66,12 +67,21 @@ __global__ void scan_local_k(const float *__restrict__ a, const float *__restric
     const int64_t c = bc % nblk, bi = bc / nblk;
     const int64_t t0 = c * SCAN_TB, t1 = min(t, t0 + SCAN_TB);
     float A = 1.0f, carry = 0.0f;
-    for (int64_t ti = t0; ti < t1; ++ti) {
-        const size_t o = ((size_t)bi * t + ti) * d + j;
-        const float av = a[o];
-        carry = av * carry + b[o];
-        h[o] = carry;
-        A = A * av;
+    for (int64_t tb = t0; tb < t1; tb += SCAN_PB) {
+        float av[SCAN_PB], bv[SCAN_PB];
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            const size_t o = ((size_t)bi * t + tb + e) * d + j;
+            av[e] = tb + e < t1 ? a[o] : 1.0f;
+            bv[e] = tb + e < t1 ? b[o] : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            if (tb + e >= t1) break;
+            carry = av[e] * carry + bv[e];
+            h[((size_t)bi * t + tb + e) * d + j] = carry;
+            A = A * av[e];
+        }
     }
     blkA[i] = A;
     blkB[i] = carry;
@@ -102,11 +112,26 @@ __global__ void scan_fix_k(const float *__restrict__ a, float *__restrict__ h,
     if (cin == 0.0f) return;
     const int64_t t0 = c * SCAN_TB, t1 = min(t, t0 + SCAN_TB);
     float P = 1.0f;
-    for (int64_t ti = t0; ti < t1; ++ti) {
-        const size_t o = ((size_t)bi * t + ti) * d + j;
-        P = P * a[o];
-        if (P == 0.0f) break;
-        h[o] = h[o] + P * cin;
+    for (int64_t tb = t0; tb < t1; tb += SCAN_PB) {
+        float av[SCAN_PB], hv[SCAN_PB];
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            const size_t o = ((size_t)bi * t + tb + e) * d + j;
+            av[e] = tb + e < t1 ? a[o] : 1.0f;
+            hv[e] = tb + e < t1 ? h[o] : 0.0f;
+        }
+        bool done = false;
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            if (tb + e >= t1) break;
+            P = P * av[e];
+            if (P == 0.0f) {
+                done = true;
+                break;
+            }
+            h[((size_t)bi * t + tb + e) * d + j] = hv[e] + P * cin;
+        }
+        if (done) break;
     }
 }
 
@@ -159,13 +184,22 @@ __global__ void adj_local_k(const float *__restrict__ a, const float *__restrict
     const int64_t k = bc % nblk, bi = bc / nblk;
     const int64_t t0 = k * SCAN_TB, t1 = min(t, t0 + SCAN_TB);
     float A = 1.0f, carry = 0.0f;
-    for (int64_t ti = t1 - 1; ti >= t0; --ti) {
-        const size_t o = ((size_t)bi * t + ti) * d + j;
-        const float av = a[o];
-        const float cv = g[o] + carry;
-        c[o] = cv;
-        carry = av * cv;
-        A = A * av;
+    for (int64_t tb = t1 - 1; tb >= t0; tb -= SCAN_PB) {  // steps tb, tb - 1, ... walking down
+        float av[SCAN_PB], gv[SCAN_PB];
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            const size_t o = ((size_t)bi * t + tb - e) * d + j;
+            av[e] = tb - e >= t0 ? a[o] : 1.0f;
+            gv[e] = tb - e >= t0 ? g[o] : 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            if (tb - e < t0) break;
+            const float cv = gv[e] + carry;
+            c[((size_t)bi * t + tb - e) * d + j] = cv;
+            carry = av[e] * cv;
+            A = A * av[e];
+        }
     }
     blkA[i] = A;
     blkB[i] = carry;
@@ -199,11 +233,26 @@ __global__ void adj_fix_k(const float *__restrict__ a, float *__restrict__ c, co
     if (cin == 0.0f) return;
     const int64_t t0 = k * SCAN_TB, t1 = min(t, t0 + SCAN_TB);
     float P = 1.0f;
-    for (int64_t ti = t1 - 1; ti >= t0; --ti) {
-        const size_t o = ((size_t)bi * t + ti) * d + j;
-        c[o] = c[o] + P * cin;
-        P = P * a[o];
-        if (P == 0.0f) break;
+    for (int64_t tb = t1 - 1; tb >= t0; tb -= SCAN_PB) {
+        float av[SCAN_PB], cv[SCAN_PB];
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            const size_t o = ((size_t)bi * t + tb - e) * d + j;
+            av[e] = tb - e >= t0 ? a[o] : 1.0f;
+            cv[e] = tb - e >= t0 ? c[o] : 0.0f;
+        }
+        bool done = false;
+#pragma unroll
+        for (int e = 0; e < SCAN_PB; ++e) {
+            if (tb - e < t0) break;
+            c[((size_t)bi * t + tb - e) * d + j] = cv[e] + P * cin;
+            P = P * av[e];
+            if (P == 0.0f) {
+                done = true;
+                break;
+            }
+        }
+        if (done) break;
     }
 }
 
