@@ -7,13 +7,13 @@
 //
 //   producer warp   streams the weight rows this CTA owns, for every layer
 //                   and phase, into a ring of shared-memory stages with
-//                   cp.async.bulk (mbarrier completion).  Weights do not
-//                   depend on activations, so the stream runs ahead across
-//                   phases and layers, limited only by free stages, and HBM
-//                   stays busy while the consumers wait at grid barriers.
-//   16 consumer     per phase: fetch the residual stream x from L2, take
+//                   cp.async.bulk (mbarrier completion, a few copies in
+//                   flight).  Weights do not depend on activations, so the
+//                   stream runs ahead across phases and layers, limited only
+//                   by free stages, while the consumers wait at grid barriers.
+//   15 consumer     per phase: fetch the residual stream x from L2, take
 //   warps           the streamed rows, apply the epilogue, publish, meet at
-//                   a grid barrier.
+//                   a grid barrier.  (16 warps in all: 128 registers each.)
 //
 // Every streamed row is d floats long.  A layer is two phases, each ending
 // in one grid barrier (release-add, bounded acquire spin):
