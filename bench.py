@@ -71,18 +71,30 @@ class ClockSampler:
         self.uuid = uuid
         self.proc = None
         self.lines = []
+        self.first = 0
         self.thread = None
 
     def start(self):
+        """Starts nvidia-smi at a 50 ms period on this GPU alone and waits (up
+        to 10 s) for its first sample, so that a short timed region is still
+        sampled; mark() then opens the region."""
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader", "-lms", "50"]
+        if self.uuid:
+            cmd += ["-i", self.uuid]
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
-                                         text=True)
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        deadline = time.monotonic() + 10.0
+        while not self.lines and self.proc.poll() is None and time.monotonic() < deadline:
+            time.sleep(0.01)
+
+    def mark(self):
+        """The timed region starts here: earlier samples are not counted."""
+        self.first = len(self.lines)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -100,7 +112,7 @@ class ClockSampler:
             self.thread.join(timeout=5)
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        for line in self.lines[self.first:]:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9 or (self.uuid and parts[0] != self.uuid):
                 continue
@@ -548,9 +560,9 @@ def run_ours(args, rank, world, local_rank):
         pass
     sampler = ClockSampler(uuid)
     sampler.start()
-    time.sleep(0.3)
     barrier()
     torch.cuda.synchronize()
+    sampler.mark()
     launches0 = dec.launch_count()
     torch.cuda.nvtx.range_push("decode_steps")
     e0.record(stream)
