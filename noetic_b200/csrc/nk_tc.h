@@ -93,9 +93,6 @@ cudaError_t tc_split_transposed(const float *src, int rows, int cols, int ld_out
 bool tc_operand_from(const float *hi, const float *lo, int N, int K, TcOperand &op);
 void tc_weights_free(TcWeights &w);
 
-// hi = tf32(A), lo = tf32(A - hi) for an f32 operand [rows, cols] (row stride lda).
-cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st);
-
 // epilogue(A . W^T) with A given as its hi/lo operand pair [M, K] (dense).
 // A kernel whose bounded waits expire writes a nonzero code to *err.
 cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,

@@ -5,7 +5,9 @@
 // error-corrected TF32 product of Ootomo & Yokota 2022, "3xTF32" in
 // CUTLASS); A.W^T = A_hi.W_hi^T + A_hi.W_lo^T + A_lo.W_hi^T, dropping the
 // A_lo.W_lo^T term (~2^-22 relative).  Weights are split once at load; the
-// activation operand is split by a small pre-pass per projection.
+// activation operand pair is written by the kernel that produces the
+// activation (RMSNorm, the SSM update, the SwiGLU epilogue, the prefill
+// passes), and gemm_tn splits both operands with one transposing pass.
 //
 // Kernel structure: persistent, at most one CTA per SM slot (BN = 256: one
 // per SM; BN = 128: two), each walking 128 x BN output tiles in steps of the
@@ -1159,10 +1161,6 @@ int tc_tiles_n(int N, int bn) {
     return (N + w - 1) / w;
 }
 int tc_argmax_parts(int N, int bn) { return 2 * tc_tiles_n(N, bn); }
-
-cudaError_t tc_split(const float *A, int lda, float *hi, float *lo, int rows, int cols, cudaStream_t st) {
-    return split(A, lda, hi, lo, rows, cols, st);
-}
 
 cudaError_t tc_split_transposed(const float *src, int rows, int cols, int ld_out, float *hi, float *lo,
                                 int *nonfinite, cudaStream_t st) {
