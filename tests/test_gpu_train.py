@@ -148,7 +148,7 @@ def test_gemm_tn_tensor_core_path_with_non_finite_operands(gpu, orc):
     assert np.array_equal(np.isnan(got), np.isnan(ref)) and np.array_equal(np.isinf(got), np.isinf(ref))
     fin = np.isfinite(ref)
     bound = 1e-5 * (np.abs(a).T.astype(np.float64) @ np.where(np.isfinite(b), np.abs(b), 0).astype(np.float64))
-    assert (np.abs(got - ref)[fin] <= bound[fin] + 1e-6).all()
+    assert (np.abs(got[fin] - ref[fin]) <= bound[fin] + 1e-6).all()
     # All finite at the same shape: the tensor-core result within the sum bound.
     b[5, 7], b[9, 11] = 1.0, -1.0
     got = gpu.gemm_tn(a, b, p, m, n)
