@@ -325,7 +325,10 @@ def run_scan(args):
     reps = max(3, args.steps)
     out = {"metric": "stand-alone scans (scan.rs), GB/s of algorithmic bytes", "peak_gbs": peaks["hbm_gbs"],
            "peak_basis": basis}
-    for name, (B, T, D) in [("long_prompt", (64, 32768, 768)), ("many_streams", (4096, 512, 512))]:
+    shapes = [("long_prompt", (64, 32768, 768)), ("many_streams", (4096, 512, 512))]
+    if args.scan_shape:
+        shapes = [("custom", tuple(int(v) for v in args.scan_shape.split(",")))]
+    for name, (B, T, D) in shapes:
         n = B * T * D
         a = torch.rand(n, device="cuda")
         b = torch.randn(n, device="cuda")
@@ -734,6 +737,7 @@ def main():
     ap.add_argument("--ckpt-load", action="store_true",
                     help="time the checkpoint -> device load of the headline model instead")
     ap.add_argument("--scan", action="store_true", help="time the stand-alone scans instead")
+    ap.add_argument("--scan-shape", default=None, help="B,T,D: one scan shape instead of the two defaults")
     ap.add_argument("--long-prefill", action="store_true",
                     help="time the long-prompt prefill workload (d768 L12, 64 x 32768 tokens) instead")
     args = ap.parse_args()
