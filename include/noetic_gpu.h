@@ -205,8 +205,10 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * cooperative kernel, for <= 8 streams the fused small-batch step).  Bit 0: f32
  * CUDA-core projections only.  Bit 1 / bit 2: force the time-chunked /
  * sequential prefill scan.  Bit 3: no fused small-batch step.  Bits 4 / 5:
- * tensor-core tiles 128 / 256 columns wide (default: 256 while the grid
- * covers every SM twice, else 128).  Bit 6: the persistent step kernel for
+ * tensor-core tiles 128 / 256 columns wide (default: 128 when N < 256 or
+ * the streams fit one row of tiles (<= 128), else 256 with stream-K for the
+ * store and SwiGLU epilogues; for the argmax epilogue the width with the
+ * higher modelled SM occupancy).  Bit 6: the persistent step kernel for
  * 1-4 streams (the default; kept for compatibility).  Bit 7: the CTA-pair projection kernel (256 x 256 tiles on two
  * SMs) wherever N >= 256.  Bit 8: whole tiles per CTA instead of stream-K
  * (equal K-block ranges per SM, partial tiles summed in a fixed order).
