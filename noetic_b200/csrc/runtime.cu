@@ -1004,7 +1004,7 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
     // Rows per chunk: bounded scratch (about 3 GiB at most).
     const size_t row_bytes = 4 * (2 * (size_t)d + std::max(3 * (size_t)E, 2 * (size_t)H) + std::max((size_t)E, (size_t)H) +
                                   2 * std::max({(size_t)d, (size_t)E, (size_t)H}));
-    size_t rows_budget = std::max<size_t>((size_t)3 << 30, 0) / row_bytes;
+    size_t rows_budget = ((size_t)3 << 30) / row_bytes;
     rows_budget = std::min<size_t>(std::max<size_t>(rows_budget, (size_t)S), (size_t)1 << 20);
     int tc = (int)std::max<size_t>(1, std::min<size_t>(max_t, rows_budget / (size_t)S));
     const size_t rows = (size_t)S * tc;
