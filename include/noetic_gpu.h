@@ -239,7 +239,8 @@ nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out);
  * recurrence: c_t = g_t + a_{t+1} c_{t+1} with c_T = 0, over [batch, t, d]
  * host arrays (layout (b*t + i)*d + j); chunked = 1 uses the three-pass
  * time-parallel form (equal to the sequential one within f32 rounding).
- * The _device form takes device pointers and a CUDA stream. */
+ * The _device form takes device pointers and a CUDA stream.
+ * batch * t * d <= 2^37, else NK_ERR_INVALID. */
 nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
                           int chunked, int device);
 nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
@@ -279,7 +280,8 @@ nk_status nk_bpe_decode_bytes(const nk_bpe *bpe, const uint32_t *ids, uint64_t n
 /* gemm_tn (tensor.rs:156-198): C[m, n] = A[p, m]^T B[p, n], the weight-
  * gradient product; a zero element of A skips its product as kern_tn does.
  * Host arrays, run on `device`; the _device form takes device pointers and a
- * CUDA stream.  m < 2^22, n < 2^31. */
+ * CUDA stream.  m < 2^22, n < 2^31, and p*m, p*n, m*n <= 2^37, else
+ * NK_ERR_INVALID. */
 nk_status nk_gemm_tn(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n, int device);
 nk_status nk_gemm_tn_device(const float *a, const float *b, float *c, uint64_t p, uint64_t m, uint64_t n,
                             void *stream);
@@ -289,8 +291,9 @@ nk_status nk_gemm_tn_device(const float *a, const float *b, float *c, uint64_t p
  * [batch*t*d], gw [k*d] and gb [d] (each nullable, as Graph::backward
  * accumulates).  gx follows the reference's order bit for bit; gw and gb are
  * sums over batch*t rows in a fixed blocked order (deterministic, equal to
- * the sequential sums within f32 rounding).  k <= 16.  Host arrays on
- * `device`; the _device form takes device pointers and a CUDA stream. */
+ * the sequential sums within f32 rounding).  k <= 16, d < 2^21,
+ * batch * t * d <= 2^37.  Host arrays on `device`; the _device form takes
+ * device pointers and a CUDA stream. */
 nk_status nk_dwconv_backward(const float *x, const float *w, const float *go, float *gx, float *gw, float *gb,
                              uint64_t batch, uint64_t t, uint64_t d, uint64_t k, int device);
 nk_status nk_dwconv_backward_device(const float *x, const float *w, const float *go, float *gx, float *gw,
@@ -303,7 +306,7 @@ nk_status nk_dwconv_backward_device(const float *x, const float *w, const float 
  * parameter returns NK_ERR_INVALID (the reference asserts), with that
  * element untouched and the others updated.  Host arrays on `device`; the
  * _device form takes device pointers and a CUDA stream (synchronous: it
- * reads the error flag). */
+ * reads the error flag).  n <= 2^37. */
 typedef struct nk_adamw_cfg {
     float lr, b1, b2, eps, wd; /* AdamW::new defaults: b1 0.9, b2 0.95, eps 1e-8 */
     uint64_t t;
@@ -317,7 +320,8 @@ nk_status nk_adamw_step_device(float *val, const float *grad, float *m, float *v
 /* scan_sequential / scan_chunked (scan.rs:35-57, 98-225):
  * h[b,t,j] = a[b,t,j] * h[b,t-1,j] + b[b,t,j], h[b,-1,j] = 0, layout
  * (b*T + t)*D + j.  Host pointers; runs on `device`.  chunked != 0 selects
- * the time-chunked associative scan. */
+ * the time-chunked associative scan.  batch * t * d <= 2^37 (checked
+ * without wrap-around), else NK_ERR_INVALID. */
 nk_status nk_scan(const float *a, const float *b, float *h, uint64_t batch, uint64_t t,
                   uint64_t d, int chunked, int device);
 

@@ -192,6 +192,23 @@ cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch
                          int64_t d, float *scratch, cudaStream_t st);
 size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d);
 
+// Largest array the stand-alone ops take: 2^37 floats (512 GB, more than a
+// device holds), so element counts, byte counts and every grid derived from
+// them stay far from overflow (scan grids within 2^30 blocks).
+constexpr uint64_t MAX_ELEMENTS = 1ull << 37;
+// out = a * b; false when the product exceeds MAX_ELEMENTS (no wrap-around).
+inline bool checked_mul(uint64_t a, uint64_t b, uint64_t &out) {
+    out = 0;
+    if (a != 0 && b > MAX_ELEMENTS / a) return false;
+    out = a * b;
+    return true;
+}
+// n = batch * t * d within MAX_ELEMENTS; any zero size gives n = 0 (an empty scan).
+inline bool scan_elements(uint64_t batch, uint64_t t, uint64_t d, uint64_t &n) {
+    uint64_t bt = 0;
+    return checked_mul(batch, t, bt) && checked_mul(bt, d, n);
+}
+
 // ---- training-side ops (train.cu)
 // gemm_tn (tensor.rs:156-198): C[m, n] = A[p, m]^T B[p, n].
 cudaError_t gemm_tn(const float *a, const float *b, float *c, int64_t p, int m, int n, cudaStream_t st);

@@ -2127,7 +2127,9 @@ struct ScratchLease {
 nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
                          int chunked, void *stream) {
     return guard([&] {
-        if (batch * t * d == 0) return;
+        uint64_t n = 0;
+        if (!nk::scan_elements(batch, t, d, n)) fail(NK_ERR_INVALID, "scan shape too large: batch * t * d is limited to 2^37 elements");
+        if (n == 0) return;
         if (!a || !b || !h) fail(NK_ERR_INVALID, "null argument");
         cudaStream_t st = (cudaStream_t)stream;
         if (!chunked) {
@@ -2146,7 +2148,9 @@ nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batc
 nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
                                  int chunked, void *stream) {
     return guard([&] {
-        if (batch * t * d == 0) return;
+        uint64_t n = 0;
+        if (!nk::scan_elements(batch, t, d, n)) fail(NK_ERR_INVALID, "scan shape too large: batch * t * d is limited to 2^37 elements");
+        if (n == 0) return;
         if (!a || !g || !c) fail(NK_ERR_INVALID, "null argument");
         cudaStream_t st = (cudaStream_t)stream;
         if (!chunked) {
@@ -2170,7 +2174,10 @@ nk_status nk_gemm_tn_device(const float *a, const float *b, float *c, uint64_t p
     return guard([&] {
         if (m == 0 || n == 0) return;
         if (!c || (p && (!a || !b))) fail(NK_ERR_INVALID, "null argument");
-        if (m >= (1ull << 22) || n >= (1ull << 31) || p >= (1ull << 62)) fail(NK_ERR_INVALID, "gemm_tn shape too large");
+        uint64_t pm = 0, pn = 0, mn = 0;
+        if (m >= (1ull << 22) || n >= (1ull << 31) || !nk::checked_mul(p, m, pm) || !nk::checked_mul(p, n, pn) ||
+            !nk::checked_mul(m, n, mn))
+            fail(NK_ERR_INVALID, "gemm_tn shape too large: m < 2^22, n < 2^31, p*m, p*n, m*n <= 2^37");
         cudaStream_t st = (cudaStream_t)stream;
         if (!nk::gemm_tn_tc_eligible((int64_t)p, (int)m, (int)n)) {
             cuda_check(nk::gemm_tn(a, b, c, (int64_t)p, (int)m, (int)n, st), "gemm_tn");
@@ -2195,7 +2202,10 @@ nk_status nk_gemm_tn(const float *a, const float *b, float *c, uint64_t p, uint6
     return guard([&] {
         if (m == 0 || n == 0) return;
         if (!c || (p && (!a || !b))) fail(NK_ERR_INVALID, "null argument");
-        if (m >= (1ull << 22) || n >= (1ull << 31) || p >= (1ull << 62)) fail(NK_ERR_INVALID, "gemm_tn shape too large");
+        uint64_t pm = 0, pn = 0, mn = 0;
+        if (m >= (1ull << 22) || n >= (1ull << 31) || !nk::checked_mul(p, m, pm) || !nk::checked_mul(p, n, pn) ||
+            !nk::checked_mul(m, n, mn))
+            fail(NK_ERR_INVALID, "gemm_tn shape too large: m < 2^22, n < 2^31, p*m, p*n, m*n <= 2^37");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
         float *da = nullptr, *db = nullptr, *dc = nullptr;
         dalloc(&da, p * m, "gemm_tn a");
@@ -2220,7 +2230,9 @@ nk_status nk_dwconv_backward_device(const float *x, const float *w, const float 
         if (d == 0 || k == 0) fail(NK_ERR_INVALID, "dwconv: width and kernel width must be positive");
         if (k > (uint64_t)nk::dwconv_max_k()) fail(NK_ERR_INVALID, "dwconv backward: kernel width above 16");
         if (d >= (1ull << 21)) fail(NK_ERR_INVALID, "dwconv backward: width too large");
-        const uint64_t rows = batch * t;
+        uint64_t rows = 0, elems = 0;
+        if (!nk::checked_mul(batch, t, rows) || !nk::checked_mul(rows, d, elems))
+            fail(NK_ERR_INVALID, "dwconv backward: batch * t * d is limited to 2^37 elements");
         if (rows == 0 || (!gx && !gw && !gb)) return;
         if (!go || (gx && !w) || (gw && !x)) fail(NK_ERR_INVALID, "null argument");
         cudaStream_t st = (cudaStream_t)stream;
@@ -2242,7 +2254,9 @@ nk_status nk_dwconv_backward(const float *x, const float *w, const float *go, fl
         if (d == 0 || k == 0) fail(NK_ERR_INVALID, "dwconv: width and kernel width must be positive");
         if (k > (uint64_t)nk::dwconv_max_k()) fail(NK_ERR_INVALID, "dwconv backward: kernel width above 16");
         if (d >= (1ull << 21)) fail(NK_ERR_INVALID, "dwconv backward: width too large");
-        const uint64_t n = batch * t * d;
+        uint64_t n = 0;
+        if (!nk::scan_elements(batch, t, d, n))
+            fail(NK_ERR_INVALID, "dwconv backward: batch * t * d is limited to 2^37 elements");
         if (n == 0 || (!gx && !gw && !gb)) return;
         if (!go || (gx && !w) || (gw && !x)) fail(NK_ERR_INVALID, "null argument");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
@@ -2288,6 +2302,7 @@ nk_status nk_adamw_step_device(float *val, const float *grad, float *m, float *v
                                const nk_adamw_cfg *cfg, void *stream) {
     return guard([&] {
         const nk::AdamwParams a = adamw_params(cfg);
+        if (n > nk::MAX_ELEMENTS) fail(NK_ERR_INVALID, "AdamW: n is limited to 2^37 parameters per call");
         if (n == 0) return;
         if (!val || !grad || !m || !v) fail(NK_ERR_INVALID, "null argument");
         cudaStream_t st = (cudaStream_t)stream;
@@ -2306,6 +2321,7 @@ nk_status nk_adamw_step(float *val, const float *grad, float *m, float *v, uint6
                         int device) {
     return guard([&] {
         adamw_params(cfg);
+        if (n > nk::MAX_ELEMENTS) fail(NK_ERR_INVALID, "AdamW: n is limited to 2^37 parameters per call");
         if (n == 0) return;
         if (!val || !grad || !m || !v) fail(NK_ERR_INVALID, "null argument");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
@@ -2336,7 +2352,8 @@ nk_status nk_adamw_step(float *val, const float *grad, float *m, float *v, uint6
 nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
                           int chunked, int device) {
     return guard([&] {
-        const size_t n = batch * t * d;
+        uint64_t n = 0;
+        if (!nk::scan_elements(batch, t, d, n)) fail(NK_ERR_INVALID, "scan shape too large: batch * t * d is limited to 2^37 elements");
         if (n == 0) return;
         if (!a || !g || !c) fail(NK_ERR_INVALID, "null argument");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
@@ -2358,7 +2375,8 @@ nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t bat
 nk_status nk_scan(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
                   int chunked, int device) {
     return guard([&] {
-        const size_t n = batch * t * d;
+        uint64_t n = 0;
+        if (!nk::scan_elements(batch, t, d, n)) fail(NK_ERR_INVALID, "scan shape too large: batch * t * d is limited to 2^37 elements");
         if (n == 0) return;
         if (!a || !b || !h) fail(NK_ERR_INVALID, "null argument");
         cuda_check(cudaSetDevice(device), "cudaSetDevice");

@@ -42,7 +42,13 @@ float *g_scratch_ptr[kMaxDevices] = {};
 extern "C" nk_status nk_scan_chunked_noalloc_device(const float *a, const float *b, float *h, uint64_t batch,
                                                     uint64_t t, uint64_t d, void *stream) {
     nk::set_last_error("");
-    const uint64_t n = batch * t * d;
+    uint64_t n = 0;
+    if (!nk::scan_elements(batch, t, d, n)) {
+        nk::set_last_error("nk_scan_chunked_noalloc_device: batch * t * d overflows the scan size limit; the "
+                           "scratch limit is batch * ceil(t / " + std::to_string(NK_SCAN_TIME_BLOCK) + ") * d <= " +
+                           std::to_string(NK_SCAN_NOALLOC_SCRATCH_FLOATS / 3));
+        return NK_ERR_INVALID;
+    }
     if (n == 0) return NK_OK;
     if (!a || !b || !h) {
         nk::set_last_error("nk_scan_chunked_noalloc_device: null argument");

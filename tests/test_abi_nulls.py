@@ -79,3 +79,32 @@ def test_null_handles_and_outputs_are_refused(nb, name):
 @pytest.mark.parametrize("name", DESTROY)
 def test_destroying_null_is_a_no_op(nb, name):
     assert getattr(nb.lib(), name)(None) == 0
+
+
+# Sizes whose products would wrap around 64 bits (or exceed 2^37 elements per
+# array, more than a device holds) are refused before any device work, rather
+# than wrapping to an "empty" request or an undersized allocation.
+HUGE = 1 << 33
+
+
+def test_oversized_requests_are_refused(nb):
+    L = nb.lib()
+    buf = (C.c_float * 64)()
+    p = C.cast(buf, C.c_void_p)
+    cfg = nb.NkAdamwCfg(1e-3, 0.9, 0.999, 1e-8, 0.0, 1, 0)
+    calls = {
+        "scan": lambda: L.nk_scan(p, p, p, HUGE, HUGE, HUGE, 1, 0),
+        "scan_device": lambda: L.nk_scan_device(p, p, p, HUGE, HUGE, HUGE, 0, None),
+        "scan_adjoint": lambda: L.nk_scan_adjoint(p, p, p, HUGE, HUGE, HUGE, 1, 0),
+        "scan_adjoint_device": lambda: L.nk_scan_adjoint_device(p, p, p, 1 << 20, 1 << 20, 1 << 20, 1, None),
+        "scan_noalloc": lambda: L.nk_scan_chunked_noalloc_device(p, p, p, HUGE, HUGE, HUGE, None),
+        "gemm_tn": lambda: L.nk_gemm_tn(p, p, p, 1 << 40, 1 << 20, 1 << 20, 0),
+        "gemm_tn_device": lambda: L.nk_gemm_tn_device(p, p, p, 1 << 61, 4, 4, None),
+        "dwconv": lambda: L.nk_dwconv_backward(p, p, p, p, p, p, HUGE, HUGE, 1, 1, 0),
+        "dwconv_device": lambda: L.nk_dwconv_backward_device(p, p, p, p, p, p, 1 << 20, 1 << 20, 1 << 20, 1, None),
+        "adamw": lambda: L.nk_adamw_step(p, p, p, p, 1 << 62, C.byref(cfg), 0),
+        "adamw_device": lambda: L.nk_adamw_step_device(p, p, p, p, (1 << 37) + 1, C.byref(cfg), None),
+    }
+    for name, call in calls.items():
+        assert call() == nb.NK_ERR_INVALID, name
+        assert b"2^37" in nb.lib().nk_last_error() or b"limit" in nb.lib().nk_last_error(), name
