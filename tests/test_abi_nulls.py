@@ -108,3 +108,16 @@ def test_oversized_requests_are_refused(nb):
     for name, call in calls.items():
         assert call() == nb.NK_ERR_INVALID, name
         assert b"2^37" in nb.lib().nk_last_error() or b"limit" in nb.lib().nk_last_error(), name
+
+
+def test_a_missing_library_fails_loudly(nb, monkeypatch, tmp_path):
+    # No CPU fallback: without the built library every product call raises.
+    import numpy as np
+
+    monkeypatch.setattr(nb, "LIB_PATH", str(tmp_path / "libnoetic_gpu.so"))
+    monkeypatch.setattr(nb, "_lib", None)
+    with pytest.raises(nb.NoeticError) as e:
+        nb.lib()
+    assert e.value.status == nb.NK_ERR_UNSUPPORTED
+    with pytest.raises(nb.NoeticError):
+        nb.scan_chunked(np.ones(4, np.float32), np.ones(4, np.float32), 1, 4, 1)
