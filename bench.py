@@ -41,6 +41,10 @@ PROMPT_SEED_BASE = 5000
 WORKLOAD = "d1024 L24 E=d V32768 (seed 2), 16384 streams x 64-token uniform prompts, greedy decode"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
+# Collective timeout: well above the longest wait between collectives (the
+# other ranks wait at the last barrier while rank 0 measures one stream, a few
+# seconds), so that if one rank fails the others stop with an error quickly.
+PG_TIMEOUT_S = 180
 
 
 def _env_int(name, default):
@@ -381,7 +385,7 @@ def run_long_prefill(args, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=PG_TIMEOUT_S),
                                 device_id=torch.device("cuda", local_rank))
 
     def barrier():
@@ -497,7 +501,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=PG_TIMEOUT_S),
                                 device_id=torch.device("cuda", local_rank))
 
     def barrier():
