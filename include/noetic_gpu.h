@@ -344,7 +344,9 @@ nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batc
  * (three scratch floats per stream, time block and channel); larger scans
  * return NK_ERR_INVALID with a message.  It calls no allocator at all.  The
  * first call on each device looks up the array's device address (with that
- * device current), so make that first call before any stream capture.  All
+ * device current), so make that first call before any stream capture.  After
+ * a cudaDeviceReset the array may sit at a new address: the next call sees
+ * the new context and looks it up again, so it too is a first call.  All
  * calls share the array: calls whose GPU work overlaps (other streams or
  * threads without ordering) race and may return wrong results; order them. */
 #define NK_SCAN_TIME_BLOCK 256u

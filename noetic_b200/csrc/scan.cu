@@ -16,6 +16,7 @@
 //   naturally (values below 1e-30 times an O(1) carry cannot move an f32 h
 //   of the same row beyond rounding).
 
+#include "../../include/noetic_gpu.h"
 #include "nk_common.cuh"
 #include "nk_kernels.h"
 
@@ -24,6 +25,8 @@ namespace nk {
 namespace {
 
 constexpr int SCAN_TB = 256;  // time steps per block in the chunked scan
+// The public header states the time block in the no-allocation scan's limit.
+static_assert(SCAN_TB == (int)NK_SCAN_TIME_BLOCK, "NK_SCAN_TIME_BLOCK must equal the chunked scan's time block");
 constexpr int SCAN_PB = 8;    // steps whose operands the chunked passes load ahead of use
 
 inline unsigned blocks_for(int64_t n, int threads) { return (unsigned)((n + threads - 1) / threads); }

@@ -62,3 +62,28 @@ def test_noalloc_scan_refuses_sizes_beyond_its_fixed_scratch(gpu):
     status = L.nk_scan_chunked_noalloc_device(p, p, p, batch, t, d, None)
     assert status == gpu.NK_ERR_INVALID
     assert "exceeds the fixed scratch limit" in L.nk_last_error().decode()
+
+
+def test_noalloc_scan_at_the_exact_scratch_boundary(gpu):
+    """batch * ceil(t / 256) * d == 1048576 fills the fixed scratch exactly
+    (every one of its floats is written and read) and is accepted, equal to
+    the allocating scan; one more stream, or one more time step (a second
+    time block per channel), is refused before anything runs."""
+    import torch
+
+    stream = torch.cuda.current_stream().cuda_stream
+    batch, t, d = 512, 1, 2048
+    rs = np.random.default_rng(7)
+    n = batch * t * d
+    a = rs.uniform(0.01, 0.99, n).astype(np.float32)
+    b = rs.standard_normal(n).astype(np.float32)
+    new, ref = _scan_pair(gpu, torch, a, b, batch, t, d, stream)
+    assert np.isfinite(new).all()
+    assert np.abs(new - ref).max() <= TOL
+    L = gpu.lib()
+    dummy = torch.zeros(4, device="cuda")
+    p = C.c_void_p(dummy.data_ptr())
+    for shape in [(513, 1, 2048), (512, 257, 2048)]:
+        status = L.nk_scan_chunked_noalloc_device(p, p, p, *shape, None)
+        assert status == gpu.NK_ERR_INVALID, shape
+        assert "exceeds the fixed scratch limit" in L.nk_last_error().decode()
