@@ -170,10 +170,15 @@ struct SampleParams {
     uint64_t rep_window;
     uint32_t greedy;
 };
+// Any V.  Configurations that keep more than 4096 candidates (top_k == 0 or
+// top_k > 4096) sort in per-CTA global scratch `ws` (sample_ws_bytes; fewer
+// CTAs run when ws holds fewer slots); others need none (ws may be null).
 cudaError_t sample_rows(float *logits, int S, int V, SampleParams cfg, const uint32_t *history,
                         const uint32_t *history_len, int history_stride, uint64_t *rng,
-                        uint32_t *out, int *err, cudaStream_t st);
-int sample_max_vocab();
+                        uint32_t *out, int *err, void *ws, size_t ws_bytes, cudaStream_t st);
+// Scratch sample_rows wants for S rows (0 when none); with budget > 0 at most
+// that many bytes, but always at least one CTA's slot.
+size_t sample_ws_bytes(int S, int V, SampleParams cfg, size_t budget = 0);
 
 // History ring maintenance for generate (cli.rs:495-503).
 cudaError_t history_push(uint32_t *history, uint32_t *history_len, const uint32_t *tok, int S,

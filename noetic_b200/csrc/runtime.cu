@@ -524,6 +524,9 @@ struct nk_decoder {
     uint64_t *rng = nullptr;
     uint32_t *hist = nullptr, *hist_len = nullptr;
     uint32_t hist_cap = 0;
+    // sampler scratch (lazy sort of large candidate sets), grown on demand
+    void *samp_ws = nullptr;
+    size_t samp_ws_bytes = 0;
     // prefill scratch (grown on demand)
     float *p_x = nullptr, *p_n = nullptr, *p_u = nullptr, *p_y = nullptr, *p_last = nullptr,
           *p_scan = nullptr, *p_logits = nullptr;
@@ -579,7 +582,7 @@ struct nk_decoder {
                         (void *)p_lens})
             if (p) cudaFree(p);
         for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo,
-                        (void *)players_dev, (void *)pws, (void *)ksplit_ws, (void *)ksplit_flags})
+                        (void *)players_dev, (void *)pws, (void *)ksplit_ws, (void *)ksplit_flags, samp_ws})
             if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         for (auto &gph : graphs) cudaGraphExecDestroy(gph.exec);
@@ -1118,9 +1121,15 @@ nk::SampleParams to_params(const nk_sample_cfg &c) {
     return nk::SampleParams{c.temperature, c.top_k, c.top_p, c.rep_penalty, c.rep_window, c.greedy};
 }
 
-void check_sample_cfg(const nk_model *m, const nk_sample_cfg &c) {
-    if (!c.greedy && m->cfg.vocab > (uint64_t)nk::sample_max_vocab())
-        fail(NK_ERR_UNSUPPORTED, "stochastic sampling is limited to vocab <= " + std::to_string(nk::sample_max_vocab()));
+// Device scratch of the sampler for this configuration (none for most).
+constexpr size_t SAMPLE_WS_BUDGET = (size_t)256 << 20;
+void ensure_sample_ws(nk_decoder *dec, const nk::SampleParams &p) {
+    const size_t need = nk::sample_ws_bytes((int)dec->S, (int)dec->model->cfg.vocab, p, SAMPLE_WS_BUDGET);
+    if (need <= dec->samp_ws_bytes) return;
+    cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+    if (dec->samp_ws) cudaFree(dec->samp_ws), dec->samp_ws = nullptr, dec->samp_ws_bytes = 0;
+    cuda_check(cudaMalloc(&dec->samp_ws, need), "cudaMalloc(sampler scratch)");
+    dec->samp_ws_bytes = need;
 }
 
 }  // namespace
@@ -1876,8 +1885,8 @@ nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uin
                             uint32_t *out_tokens) {
     return guard([&] {
         if (!dec || !cfg || !rng_state || !out_tokens) fail(NK_ERR_INVALID, "null argument");
-        check_sample_cfg(dec->model, *cfg);
         ensure_ready(dec);
+        ensure_sample_ws(dec, to_params(*cfg));
         const bool use_hist = history && history_len && history_stride > 0;
         if (use_hist) {
             for (uint32_t s = 0; s < dec->S; ++s)
@@ -1892,7 +1901,8 @@ nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uin
                                    cudaMemcpyHostToDevice, dec->stream), "upload rng");
         launch_ok(dec, nk::sample_rows(dec->logits, (int)dec->S, (int)dec->model->cfg.vocab, to_params(*cfg),
                                        use_hist ? dec->hist : nullptr, use_hist ? dec->hist_len : nullptr,
-                                       (int)history_stride, dec->rng, dec->tok_b, dec->err, dec->stream),
+                                       (int)history_stride, dec->rng, dec->tok_b, dec->err, dec->samp_ws,
+                                       dec->samp_ws_bytes, dec->stream),
                   "sample");
         cuda_check(cudaMemcpyAsync(out_tokens, dec->tok_b, dec->S * sizeof(uint32_t), cudaMemcpyDeviceToHost,
                                    dec->stream), "download tokens");
@@ -1908,7 +1918,6 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
     return guard([&] {
         if (!dec || !lens || !cfg || !rng_state || (n_new && !out_tokens) || (!ids && max_t))
             fail(NK_ERR_INVALID, "null argument");
-        check_sample_cfg(dec->model, *cfg);
         const uint32_t S = dec->S;
         // An empty prompt becomes the newline byte token (cli.rs:474-476).
         const uint32_t mt = std::max<uint32_t>(max_t, 1);
@@ -1949,10 +1958,12 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
         dalloc(&d_out, (size_t)S * std::max<uint32_t>(n_new, 1), "generated tokens");
         std::unique_ptr<uint32_t, void (*)(uint32_t *)> own(d_out, [](uint32_t *p) { cudaFree(p); });
         const nk::SampleParams sp = to_params(*cfg);
+        ensure_sample_ws(dec, sp);
         for (uint32_t gi = 0; gi < n_new; ++gi) {
             launch_ok(dec, nk::sample_rows(dec->logits, (int)S, (int)dec->model->cfg.vocab, sp,
                                            use_hist ? dec->hist : nullptr, use_hist ? dec->hist_len : nullptr,
-                                           (int)W, dec->rng, dec->tok_b, dec->err, dec->stream), "sample");
+                                           (int)W, dec->rng, dec->tok_b, dec->err, dec->samp_ws, dec->samp_ws_bytes,
+                                           dec->stream), "sample");
             cuda_check(cudaMemcpy2DAsync(d_out + gi, (size_t)n_new * sizeof(uint32_t), dec->tok_b, sizeof(uint32_t),
                                          sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, dec->stream), "collect tokens");
             if (W > 0) launch_ok(dec, nk::history_push(dec->hist, dec->hist_len, dec->tok_b, (int)S, (int)W, dec->stream), "history");
@@ -2401,9 +2412,11 @@ nk_status nk_sample_token(float *logits, uint64_t vocab, const nk_sample_cfg *cf
         if (!logits || !cfg || !rng_state || !out_token || (n_history && !history)) fail(NK_ERR_INVALID, "null argument");
         if (vocab == 0) fail(NK_ERR_INVALID, "cannot sample from an empty vocabulary");
         if (vocab > (1u << 30)) fail(NK_ERR_UNSUPPORTED, "vocabulary too large");
-        if (!cfg->greedy && vocab > (uint64_t)nk::sample_max_vocab())
-            fail(NK_ERR_UNSUPPORTED, "stochastic sampling is limited to vocab <= " + std::to_string(nk::sample_max_vocab()));
         cuda_check(cudaSetDevice(device), "cudaSetDevice");
+        const size_t ws_bytes = nk::sample_ws_bytes(1, (int)vocab, to_params(*cfg));
+        void *dws = nullptr;
+        if (ws_bytes) cuda_check(cudaMalloc(&dws, ws_bytes), "cudaMalloc(sampler scratch)");
+        std::unique_ptr<void, void (*)(void *)> o0(dws, [](void *p) { if (p) cudaFree(p); });
         float *dl = nullptr;
         uint64_t *dr = nullptr;
         uint32_t *dh = nullptr, *dhl = nullptr, *dt = nullptr;
@@ -2427,7 +2440,7 @@ nk_status nk_sample_token(float *logits, uint64_t vocab, const nk_sample_cfg *cf
         cuda_check(cudaMemcpy(dhl, &hl, 4, cudaMemcpyHostToDevice), "upload history length");
         cuda_check(cudaMemset(de, 0, 4), "memset");
         cuda_check(nk::sample_rows(dl, 1, (int)vocab, to_params(*cfg), n_history ? dh : nullptr, n_history ? dhl : nullptr,
-                                   (int)std::max<uint64_t>(n_history, 1), dr, dt, de, nullptr),
+                                   (int)std::max<uint64_t>(n_history, 1), dr, dt, de, dws, ws_bytes, nullptr),
                    "sample");
         int e = 0;
         cuda_check(cudaMemcpy(out_token, dt, 4, cudaMemcpyDeviceToHost), "download token");

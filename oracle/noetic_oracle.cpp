@@ -715,14 +715,18 @@ uint32_t sample_impl(float *logits, uint64_t vocab, const orc_sample_cfg *cfg,
     std::sort(idx.begin(), idx.end(), before);
     idx.resize(keep);
     float top_p = std::isfinite(cfg->top_p) ? std::min(std::max(cfg->top_p, 0.0f), 1.0f) : 1.0f;
-    float cumulative = 0.0f;
+    float cumulative = 0.0f, previous = 0.0f;
     uint64_t kept = 0;
     for (uint32_t i : idx) {
+        previous = cumulative;
         cumulative += logits[i];
         ++kept;
         if (cumulative >= top_p) break;
     }
+    // Distance of top_p to the cumulative sums on both sides of the cut: a
+    // slightly different sum moves the cut one entry either way.
     local.cut_margin = std::fabs((double)cumulative - (double)top_p);
+    if (kept >= 2) local.cut_margin = std::min(local.cut_margin, std::fabs((double)previous - (double)top_p));
     uint64_t n_cand = std::max<uint64_t>(kept, 1);
     local.kept = (uint32_t)n_cand;
     double total = 0.0;

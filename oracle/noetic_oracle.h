@@ -60,7 +60,7 @@ typedef struct orc_sample_info {
     double draw;            /* draw = f32_unit * total (before walking) */
     double total;           /* f64 sum of kept probabilities */
     double cdf_margin;      /* distance of draw to the nearest CDF edge, / total */
-    double cut_margin;      /* |cumulative at the cut - top_p| */
+    double cut_margin;      /* min |cumulative - top_p| at the cut and one entry before it */
     double top2_margin;     /* greedy: best - second best logit */
 } orc_sample_info;
 

@@ -1,0 +1,136 @@
+"""Parity at the benchmark workloads' own shapes, through the public calls
+(cli.rs:470-518 generate, infer.rs:106-200 stepping, model.rs:148-165 scan
+prefill), against the oracle:
+
+- d192 L3 V1024 (seed 0), 1 stream, a 32-token prompt (Rng::new(1000)), 256
+  greedy tokens: every step's logits within 1e-3 and every token equal where
+  the oracle's top-2 margin exceeds 1e-3;
+- the same model, 256 streams x 128-token prompts (Rng::new(2000 + s)), 512
+  tokens sampled at temperature 0.8 / top-p 0.95 with sampler Rng::new(3000 +
+  s): 8 streams spread over the batch teacher-forced, all 256 rng states
+  bit-identical at the end;
+- d1024 L24 V32768 (seed 2) at 16384 streams: 64-token scan prefill and two
+  greedy steps through the benchmark's own tiling (whole waves plus stream-K
+  partial tiles, graph replay, argmax epilogue), 8 streams including the last
+  tile checked: logits, tokens and every layer's state."""
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import c1_cfg, same_model, state_rel_err
+
+pytestmark = pytest.mark.gpu
+
+GREEDY = dict(temperature=1.0, top_k=0, top_p=1.0, rep_penalty=1.0, rep_window=0, greedy=True)
+GEN_GREEDY = dict(temperature=0.9, top_k=40, top_p=0.95, rep_penalty=1.1, rep_window=64, greedy=True)
+C2_CFG = dict(temperature=0.8, top_k=0, top_p=0.95, rep_penalty=1.0, rep_window=0, greedy=False)
+
+
+def _prompt(orc, seed, n, vocab):
+    r = orc.Rng(seed)
+    return np.array([r.below(vocab) for _ in range(n)], dtype=np.uint32)
+
+
+@pytest.mark.parametrize("cfgd", [GREEDY, GEN_GREEDY])
+def test_c1_single_stream_greedy_generate(gpu, orc, cfgd):
+    kw = c1_cfg(dict)
+    om, gm = same_model(orc, gpu, kw, seed=0)
+    prompt = _prompt(orc, 1000, 32, 1024)
+    N = 256
+    rng = gpu.rng_state(1)[None, :].copy()
+    out = gpu.Decoder(gm, 1).generate(prompt[None, :], np.array([32], np.uint32), N, gpu.SampleCfg(**cfgd), rng)[0]
+    # Teacher-forced replay on the oracle, with the stepping decoder's logits
+    # compared at every position.
+    od = orc.Decoder(om)
+    gd = gpu.Decoder(gm, 1)
+    ocfg = orc.SampleCfg(**cfgd)
+    W = cfgd["rep_window"]
+    hist = list(prompt[-W:]) if W else []
+    worst = 0.0
+    lg = None
+    for t in prompt:
+        lg = od.step(int(t)).copy()
+        worst = max(worst, float(np.abs(gd.step([int(t)])[0] - lg).max()))
+    checked = 0
+    for i in range(N):
+        tok, info = orc.sample_token(lg.copy(), ocfg, hist, orc.Rng(1), info=True)
+        if info.top2_margin > 1e-3:
+            assert int(out[i]) == tok, i
+            checked += 1
+        if W:
+            hist = (hist + [int(out[i])])[-W:]
+        if i + 1 < N:
+            lg = od.step(int(out[i])).copy()
+            worst = max(worst, float(np.abs(gd.step([int(out[i])])[0] - lg).max()))
+    assert worst <= 1e-3, worst
+    assert checked >= 200
+
+
+def test_c2_sampled_generate_at_full_shape(gpu, orc):
+    kw = c1_cfg(dict)
+    om, gm = same_model(orc, gpu, kw, seed=0)
+    S, T, N = 256, 128, 512
+    from noetic_b200 import prompts
+
+    ids = prompts.uniform_prompts(S, T, 1024, 2000)
+    rng = prompts.rng_states(np.arange(S, dtype=np.uint64) + np.uint64(3000))
+    out = gpu.Decoder(gm, S).generate(ids, np.full(S, T, np.uint32), N, gpu.SampleCfg(**C2_CFG), rng)
+    assert out.shape == (S, N) and out.max() < 1024
+    # Every stream drew exactly one f32_unit per token.
+    expect = prompts.rng_states(np.arange(S, dtype=np.uint64) + np.uint64(3000))
+    for _ in range(N):
+        prompts.next_u64(expect)
+    assert np.array_equal(rng, expect)
+    ocfg = orc.SampleCfg(**C2_CFG)
+    soft = 0
+    for s in [0, 37, 64, 101, 128, 190, 222, 255]:
+        r = orc.Rng(3000 + s)
+        od = orc.Decoder(om)
+        for t in ids[s]:
+            lg = od.step(int(t)).copy()
+        for i in range(N):
+            tok, info = orc.sample_token(lg, ocfg, [], r, info=True)
+            if tok != int(out[s, i]):
+                assert info.cdf_margin < 1e-5 or info.cut_margin < 1e-6, (s, i)
+                soft += 1
+            if i + 1 < N:
+                lg = od.step(int(out[s, i])).copy()
+        assert r.s == [int(v) for v in rng[s]], s
+    assert soft <= 4
+
+
+def test_c4_headline_at_16384_streams(gpu, orc):
+    kw = dict(vocab=32768, d_model=1024, n_layer=24, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=2)
+    om.set_threads(max(1, os.cpu_count() or 1))
+    from noetic_b200 import prompts
+
+    S, T = 16384, 64
+    ids = prompts.uniform_prompts(S, T, 32768, 5000)
+    dec = gpu.Decoder(gm, S)
+    last = dec.prefill(ids)
+    tok0 = np.argmax(last, axis=1).astype(np.uint32)
+    probe = [0, 1, 4097, 8191, 12000, 16256, 16382, 16383]
+    last_probe = last[probe].copy()
+    del last
+    tok1 = dec.step_greedy(tok0).copy()
+    tok2 = dec.step_greedy(tok1).copy()
+    k, E = 4, 1024
+    for j, s in enumerate(probe):
+        st, heads = dec.get_state(s, 1)
+        od = orc.Decoder(om)
+        for t in ids[s]:
+            ref = od.step(int(t)).copy()
+        assert np.abs(last_probe[j] - ref).max() <= 1e-3, s
+        for tok_in, tok_out in ((tok0, tok1), (tok1, tok2)):
+            lg = od.step(int(tok_in[s])).copy()
+            top2 = np.sort(lg)[-2:]
+            if top2[1] - top2[0] > 1e-3:
+                assert int(tok_out[s]) == orc.argmax(lg), s
+        ost, oh = od.get_state()
+        assert int(heads[0]) == oh
+        for layer in range(24):
+            assert state_rel_err(st[0, layer, k * E:], ost[layer, k * E:]) <= 1e-4, (s, layer)
+            assert state_rel_err(st[0, layer, : k * E], ost[layer, : k * E]) <= 1e-4, (s, layer)

@@ -99,3 +99,30 @@ def test_checkpoint_reload_reproduces_logits(gpu, orc, tmp_path):
     d2 = gpu.Decoder(gm2, 1)
     for i, t in enumerate(ids):
         assert np.abs(d2.step([t])[0] - first[i]).max() < 1e-6
+
+
+@pytest.mark.parametrize("cfgd", [
+    dict(temperature=0.9, top_k=40, top_p=0.95, rep_penalty=1.1, rep_window=64, greedy=False),  # SampleCfg::default_cfg
+    dict(temperature=0.8, top_k=0, top_p=0.95, rep_penalty=1.0, rep_window=0, greedy=False),
+])
+def test_generate_samples_at_the_headline_vocabulary(gpu, orc, cfgd):
+    """noetic gen's default (sampled) path at V = 32768, teacher-forced
+    against the oracle with the rng state bit-exact per stream."""
+    kw = dict(vocab=32768, d_model=64, n_layer=2, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=2)
+    S, T, N = 5, 12, 16
+    lens = np.array([12, 3, 0, 12, 7], dtype=np.uint32)
+    ids = np.zeros((S, T), dtype=np.uint32)
+    for s in range(S):
+        r = orc.Rng(5000 + s)
+        ids[s, : lens[s]] = [r.below(32768) for _ in range(lens[s])]
+    rng = np.stack([gpu.rng_state(3000 + s) for s in range(S)])
+    out = gpu.Decoder(gm, S).generate(ids, lens, N, gpu.SampleCfg(**cfgd), rng)
+    assert out.shape == (S, N) and out.max() < 32768
+    total_soft = 0
+    for s in range(S):
+        soft, hard, r = _teacher_forced(orc, om, ids[s, : lens[s]], out[s], cfgd, 3000 + s)
+        assert hard == 0, s
+        total_soft += soft
+        assert [int(v) for v in rng[s]] == r.s, s
+    assert total_soft <= 1

@@ -132,18 +132,6 @@ def test_decoder_sample_batched_rows(gpu, orc):
         assert out[s] == tok or info.cdf_margin < 1e-5 or info.cut_margin < 1e-6
 
 
-def test_sampling_above_the_vocab_limit_is_refused(gpu):
-    V = 20000
-    cfg = gpu.SampleCfg(temperature=0.8, top_k=0, top_p=0.9, rep_penalty=1.0, rep_window=0, greedy=False)
-    with pytest.raises(gpu.NoeticError) as e:
-        gpu.sample_token(np.zeros(V, np.float32), cfg, [], gpu.rng_state(1))
-    assert e.value.status == gpu.NK_ERR_UNSUPPORTED
-    g = gpu.SampleCfg(greedy=True, rep_penalty=1.0)
-    x = np.zeros(V, np.float32)
-    x[12345] = 1.0
-    assert gpu.sample_token(x, g, [], gpu.rng_state(1)) == 12345
-
-
 @pytest.mark.parametrize("chunked", [False, True])
 def test_scan_adjoint_matches_oracle(gpu, orc, chunked):
     # The awkward-shape table of scan.rs:269-288 plus blocks crossing 256.
