@@ -169,6 +169,42 @@ def cpu_decode_rate(steps: int, warmup: int, prompt_tokens: int = 4):
     }
 
 
+def cpu_stream_parallel_rate(tokens_per_stream: int = 2):
+    """Ours, not the reference's design (the reference decodes one stream at a
+    time): one oracle decoder per host core, each stepping its own stream of
+    the headline model single-threaded, all at once; total tokens/s."""
+    import oracle as O
+
+    cores = os.cpu_count() or 1
+    om = O.Model(O.LmConfig(**MODEL), seed=MODEL_SEED)
+    om.set_threads(1)
+    from noetic_b200.prompts import uniform_prompts
+
+    ids = uniform_prompts(cores, 2, MODEL["vocab"], PROMPT_SEED_BASE)
+    decs = [O.Decoder(om) for _ in range(cores)]
+
+    def work(i, n):
+        tok = int(ids[i, 0])
+        for _ in range(n):
+            tok = O.argmax(decs[i].step(tok))
+
+    def run_all(n):
+        ts = [threading.Thread(target=work, args=(i, n)) for i in range(cores)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+
+    run_all(1)  # warm-up: page in the weights on every core
+    t0 = time.perf_counter()
+    run_all(tokens_per_stream)
+    dt = time.perf_counter() - t0
+    return {"value": cores * tokens_per_stream / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": (f"headline model, {cores} streams at once (one per host thread, matvec single-threaded), "
+                       f"1 warm-up + {tokens_per_stream} timed greedy tokens each; ours, not the reference's "
+                       f"design (the reference has no multi-stream decode)")}
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -187,7 +223,7 @@ def run_reference(args, rank):
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded random-init weights, uniform-random prompt ids)",
-        "config": {"workload": WORKLOAD, "streams": STREAMS, "prompt_len": PROMPT_LEN, "model_seed": MODEL_SEED,
+        "config": {"workload": WORKLOAD, "streams": args.streams, "prompt_len": PROMPT_LEN, "model_seed": MODEL_SEED,
                    "parallelism": "host CPU, one stream at a time (the reference has no batched decode)"},
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -489,6 +525,132 @@ def run_long_prefill(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+C1_MODEL = dict(vocab=1024, d_model=192, n_layer=3, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+C3_MODEL = dict(vocab=8192, d_model=512, n_layer=8, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+
+
+def run_configs(args):
+    """The reference's other workloads on one GPU, each through the public
+    calls with CUDA events on the decoder's stream (inputs resident):
+    c1: d192 L3 V1024 (seed 0), 1 stream, 32-token prompt (Rng::new(1000)),
+        256 greedy tokens through generate (cli.rs:470-518);
+    c2_sampled: the same model, 256 streams x 128-token prompts
+        (Rng::new(2000 + s)), 512 tokens sampled at temperature 0.8 / top-p
+        0.95 with sampler Rng::new(3000 + s), through generate; the sampler's
+        share from its own CUDA events;
+    c3: d512 L8 V8192 (seed 1), 4096 streams x 512-token prompts
+        (Rng::new(4000 + s)) by scan prefill, then 256 greedy decode steps;
+    c5_prefill: d768 L12 V16384 (seed 3), 64 streams x 32768-token prompts
+        (Rng::new(6000 + s)) by the chunked scan prefill, then 64 greedy steps.
+    Each generate call includes its host copies (prompts in, tokens out)."""
+    import torch
+
+    import noetic_b200 as nb
+    from noetic_b200.prompts import rng_states, uniform_prompts
+
+    out = {}
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timed_on(stream, fn):
+        torch.cuda.synchronize()
+        e0.record(stream)
+        r = fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1), r
+
+    # ---- c1
+    gm = nb.Model.new(nb.LmConfig(**C1_MODEL), 0, device=0)
+    prompt = uniform_prompts(1, 32, 1024, 1000)
+    greedy = nb.SampleCfg(temperature=1.0, top_k=0, top_p=1.0, rep_penalty=1.0, rep_window=0, greedy=True)
+    dec = nb.Decoder(gm, 1)
+    st = torch.cuda.ExternalStream(dec.cuda_stream())
+    dec.generate(prompt, np.array([32], np.uint32), 256, greedy, np.zeros((1, 4), np.uint64))  # warm-up
+    ms, toks = timed_on(st, lambda: dec.generate(prompt, np.array([32], np.uint32), 256, greedy,
+                                                 np.zeros((1, 4), np.uint64)))
+    out["c1"] = {"workload": "d192 L3 V1024 (seed 0), 1 stream, 32-token prompt, 256 greedy tokens (generate)",
+                 "tokens_per_s": 256 / (ms / 1000.0), "us_per_token": ms * 1000.0 / 256, "ms": ms,
+                 "includes": "prompt prefill and host copies of the generate call"}
+    dec.close()
+    # ---- c2 (same model)
+    S2, T2, N2 = 256, 128, 512
+    ids = uniform_prompts(S2, T2, 1024, 2000)
+    cfg2 = nb.SampleCfg(temperature=0.8, top_k=0, top_p=0.95, rep_penalty=1.0, rep_window=0, greedy=False)
+    dec = nb.Decoder(gm, S2)
+    st = torch.cuda.ExternalStream(dec.cuda_stream())
+    seeds = np.arange(S2, dtype=np.uint64) + np.uint64(3000)
+    dec.generate(ids, np.full(S2, T2, np.uint32), 8, cfg2, rng_states(seeds))  # warm-up, sizes buffers
+    ms, _ = timed_on(st, lambda: dec.generate(ids, np.full(S2, T2, np.uint32), N2, cfg2, rng_states(seeds)))
+    dec.profile_begin()
+    dec.generate(ids, np.full(S2, T2, np.uint32), N2, cfg2, rng_states(seeds))
+    prof = dec.profile_end()
+    out["c2_sampled"] = {
+        "workload": "d192 L3 V1024 (seed 0), 256 streams x 128-token prompts, 512 tokens sampled (T 0.8, top-p 0.95)",
+        "tokens_per_s": S2 * N2 / (ms / 1000.0), "ms": ms,
+        "sampler_ms": prof["sample_ms"], "sampler_launches": prof["sample_launches"],
+        "sampler_share": prof["sample_ms"] / ms if ms > 0 else None,
+        "projection_ms": prof["proj_ms"],
+        "note": "sampler and projection times from the decoder's per-launch CUDA events in a second, profiled "
+                "run (launched eagerly); includes the 128-token prefill"}
+    dec.close()
+    gm.close()
+    # ---- c3
+    gm = nb.Model.new(nb.LmConfig(**C3_MODEL), 1, device=0)
+    S3, T3, N3 = 4096, 512, 256
+    ids = uniform_prompts(S3, T3, 8192, 4000)
+    dec = nb.Decoder(gm, S3)
+    st = torch.cuda.ExternalStream(dec.cuda_stream())
+    dec.prefill(ids, want_logits=False)  # warm-up
+    dec.reset()
+    pms, _ = timed_on(st, lambda: dec.prefill(ids, want_logits=False))
+    tok = torch.from_numpy(dec.sample(greedy, np.zeros((S3, 4), np.uint64)).astype(np.int32)).cuda()
+    nxt = torch.empty_like(tok)
+    for _ in range(3):
+        dec.step_greedy_device(tok.data_ptr(), nxt.data_ptr())
+        tok, nxt = nxt, tok
+
+    def decode3():
+        nonlocal tok, nxt
+        for _ in range(N3):
+            dec.step_greedy_device(tok.data_ptr(), nxt.data_ptr())
+            tok, nxt = nxt, tok
+
+    dms, _ = timed_on(st, decode3)
+    out["c3"] = {"workload": "d512 L8 V8192 (seed 1), 4096 streams x 512-token prompts, 256 greedy tokens",
+                 "prefill_tokens_per_s": S3 * T3 / (pms / 1000.0), "prefill_ms": pms,
+                 "decode_tokens_per_s": S3 * N3 / (dms / 1000.0), "decode_ms": dms,
+                 "note": "3 decode steps untimed after the prefill (graph capture)"}
+    dec.close()
+    gm.close()
+    # ---- c5 prefill
+    gm = nb.Model.new(nb.LmConfig(**LONG_MODEL), LONG_SEED, device=0)
+    ids = uniform_prompts(LONG_STREAMS, LONG_PROMPT, LONG_MODEL["vocab"], 6000)
+    dec = nb.Decoder(gm, LONG_STREAMS)
+    st = torch.cuda.ExternalStream(dec.cuda_stream())
+    dec.prefill(ids[:, :4096], want_logits=False)  # warm-up on a shorter prompt (sizes the chunk buffers)
+    dec.reset()
+    pms, _ = timed_on(st, lambda: dec.prefill(ids, want_logits=False))
+    tok = torch.from_numpy(dec.sample(greedy, np.zeros((LONG_STREAMS, 4), np.uint64)).astype(np.int32)).cuda()
+    nxt = torch.empty_like(tok)
+    for _ in range(3):
+        dec.step_greedy_device(tok.data_ptr(), nxt.data_ptr())
+        tok, nxt = nxt, tok
+
+    def decode5():
+        nonlocal tok, nxt
+        for _ in range(LONG_DECODE):
+            dec.step_greedy_device(tok.data_ptr(), nxt.data_ptr())
+            tok, nxt = nxt, tok
+
+    dms, _ = timed_on(st, decode5)
+    out["c5_prefill"] = {"workload": "d768 L12 V16384 (seed 3), 64 streams x 32768-token prompts, then 64 greedy tokens",
+                         "prefill_tokens_per_s": LONG_STREAMS * LONG_PROMPT / (pms / 1000.0), "prefill_ms": pms,
+                         "decode_tokens_per_s": LONG_STREAMS * LONG_DECODE / (dms / 1000.0), "decode_ms": dms}
+    dec.close()
+    gm.close()
+    return out
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
 
@@ -656,10 +818,15 @@ def run_ours(args, rank, world, local_rank):
                                    "us_per_token": us_m, "launches_per_token": launches_m,
                                    "frac": (weight_bytes + state_bytes) / (us_m * 1e-6) / 1e9 / peaks["hbm_gbs"]}}
 
+    configs = None
+    if rank == 0 and world == 1 and not args.no_configs:
+        configs = run_configs(args)
+
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cb = cpu_decode_rate(steps=8, warmup=1)
         cpu_baseline = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu_baseline["stream_parallel"] = cpu_stream_parallel_rate()
 
     if rank == 0:
         peaks, basis = load_peaks()
@@ -694,7 +861,9 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": WORKLOAD, "streams": n_streams, "streams_per_gpu": count,
                        "prompt_len": PROMPT_LEN, "global_batch": n_streams, "seq_len": PROMPT_LEN,
                        "parallelism": f"dp{world} (streams sharded, weights replicated, no collective)",
-                       "l2": "inputs exceed L2: 1.44 GB of weights and 8.05 GB of state per step",
+                       "l2": (f"inputs exceed L2: {4.0 * 361.15e6 / 1e9:.3f} GB of weights and "
+                              f"{count * MODEL['n_layer'] * (MODEL['conv_k'] + 1) * MODEL['d_model'] * 4 / 1e9:.2f} GB "
+                              f"of state per step and GPU"),
                        "projection_engine": "tcgen05 3xTF32" if tc else "f32 CUDA cores"},
             "prefill": {"value": n_streams * PROMPT_LEN / (prefill_ms / 1000.0), "unit": "tokens/s",
                         "ms": prefill_ms},
@@ -709,6 +878,7 @@ def run_ours(args, rank, world, local_rank):
                          "proj_launches_per_step": prof["proj_launches"] / args.steps},
             "clocks": clocks,
             "batch1": batch1,
+            "configs": configs,
             "cpu_baseline": cpu_baseline,
             "setup": {"init_s": round(init_s, 2)},
         }
@@ -731,6 +901,8 @@ def main():
                     help="fixed streams per GPU (streams x N in total) instead of the fixed 16384")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true", help="skip the one-stream HBM measurement")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the other workloads (c1, c2_sampled, c3, c5_prefill) on one GPU")
     ap.add_argument("--engine", type=int, default=0, help="decoder engine flags (0 = automatic)")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling knob: fewer layers than the headline model (for small ncu captures)")
@@ -752,10 +924,12 @@ def main():
         ap.error("--warmup must be at least 3")
     if args.weak:
         args.streams *= world
+    global WORKLOAD
+    if args.streams != STREAMS:
+        WORKLOAD = f"d1024 L24 E=d V32768 (seed 2), {args.streams} streams x 64-token uniform prompts, greedy decode"
     if args.layers is not None or args.vocab is not None:
         MODEL["n_layer"] = args.layers or MODEL["n_layer"]
         MODEL["vocab"] = args.vocab or MODEL["vocab"]
-        global WORKLOAD
         WORKLOAD = (f"profiling case: d1024 L{MODEL['n_layer']} V{MODEL['vocab']}, {args.streams} streams x "
                     f"64-token prompts, greedy decode (not the headline configuration)")
     if args.train_ops:

@@ -163,7 +163,12 @@ nk_status nk_decoder_prefill(nk_decoder *dec, const uint32_t *ids, const uint32_
  * prefill for every stream.  history is [S, history_stride] with per-stream
  * lengths history_len[S] (each <= history_stride; nullable when
  * rep_window == 0 or rep_penalty <= 1); rng_state[S][4] (host, in/out) is the
- * per-stream xoshiro256++ state (rng.rs:17-22).  out_tokens[S] host. */
+ * per-stream xoshiro256++ state (rng.rs:17-22).  out_tokens[S] host.  Any
+ * vocabulary size; the softmax and nucleus sums are the reference's
+ * sequential f32 sums, bit for bit.  Configurations keeping more than 4096
+ * candidates (top_k == 0 or > 4096) sort in decoder-owned scratch (2 * vocab
+ * * 8 bytes per concurrently sampled stream, at most 256 MiB), allocated on
+ * first use. */
 nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uint32_t *history,
                             const uint32_t *history_len, uint32_t history_stride,
                             uint64_t *rng_state, uint32_t *out_tokens);
@@ -171,7 +176,11 @@ nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uin
 /* cli.rs:generate (cli.rs:470-518) on token ids for every stream: prefill
  * each prompt (an empty prompt becomes [10]), then n_new sampled tokens with
  * a rep_window history, stepping after every token but the last.
- * rng_state[S][4] in/out; out_tokens[S*n_new] host. */
+ * rng_state[S][4] in/out; out_tokens[S*n_new] host.  When the tensor cores
+ * run the logits projection, its epilogue applies the repetition penalty
+ * and temperature and emits per-row maxima for the sampler (sampled
+ * configurations), or the argmax itself (greedy without a penalty), so the
+ * step and the draw share one pass over the logits. */
 nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32_t *lens,
                               uint32_t max_t, uint32_t n_new, const nk_sample_cfg *cfg,
                               uint64_t *rng_state, uint32_t *out_tokens);
@@ -213,15 +222,25 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * SMs) wherever N >= 256.  Bit 8: whole tiles per CTA instead of stream-K
  * (equal K-block ranges per SM, partial tiles summed in a fixed order).
  * Bit 9: no L2 cache policies on projection loads and stores.  Bit 10: no
- * persistent step kernel (1-4 streams take the fused small-batch kernels). */
+ * persistent step kernel (1-4 streams take the fused small-batch kernels).
+ * Bit 11: generate stores the logits and runs the stand-alone sampler
+ * instead of the logits projection's sampling / argmax epilogues.
+ * Bits 12 / 13 are test controls of the failure path: the tensor-core
+ * projections publish no stream-K partial tile (their finishers' bounded
+ * waits run out: error code 121), or the persistent step's first CTA skips
+ * its first grid-barrier arrival (every CTA's bounded wait runs out: code
+ * 113); those waits are bounded at 2 ms instead of 1 s.  The call returns
+ * NK_ERR_DEVICE; the decoder stays usable (restore its state with
+ * nk_decoder_set_state: the failed step's results are not valid). */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */
 nk_status nk_decoder_launch_count(const nk_decoder *dec, uint64_t *count);
 
-/* Device-time profile of the projections (the dominant kernels), measured
- * with CUDA events recorded on the decoder's stream around every projection
- * launch between nk_decoder_profile_begin and nk_decoder_profile_end. */
+/* Device-time profile of the projections (the dominant kernels) and of the
+ * sampler, measured with CUDA events recorded on the decoder's stream around
+ * every projection and sampler launch between nk_decoder_profile_begin and
+ * nk_decoder_profile_end. */
 typedef struct nk_profile {
     double proj_ms;          /* summed device time of projection launches   */
     uint64_t proj_launches;  /* projection launches                          */
@@ -229,6 +248,8 @@ typedef struct nk_profile {
     double proj_bytes;       /* algorithmic bytes: A, W, bias, R read + C    */
     uint64_t launches;       /* every kernel launched while profiling        */
     int tensor_core;         /* 1 if any projection ran on tcgen05           */
+    double sample_ms;        /* summed device time of sampler launches      */
+    uint64_t sample_launches;
 } nk_profile;
 nk_status nk_decoder_profile_begin(nk_decoder *dec);
 nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out);

@@ -63,7 +63,8 @@ class NkAdamwCfg(C.Structure):
 
 class NkProfile(C.Structure):
     _fields_ = [("proj_ms", C.c_double), ("proj_launches", _u64), ("proj_flops", C.c_double),
-                ("proj_bytes", C.c_double), ("launches", _u64), ("tensor_core", _i32)]
+                ("proj_bytes", C.c_double), ("launches", _u64), ("tensor_core", _i32), ("sample_ms", C.c_double),
+                ("sample_launches", _u64)]
 
 
 SIGNATURES = {
@@ -461,7 +462,8 @@ class Decoder:
         p = NkProfile()
         _check(lib().nk_decoder_profile_end(self.h, C.byref(p)))
         return {"proj_ms": p.proj_ms, "proj_launches": p.proj_launches, "proj_flops": p.proj_flops,
-                "proj_bytes": p.proj_bytes, "launches": p.launches, "tensor_core": bool(p.tensor_core)}
+                "proj_bytes": p.proj_bytes, "launches": p.launches, "tensor_core": bool(p.tensor_core),
+                "sample_ms": p.sample_ms, "sample_launches": p.sample_launches}
 
 
 # ---------------------------------------------------------------- ops

@@ -88,6 +88,8 @@ struct PersistParams {
     int nstage;                    // ring stages
     int res_cap, gval_cap;         // floats of per-row results, of local g / s values
     int ob_cap, unit_cap, ops_cap; // operand block: owner bias, per-unit and whole-block floats
+    uint64_t barrier_wait_ns;      // bound of the grid-barrier wait
+    int withhold_arrival;          // test control: CTA 0 skips its first grid-barrier arrival
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -691,14 +693,15 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                 // The CTA barrier above orders the consumers' writes before
                 // this release; the acquire orders the other CTAs' writes
                 // before the CTA barrier below.
-                asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p.sync), "r"(1u) : "memory");
+                if (!(p.withhold_arrival && blockIdx.x == 0 && barrier_target == (uint32_t)G))
+                    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p.sync), "r"(1u) : "memory");
                 if (!*(volatile int *)&s_abort) {
                     const uint64_t t0 = gtimer();
                     for (;;) {
                         uint32_t v;
                         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p.sync) : "memory");
                         if (v >= barrier_target) break;
-                        if (gtimer() - t0 > WAIT_NS) {
+                        if (gtimer() - t0 > p.barrier_wait_ns) {
                             atomicExch(p.err, 113);
                             *(volatile int *)&s_abort = 1;
                             break;
@@ -845,6 +848,8 @@ cudaError_t launch_mr(const PersistStepArgs &a, cudaStream_t st) {
     p.unit_cap = pl.unit_cap;
     p.ops_cap = pl.ops_cap;
     p.nstage = pl.nstage;
+    p.barrier_wait_ns = a.barrier_wait_ns ? a.barrier_wait_ns : WAIT_NS;
+    p.withhold_arrival = a.withhold_arrival ? 1 : 0;
     const size_t smem = pl.smem;
     static size_t smem_set[MAXR + 1] = {};
     cudaError_t e;

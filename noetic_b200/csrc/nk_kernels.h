@@ -153,6 +153,11 @@ struct PersistStepArgs {
                              // error; every completed launch leaves it zero
     const PersistLayer *layers;  // device array [n_layer]
     int M, d, E, H, k, V, n_layer;
+    // Grid-barrier wait bound in ns (0: 1 s).  Test control: with
+    // withhold_arrival CTA 0 skips its first barrier arrival, so every CTA's
+    // wait runs out and the kernel reports code 113 instead of completing.
+    uint64_t barrier_wait_ns = 0;
+    int withhold_arrival = 0;
 };
 bool persistent_step_supported(int M, int d, int E, int H, int k, int V, int n_layer);
 int persistent_partials();
@@ -173,9 +178,23 @@ struct SampleParams {
 // Any V.  Configurations that keep more than 4096 candidates (top_k == 0 or
 // top_k > 4096) sort in per-CTA global scratch `ws` (sample_ws_bytes; fewer
 // CTAs run when ws holds fewer slots); others need none (ws may be null).
+// prep (nullable): the rows already hold pen(logit) / temperature, written by
+// the logits projection's sampling epilogue, whose per-part maxima of the
+// finite values and +inf counts ([S, parts]) replace steps 1 and 3.
+struct SamplePrepared {
+    const float *max;
+    const uint32_t *pinf;
+    int parts;
+};
 cudaError_t sample_rows(float *logits, int S, int V, SampleParams cfg, const uint32_t *history,
                         const uint32_t *history_len, int history_stride, uint64_t *rng,
-                        uint32_t *out, int *err, void *ws, size_t ws_bytes, cudaStream_t st);
+                        uint32_t *out, int *err, void *ws, size_t ws_bytes, cudaStream_t st,
+                        const SamplePrepared *prep = nullptr);
+// bits [S][words] = the distinct tokens < V of each stream's last rep_window
+// history entries (all zero when the penalty is off), for the sampling
+// epilogue of the logits projection.
+cudaError_t sample_pen_bitmap(const uint32_t *history, const uint32_t *history_len, int history_stride,
+                              SampleParams cfg, int S, int V, uint32_t *bits, int words, cudaStream_t st);
 // Scratch sample_rows wants for S rows (0 when none); with budget > 0 at most
 // that many bytes, but always at least one CTA's slot.
 size_t sample_ws_bytes(int S, int V, SampleParams cfg, size_t budget = 0);

@@ -64,6 +64,26 @@ struct TcEpilogue {
     int n_flags = 0;
     // L2 policies: weights evict-last, staged outputs evict-first.
     bool l2hints = true;
+    // Sampling preparation (temperature > 0; store mode without bias or
+    // residual, 128- or 256-wide single-SM tiles): C = pen(acc) / temperature
+    // (infer.rs:239-256), the repetition penalty applied where bit (row, col)
+    // of pen_bits [M][pen_words] is set (nullable: none), and per row and
+    // half tile the maximum of the finite outputs and the count of +inf ones
+    // into prep_max / prep_pinf [M, tc_argmax_parts(N, bn)].
+    float temperature = 0.0f;
+    float rep_penalty = 1.0f;
+    const uint32_t *pen_bits = nullptr;
+    int pen_words = 0;
+    float *prep_max = nullptr;
+    uint32_t *prep_pinf = nullptr;
+    // Stream-K hand-off wait bound in ns (0: 1 s).  Test control: with
+    // withhold_publish no partial tile is published, so the finishers' waits
+    // run out and the kernel reports code 121 instead of completing.
+    uint64_t handoff_wait_ns = 0;
+    bool withhold_publish = false;
+    // Incremented by the number of kernels tc_gemm launched (nullable): one,
+    // or two when a single row of tiles is split along K and reduced.
+    uint64_t *launches = nullptr;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.

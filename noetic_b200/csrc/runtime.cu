@@ -527,6 +527,17 @@ struct nk_decoder {
     // sampler scratch (lazy sort of large candidate sets), grown on demand
     void *samp_ws = nullptr;
     size_t samp_ws_bytes = 0;
+    // Sampling epilogue of the logits projection (generate): when
+    // fuse_sample is set, an eager step's tensor-core logits projection
+    // writes pen(logit) / temperature with per-part maxima and +inf counts,
+    // and records the part count in fused_parts (0: not fused).
+    const nk::SampleParams *fuse_sample = nullptr;
+    bool fuse_penalty = false;
+    int fused_parts = 0;
+    uint32_t *pen_bits = nullptr;
+    float *prep_max = nullptr;
+    uint32_t *prep_pinf = nullptr;
+    size_t prep_cap = 0;
     // prefill scratch (grown on demand)
     float *p_x = nullptr, *p_n = nullptr, *p_u = nullptr, *p_y = nullptr, *p_last = nullptr,
           *p_scan = nullptr, *p_logits = nullptr;
@@ -567,6 +578,10 @@ struct nk_decoder {
     double prof_flops = 0, prof_bytes = 0;
     uint64_t prof_launch0 = 0, prof_proj = 0;
     bool prof_tc = false;
+    // sampler launches while profiling (event pairs), reported beside the projections
+    std::vector<cudaEvent_t> samp_ev;
+    size_t samp_used = 0;
+    uint64_t prof_samp = 0;
 
     uint64_t L() const { return model->cfg.n_layer; }
     size_t layer_state_floats() const { return (size_t)S * (model->k() + 1) * model->e(); }
@@ -582,9 +597,11 @@ struct nk_decoder {
                         (void *)p_lens})
             if (p) cudaFree(p);
         for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo,
-                        (void *)players_dev, (void *)pws, (void *)ksplit_ws, (void *)ksplit_flags, samp_ws})
+                        (void *)players_dev, (void *)pws, (void *)ksplit_ws, (void *)ksplit_flags, samp_ws,
+                        (void *)pen_bits, (void *)prep_max, (void *)prep_pinf})
             if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+        for (cudaEvent_t e : samp_ev) cudaEventDestroy(e);
         for (auto &gph : graphs) cudaGraphExecDestroy(gph.exec);
         if (stream) cudaStreamDestroy(stream);
     }
@@ -644,6 +661,45 @@ struct ProfScope {
     }
 };
 
+// CUDA events around a sampler launch while profiling.
+struct SampScope {
+    nk_decoder *dec;
+    cudaEvent_t e1 = nullptr;
+    explicit SampScope(nk_decoder *d) : dec(d) {
+        if (!dec->profiling) return;
+        auto next = [&]() {
+            if (dec->samp_used == dec->samp_ev.size()) {
+                cudaEvent_t e;
+                cuda_check(cudaEventCreate(&e), "cudaEventCreate");
+                dec->samp_ev.push_back(e);
+            }
+            return dec->samp_ev[dec->samp_used++];
+        };
+        cudaEvent_t e0 = next();
+        e1 = next();
+        cuda_check(cudaEventRecord(e0, dec->stream), "cudaEventRecord");
+        dec->prof_samp += 1;
+    }
+    ~SampScope() {
+        if (e1) cudaEventRecord(e1, dec->stream);
+    }
+};
+
+// Test controls of the bounded waits (engine bits 12 / 13): the projections'
+// stream-K partial tiles are not published, or the persistent step's CTA 0
+// skips its first grid-barrier arrival, and the waits are bounded at 2 ms,
+// so the failure path (an expired wait reported as an error code, then
+// recovery) runs without a fault and without a hang.
+constexpr int ENGINE_WITHHOLD_PUBLISH = 4096;
+constexpr int ENGINE_WITHHOLD_ARRIVAL = 8192;
+constexpr uint64_t TEST_WAIT_NS = 2000000ull;
+void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
+    if (dec->engine & ENGINE_WITHHOLD_PUBLISH) {
+        ep.withhold_publish = true;
+        ep.handoff_wait_ns = TEST_WAIT_NS;
+    }
+}
+
 // Tile shape of a tensor-core projection; engine bits 4 / 5 / 7 force
 // 128 / 256-wide single-SM tiles / the CTA-pair kernel; bit 8 keeps whole
 // tiles (no stream-K).
@@ -670,9 +726,10 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         ep.ws_floats = nk::tc_stream_k_ws_floats();
         ep.flags = dec->ksplit_flags;
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
+        test_controls(dec, ep);
+        ep.launches = &dec->launches;
         cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, N), dec->stream, dec->err),
                    "tcgen05 projection");
-        dec->launches += 1;
         dec->prof_tc = dec->prof_tc || dec->profiling;
     } else {
         nk::GemmArgs p{a.f32, K, W, K, C, N, M, N, K, bias, R, N};
@@ -700,6 +757,7 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
         ep.ws_floats = nk::tc_stream_k_ws_floats();
         ep.flags = dec->ksplit_flags;
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
+        test_controls(dec, ep);
         Act out = gated;
         if (t_dn) {
             out = Act{nullptr, scratch, scratch + (size_t)M * H};
@@ -708,9 +766,9 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
         } else {
             ep.C = gated.f32;
         }
+        ep.launches = &dec->launches;
         cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, 2 * H), dec->stream, dec->err),
                    "tcgen05 projection + SwiGLU");
-        dec->launches += 1;
         dec->prof_tc = dec->prof_tc || dec->profiling;
         return out;
     }
@@ -732,8 +790,8 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
             ep.best_val = dec->best_val;
             ep.best_idx = dec->best_idx;
             ep.l2hints = false;  // the tied embedding (268 MB as hi + lo) does not fit L2
+            ep.launches = &dec->launches;
             cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, bn, dec->stream, dec->err), "tcgen05 projection");
-            dec->launches += 1;
             dec->prof_tc = dec->prof_tc || dec->profiling;
         }
         launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, nk::tc_argmax_parts(N, bn), M, tokens, dec->stream),
@@ -742,6 +800,30 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
         project(dec, false, a, M, K, W, Wtc, N, nullptr, dec->logits, nullptr);
         launch_ok(dec, nk::argmax_rows(dec->logits, tokens, M, N, dec->stream), "argmax");
     }
+}
+
+// Logits projection with the sampling epilogue (pen(logit) / temperature
+// into dec->logits, part maxima and +inf counts); returns the part count.
+int project_sample_prep(nk_decoder *dec, const Act &a, int M, int K, const nk::TcOperand *Wtc, int N) {
+    const nk::SampleParams &sp = *dec->fuse_sample;
+    int bn = pick_bn(dec, M, N, true);
+    if (bn == nk::TC_PAIR) bn = 256;
+    const int parts = nk::tc_argmax_parts(N, bn);
+    ProfScope prof(dec, M, N, K, false, false);
+    nk::TcEpilogue ep;
+    ep.C = dec->logits;
+    ep.ldc = N;
+    ep.l2hints = !(dec->engine & 512);
+    ep.temperature = (std::isfinite(sp.temperature) && sp.temperature > 1e-4f) ? sp.temperature : 1e-4f;
+    ep.rep_penalty = sp.rep_penalty;
+    ep.pen_bits = dec->fuse_penalty ? dec->pen_bits : nullptr;
+    ep.pen_words = (N + 31) / 32;
+    ep.prep_max = dec->prep_max;
+    ep.prep_pinf = dec->prep_pinf;
+    ep.launches = &dec->launches;
+    cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, bn, dec->stream, dec->err), "tcgen05 logits + sampling epilogue");
+    dec->prof_tc = dec->prof_tc || dec->profiling;
+    return parts;
 }
 
 bool use_persistent(const nk_decoder *dec);
@@ -822,6 +904,11 @@ void check_err_flag(nk_decoder *dec) {
         if (dec->pws)
             cuda_check(cudaMemsetAsync(dec->pws, 0, nk::persistent_ws_bytes((int)dec->model->d()), dec->stream),
                        "clear persistent workspace");
+        // A stream-K partial published after its finisher gave up would
+        // leave a counter set for the next launch.
+        if (dec->ksplit_flags)
+            cuda_check(cudaMemsetAsync(dec->ksplit_flags, 0, nk_decoder::KSPLIT_FLAGS * sizeof(int), dec->stream),
+                       "clear stream-K counters");
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
                                 ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 105-108 CTA-pair pipeline wait expired, 111-113 "
@@ -894,6 +981,10 @@ void small_step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits
         pa.k = a.k;
         pa.V = a.V;
         pa.n_layer = a.n_layer;
+        if (dec->engine & ENGINE_WITHHOLD_ARRIVAL) {
+            pa.withhold_arrival = 1;
+            pa.barrier_wait_ns = TEST_WAIT_NS;
+        }
         cuda_check(nk::persistent_step(pa, dec->stream), "persistent decode step");
         dec->launches += 1;
         return;
@@ -948,6 +1039,7 @@ void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint
 // With tokens_out, the step ends in the greedy choice (sample_token with
 // greedy and no penalty); the logits are then stored only if want_logits.
 void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
+    dec->fused_parts = 0;
     if (use_small(dec)) {
         small_step_device(dec, tokens, want_logits || !tokens_out, tokens_out);
         return;
@@ -979,6 +1071,10 @@ void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint3
     const bool t_lg = use_tc(dec, S, V, d, w_lg);
     launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, nrm.out(t_lg), S, d, st), "rmsnorm");
     if (want_logits || !tokens_out) {
+        if (dec->fuse_sample && t_lg && !tokens_out) {
+            dec->fused_parts = project_sample_prep(dec, nrm, S, d, w_lg, V);
+            return;
+        }
         project(dec, t_lg, nrm, S, d, m->dp(m->emb), w_lg, V, nullptr, dec->logits, nullptr);
         if (tokens_out) launch_ok(dec, nk::argmax_rows(dec->logits, tokens_out, S, V, st), "argmax");
     } else {
@@ -1899,6 +1995,7 @@ nk_status nk_decoder_sample(nk_decoder *dec, const nk_sample_cfg *cfg, const uin
         }
         cuda_check(cudaMemcpyAsync(dec->rng, rng_state, (size_t)dec->S * 4 * sizeof(uint64_t),
                                    cudaMemcpyHostToDevice, dec->stream), "upload rng");
+        SampScope prof(dec);
         launch_ok(dec, nk::sample_rows(dec->logits, (int)dec->S, (int)dec->model->cfg.vocab, to_params(*cfg),
                                        use_hist ? dec->hist : nullptr, use_hist ? dec->hist_len : nullptr,
                                        (int)history_stride, dec->rng, dec->tok_b, dec->err, dec->samp_ws,
@@ -1959,15 +2056,68 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
         std::unique_ptr<uint32_t, void (*)(uint32_t *)> own(d_out, [](uint32_t *p) { cudaFree(p); });
         const nk::SampleParams sp = to_params(*cfg);
         ensure_sample_ws(dec, sp);
+        const int V = (int)dec->model->cfg.vocab;
+        // Greedy without a penalty is the argmax of the logits: those steps
+        // end in the projection's argmax epilogue (logits never stored) and
+        // replay from a CUDA graph.  Sampled steps end in the projection's
+        // sampling epilogue (penalty and temperature applied, row maxima and
+        // +inf counts per part) whenever the tensor cores run the logits.
+        // Engine bit 11 keeps the plain step + sampler for comparison.
+        const bool unfused = (dec->engine & 2048) != 0;
+        const bool greedy_fast = cfg->greedy && !use_hist && !unfused;
+        if (!cfg->greedy && !unfused) {
+            const size_t parts = (size_t)nk::tc_argmax_parts(V, 128);  // the most any tile width gives
+            if (dec->prep_cap < (size_t)S * parts) {
+                cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
+                for (void *q : {(void *)dec->prep_max, (void *)dec->prep_pinf})
+                    if (q) cudaFree(q);
+                dec->prep_max = nullptr;
+                dec->prep_pinf = nullptr;
+                dalloc(&dec->prep_max, (size_t)S * parts, "sampling epilogue maxima");
+                dalloc(&dec->prep_pinf, (size_t)S * parts, "sampling epilogue +inf counts");
+                dec->prep_cap = (size_t)S * parts;
+            }
+            if (use_hist && !dec->pen_bits) dalloc(&dec->pen_bits, (size_t)S * ((V + 31) / 32), "penalty bitmap");
+        }
+        int prep_parts = 0;  // parts of the last step's sampling epilogue (0: plain logits)
+        uint32_t *tok = dec->tok_b, *spare = dec->tok_a;
         for (uint32_t gi = 0; gi < n_new; ++gi) {
-            launch_ok(dec, nk::sample_rows(dec->logits, (int)S, (int)dec->model->cfg.vocab, sp,
-                                           use_hist ? dec->hist : nullptr, use_hist ? dec->hist_len : nullptr,
-                                           (int)W, dec->rng, dec->tok_b, dec->err, dec->samp_ws, dec->samp_ws_bytes,
-                                           dec->stream), "sample");
-            cuda_check(cudaMemcpy2DAsync(d_out + gi, (size_t)n_new * sizeof(uint32_t), dec->tok_b, sizeof(uint32_t),
+            if (gi == 0 || !greedy_fast) {
+                SampScope prof(dec);
+                const nk::SamplePrepared prep{dec->prep_max, dec->prep_pinf, prep_parts};
+                launch_ok(dec, nk::sample_rows(dec->logits, (int)S, V, sp, use_hist ? dec->hist : nullptr,
+                                               use_hist ? dec->hist_len : nullptr, (int)W, dec->rng, tok, dec->err,
+                                               dec->samp_ws, dec->samp_ws_bytes, dec->stream,
+                                               prep_parts ? &prep : nullptr),
+                          "sample");
+            }
+            cuda_check(cudaMemcpy2DAsync(d_out + gi, (size_t)n_new * sizeof(uint32_t), tok, sizeof(uint32_t),
                                          sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, dec->stream), "collect tokens");
-            if (W > 0) launch_ok(dec, nk::history_push(dec->hist, dec->hist_len, dec->tok_b, (int)S, (int)W, dec->stream), "history");
-            if (gi + 1 < n_new) step_device(dec, dec->tok_b, true, nullptr);
+            if (W > 0) launch_ok(dec, nk::history_push(dec->hist, dec->hist_len, tok, (int)S, (int)W, dec->stream), "history");
+            if (gi + 1 == n_new) break;
+            if (greedy_fast) {
+                step_device(dec, tok, false, spare);
+                std::swap(tok, spare);
+                continue;
+            }
+            if (!cfg->greedy && !unfused) {
+                dec->fuse_penalty = use_hist;
+                if (use_hist)
+                    launch_ok(dec, nk::sample_pen_bitmap(dec->hist, dec->hist_len, (int)W, sp, (int)S, V, dec->pen_bits,
+                                                         (V + 31) / 32, dec->stream),
+                              "penalty bitmap");
+                dec->fuse_sample = &sp;
+                try {
+                    step_device(dec, tok, true, nullptr);
+                } catch (...) {
+                    dec->fuse_sample = nullptr;
+                    throw;
+                }
+                dec->fuse_sample = nullptr;
+                prep_parts = dec->fused_parts;
+            } else {
+                step_device(dec, tok, true, nullptr);
+            }
         }
         if (n_new)
             cuda_check(cudaMemcpyAsync(out_tokens, d_out, (size_t)S * n_new * sizeof(uint32_t), cudaMemcpyDeviceToHost,
@@ -2036,7 +2186,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 2047) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 16383) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);
@@ -2060,6 +2210,8 @@ nk_status nk_decoder_profile_begin(nk_decoder *dec) {
         dec->prof_proj = 0;
         dec->prof_tc = false;
         dec->prof_launch0 = dec->launches;
+        dec->samp_used = 0;
+        dec->prof_samp = 0;
     });
 }
 
@@ -2074,6 +2226,15 @@ nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out) {
             cuda_check(cudaEventElapsedTime(&t, dec->ev_pool[i], dec->ev_pool[i + 1]), "cudaEventElapsedTime");
             ms += t;
         }
+        double sms = 0;
+        for (size_t i = 0; i + 1 < dec->samp_used; i += 2) {
+            float t = 0;
+            cuda_check(cudaEventElapsedTime(&t, dec->samp_ev[i], dec->samp_ev[i + 1]), "cudaEventElapsedTime");
+            sms += t;
+        }
+        out->sample_ms = sms;
+        out->sample_launches = dec->prof_samp;
+        dec->samp_used = 0;
         out->proj_ms = ms;
         out->proj_launches = dec->prof_proj;
         out->proj_flops = dec->prof_flops;

@@ -418,6 +418,11 @@ struct SampleArgs {
     int *err;
     uint64_t *ws;     // per-CTA scratch for the lazy sort: 2 * ws_keys keys per CTA
     size_t ws_keys;
+    // Rows already penalised and divided by the temperature by the logits
+    // projection's epilogue, with per-part maxima / +inf counts (nullable).
+    const float *prep_max;
+    const uint32_t *prep_pinf;
+    int prep_parts;
 };
 
 // Walk sorted keys get(0..n) through the nucleus sum; returns the number
@@ -489,9 +494,10 @@ __device__ void sample_one(const SampleArgs &a, int s, SampSmem &sm) {
     const SampleParams &cfg = a.cfg;
     float *logits = a.logits + (size_t)s * V;
 
+    const bool prepped = a.prep_max != nullptr && !cfg.greedy;
     // 1. repetition penalty (sequential: the window is short and order
     //    matters only through "first occurrence").
-    if (tid == 0 && isfinite(cfg.rep_penalty) && cfg.rep_penalty > 1.0f && cfg.rep_window > 0 &&
+    if (!prepped && tid == 0 && isfinite(cfg.rep_penalty) && cfg.rep_penalty > 1.0f && cfg.rep_window > 0 &&
         a.history != nullptr) {
         const uint32_t *h = a.history + (size_t)s * a.history_stride;
         const uint64_t n = a.history_len[s];
@@ -536,11 +542,20 @@ __device__ void sample_one(const SampleArgs &a, int s, SampSmem &sm) {
         (isfinite(cfg.temperature) && cfg.temperature > 1e-4f) ? cfg.temperature : 1e-4f;
     int pinf = 0;
     float mx = -INFINITY;
-    for (int i = tid; i < V; i += ST) {
-        const float v = __fdiv_rn(logits[i], temperature);
-        logits[i] = v;
-        if (v == INFINITY) ++pinf;
-        if (isfinite(v) && v > mx) mx = v;
+    if (prepped) {
+        // Steps 1 and 3 ran in the projection epilogue: combine its parts.
+        for (int i = tid; i < a.prep_parts; i += ST) {
+            const size_t slot = (size_t)s * a.prep_parts + i;
+            pinf += (int)a.prep_pinf[slot];
+            mx = fmaxf(mx, a.prep_max[slot]);
+        }
+    } else {
+        for (int i = tid; i < V; i += ST) {
+            const float v = __fdiv_rn(logits[i], temperature);
+            logits[i] = v;
+            if (v == INFINITY) ++pinf;
+            if (isfinite(v) && v > mx) mx = v;
+        }
     }
     // 4. softmax_inplace
     const int n_pinf = block_reduce(pinf, [](int x, int y) { return x + y; }, sm.redi);
@@ -572,23 +587,40 @@ __device__ void sample_one(const SampleArgs &a, int s, SampSmem &sm) {
         if (!isfinite(sum) || sum <= 0.0f) {
             uniform = true;
         } else {
+            // Probabilities, with the level-0 histogram of their exponents.
             const float inv = __fdiv_rn(1.0f, sum);
-            for (int i = tid; i < V; i += ST) logits[i] = __fmul_rn(logits[i], inv);
+            for (int i = tid; i < 256; i += ST) sm.hist[i] = 0;
+            __syncthreads();
+            for (int b = 0; b < V; b += ST) {
+                const int i = b + tid;
+                const bool valid = i < V;
+                uint32_t K = 0;
+                if (valid) {
+                    const float p = __fmul_rn(logits[i], inv);
+                    logits[i] = p;
+                    K = __float_as_uint(p);
+                }
+                hist_add(sm.hist, digit_of(K, 0), valid);
+            }
+            __syncthreads();
         }
     }
     if (uniform) {
         const float p = __fdiv_rn(1.0f, (float)V);
         for (int i = tid; i < V; i += ST) logits[i] = p;
     }
-    // Level-0 histogram of the probabilities' exponents.
-    for (int i = tid; i < 256; i += ST) sm.hist[i] = 0;
-    __syncthreads();
-    for (int b = 0; b < V; b += ST) {
-        const int i = b + tid;
-        const bool valid = i < V;
-        hist_add(sm.hist, valid ? digit_of(__float_as_uint(logits[i]), 0) : 0u, valid);
+    if (n_pinf > 0 || uniform) {
+        // Level-0 histogram of the probabilities' exponents.
+        __syncthreads();
+        for (int i = tid; i < 256; i += ST) sm.hist[i] = 0;
+        __syncthreads();
+        for (int b = 0; b < V; b += ST) {
+            const int i = b + tid;
+            const bool valid = i < V;
+            hist_add(sm.hist, valid ? digit_of(__float_as_uint(logits[i]), 0) : 0u, valid);
+        }
+        __syncthreads();
     }
-    __syncthreads();
 
     const int keep = (cfg.top_k == 0 || cfg.top_k > (uint64_t)V) ? V : (int)cfg.top_k;
     const float top_p = isfinite(cfg.top_p) ? fminf(fmaxf(cfg.top_p, 0.0f), 1.0f) : 1.0f;
@@ -819,6 +851,24 @@ __device__ void sample_one(const SampleArgs &a, int s, SampSmem &sm) {
     __syncthreads();
 }
 
+// Bit (s, t) of bits [S][words] set for every token t < V among the last
+// `window` history entries of stream s (the tokens infer.rs:236-248
+// penalises, each once).
+__global__ void pen_bitmap_k(const uint32_t *__restrict__ history, const uint32_t *__restrict__ history_len,
+                             int stride, uint64_t window, int V, uint32_t *__restrict__ bits, int words) {
+    const int s = blockIdx.x;
+    uint32_t *row = bits + (size_t)s * words;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) row[i] = 0u;
+    __syncthreads();
+    const uint32_t *h = history + (size_t)s * stride;
+    const uint64_t n = history_len[s];
+    const uint64_t start = n > window ? n - window : 0;
+    for (uint64_t i = start + threadIdx.x; i < n; i += blockDim.x) {
+        const uint32_t t = h[i];
+        if (t < (uint32_t)V) atomicOr(&row[t >> 5], 1u << (t & 31u));
+    }
+}
+
 __global__ void __launch_bounds__(ST) sample_rows_k(SampleArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
@@ -855,9 +905,18 @@ size_t sample_ws_bytes(int S, int V, SampleParams cfg, size_t budget) {
     return ctas * per;
 }
 
+cudaError_t sample_pen_bitmap(const uint32_t *history, const uint32_t *history_len, int history_stride,
+                              SampleParams cfg, int S, int V, uint32_t *bits, int words, cudaStream_t st) {
+    if (S <= 0 || words <= 0) return cudaSuccess;
+    const uint64_t window = (history && isfinite(cfg.rep_penalty) && cfg.rep_penalty > 1.0f) ? cfg.rep_window : 0;
+    if (!history || !history_len || window == 0) return cudaMemsetAsync(bits, 0, (size_t)S * words * 4, st);
+    pen_bitmap_k<<<S, 128, 0, st>>>(history, history_len, history_stride, window, V, bits, words);
+    return cudaGetLastError();
+}
+
 cudaError_t sample_rows(float *logits, int S, int V, SampleParams cfg, const uint32_t *history,
                         const uint32_t *history_len, int history_stride, uint64_t *rng, uint32_t *out, int *err,
-                        void *ws, size_t ws_bytes, cudaStream_t st) {
+                        void *ws, size_t ws_bytes, cudaStream_t st, const SamplePrepared *prep) {
     if (S <= 0 || V <= 0) return cudaSuccess;
     static bool attr_set = false;
     if (!attr_set) {
@@ -867,7 +926,8 @@ cudaError_t sample_rows(float *logits, int S, int V, SampleParams cfg, const uin
         attr_set = true;
     }
     int grid = std::min(S, resident_ctas());
-    SampleArgs a{logits, S, V, cfg, history, history_len, history_stride, rng, out, err, nullptr, 0};
+    SampleArgs a{logits, S, V, cfg, history, history_len, history_stride, rng, out, err, nullptr, 0,
+                 prep ? prep->max : nullptr, prep ? prep->pinf : nullptr, prep ? prep->parts : 0};
     if (needs_lazy_sort(V, cfg)) {
         const size_t per = (size_t)2 * V * sizeof(uint64_t);
         const size_t fit = ws ? ws_bytes / per : 0;

@@ -110,18 +110,62 @@ struct TcArgs {
     float *ws;
     int *flags;
     int l2hints;  // 1: weights loaded evict-last, staged outputs stored evict-first
+    // Sampling preparation of a logits projection (temperature > 0; store
+    // mode, no bias / residual, whole tiles): C = pen(acc) / temperature,
+    // pen = the repetition penalty where bit (row, column) of pen_bits
+    // ([M][pen_words] u32) is set; per row and half tile the maximum of the
+    // finite outputs and the number of +inf ones go to prep_max / prep_pinf
+    // (slot layout of the argmax partials).
+    float temperature;
+    float rep_penalty;
+    const uint32_t *pen_bits;
+    int pen_words;
+    float *prep_max;
+    uint32_t *prep_pinf;
+    // Bound of the stream-K hand-off waits (ns), and a test control: when
+    // set, no CTA publishes its partial tiles, so every finisher's wait runs
+    // out and reports code 121 (the failure path, exercised without a fault).
+    uint64_t handoff_wait_ns;
+    int withhold_publish;
+    // Split-K (splits > 0; 128-wide tiles, store and SwiGLU modes, one row
+    // of tiles): piece g is K-blocks [s * kps, (s + 1) * kps) of tile
+    // g / splits, s = g % splits, and its raw sum goes to
+    // split_part[(s * M + row) * N + col]; splitk_reduce_k then adds the
+    // pieces in split order and applies the epilogue.
+    int splits;
+    int kps;
+    float *split_part;
 };
+
+// infer.rs:239-247 then 253-256 for one logit: the repetition penalty when
+// the token is in the history window, then the temperature division.
+__device__ __forceinline__ float sample_prep(float x, bool penalised, const TcArgs &p) {
+    if (penalised) x = x > 0.0f ? __fdiv_rn(x, p.rep_penalty) : __fmul_rn(x, p.rep_penalty);
+    return __fdiv_rn(x, p.temperature);
+}
 
 // One piece of a CTA's work: tile t, K-blocks [kb0, kb1).  np < 0: a partial
 // piece (written to ws slot blockIdx.x); np == 0: the whole tile; np > 0:
 // the tile's first K-blocks, finished after adding slots blockIdx.x + 1 ..
 // blockIdx.x + np.
 struct Piece {
-    int t, kb0, kb1, np;
+    int t, kb0, kb1, np, split;
 };
 
 __device__ __forceinline__ bool next_piece(const TcArgs &p, int n_tiles, int kblocks, int &cursor, Piece &pc) {
     const int G = gridDim.x, c = blockIdx.x;
+    if (p.splits > 0) {
+        const long g = (long)c + (long)cursor * G;
+        if (g >= (long)n_tiles * p.splits) return false;
+        ++cursor;
+        pc.t = (int)(g / p.splits);
+        pc.split = (int)(g % p.splits);
+        pc.kb0 = pc.split * p.kps;
+        pc.kb1 = min(kblocks, pc.kb0 + p.kps);
+        pc.np = 0;
+        return true;
+    }
+    pc.split = -1;
     const int dp_tiles = p.skb > 0 ? p.sk_t0 : n_tiles;
     const int n_dp = c < dp_tiles ? (dp_tiles - c + G - 1) / G : 0;
     if (cursor < n_dp) {
@@ -272,12 +316,43 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // ([BM][BN] raw sums, no bias / residual / SwiGLU) instead of C; parts !=
 // null adds the nparts partial tiles at parts, parts + BM*BN, ... in order
 // before the bias and residual (or SwiGLU).
-template <int BN>
+// Kernel variants: the general projection (store / SwiGLU / argmax
+// epilogues, stream-K), the logits projection with the sampling epilogue,
+// and split-K pieces; separate instantiations keep each one's registers.
+constexpr int MODE_GENERAL = 0, MODE_PREP = 1, MODE_SPLIT = 2;
+
+template <int BN, int MODE = MODE_GENERAL>
 __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, int q, int lane, int m0, int n0,
                                               int c_begin, int c_end, bool argmax_mode, bool vec, float &best,
                                               uint32_t &best_n, float *stg, const float *parts = nullptr,
-                                              int nparts = 0, float *part_out = nullptr) {
+                                              int nparts = 0, float *part_out = nullptr, int split = -1) {
     const int row = m0 + q * 32 + lane;
+    if constexpr (MODE == MODE_SPLIT) {
+        // Split-K piece: the raw sum of both accumulator chains, rows < M.
+        for (int c0 = c_begin; c0 < c_end; c0 += 32) {
+            if (n0 + c0 >= p.N) break;  // warp-uniform
+            float v[32], corr[32];
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
+            if (row < p.M) {
+                float *dst = p.split_part + ((size_t)split * p.M + row) * p.N + n0 + c0;
+                const bool full = n0 + c0 + 32 <= p.N && (p.N & 3) == 0;
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) {
+                    if (full) {
+                        *reinterpret_cast<float4 *>(dst + j) =
+                            make_float4(v[j] + corr[j], v[j + 1] + corr[j + 1], v[j + 2] + corr[j + 2],
+                                        v[j + 3] + corr[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj)
+                            if (n0 + c0 + j + jj < p.N) dst[j + jj] = v[j + jj] + corr[j + jj];
+                    }
+                }
+            }
+        }
+        return;
+    }
     if (stg && !argmax_mode) {
         const uint64_t pol_out = policy_evict_first();
         // Transpose each 32 x 32 chunk through this warp's shared buffer
@@ -357,6 +432,23 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
             float v[32], corr[32];
             tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
             tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
+            if constexpr (MODE == MODE_PREP) {
+                // lane = row here: penalty bits of 32 columns in one word,
+                // the row's running maximum and +inf count in registers.
+                const int nb = n0 + c0;
+                const uint32_t pw =
+                    (p.pen_bits && row < p.M) ? p.pen_bits[(size_t)row * p.pen_words + (nb >> 5)] : 0u;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float y = sample_prep(v[j] + corr[j], (pw >> j) & 1u, p);
+                    v[j] = y;
+                    corr[j] = 0.0f;
+                    if (nb + j < p.N) {
+                        if (y == INFINITY) ++best_n;
+                        if (isfinite(y) && y > best) best = y;
+                    }
+                }
+            }
 #pragma unroll
             for (int c4 = 0; c4 < 8; ++c4) {
                 float4 o;
@@ -462,6 +554,17 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = v[j] + corr[j];
         const int nb = n0 + c0;
+        if constexpr (MODE == MODE_PREP) {
+            const uint32_t pw = (p.pen_bits && row < p.M) ? p.pen_bits[(size_t)row * p.pen_words + (nb >> 5)] : 0u;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                v[j] = sample_prep(v[j], (pw >> j) & 1u, p);
+                if (nb + j < p.N) {
+                    if (v[j] == INFINITY) ++best_n;
+                    if (isfinite(v[j]) && v[j] > best) best = v[j];
+                }
+            }
+        }
         if (argmax_mode) {
             // First strict maximum over this tile's columns, NaN skipped.
 #pragma unroll
@@ -509,7 +612,7 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
     }
 }
 
-template <int BN>
+template <int BN, int MODE>
 __global__ void __launch_bounds__(THREADS, Tile<BN>::CTAS_PER_SM)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
@@ -700,7 +803,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                                          : "l"(p.flags + blockIdx.x + c)
                                          : "memory");
                             if (v) break;
-                            if (globaltimer() - t0 > WAIT_NS) {
+                            if (globaltimer() - t0 > p.handoff_wait_ns) {
                                 atomicExch(p.err, 121);
                                 break;
                             }
@@ -722,12 +825,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 __syncwarp();
             }
             const int row = m0 + q * 32 + lane;
+            constexpr bool prep_mode = MODE == MODE_PREP;
             float best = -INFINITY;
-            uint32_t best_n = 0xFFFFFFFFu;
+            uint32_t best_n = prep_mode ? 0u : 0xFFFFFFFFu;
             float *stg =
                 BN == 256 ? reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES) + (warp - 4) * 1024 : nullptr;
-            epilogue_cols<BN>(p, tmem, q, lane, m0, n0, half * COLS, (half + 1) * COLS, argmax_mode, vec, best, best_n,
-                              stg, parts, pc.np > 0 ? pc.np : 0, part_out);
+            epilogue_cols<BN, MODE>(p, tmem, q, lane, m0, n0, half * COLS, (half + 1) * COLS, argmax_mode, vec, best, best_n,
+                              stg, parts, pc.np > 0 ? pc.np : 0, part_out, pc.split);
             // TMEM of this piece fully read: hand the accumulators back.
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -747,7 +851,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                             break;
                         }
                     __threadfence();
-                    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p.flags + blockIdx.x), "r"(1) : "memory");
+                    if (!p.withhold_publish)
+                        asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p.flags + blockIdx.x), "r"(1)
+                                     : "memory");
                 }
                 __syncwarp();
             }
@@ -759,6 +865,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 const size_t slot = (size_t)row * p.n_tiles + 2 * tn + half;
                 p.best_val[slot] = best;
                 p.best_idx[slot] = best_n;
+            }
+            if (prep_mode && row < p.M) {  // MODE_PREP only
+                const size_t slot = (size_t)row * p.n_tiles + 2 * tn + half;
+                p.prep_max[slot] = best;
+                p.prep_pinf[slot] = best_n;
             }
         }
     }
@@ -1072,6 +1183,46 @@ __global__ void split_tf32_t_k(const float *__restrict__ src, int rows, int cols
     }
 }
 
+// Split-K reduction: out = sum over splits (in split order) of the pieces'
+// raw sums, then the store epilogue (bias, residual) or the SwiGLU epilogue
+// of the interleaved operand (output channel j: gate column 64 (j / 32) +
+// j % 32, value column 32 later), with the same f32 operations as the
+// single-piece epilogues.
+__global__ void splitk_reduce_k(const float *__restrict__ part, int splits, int M, int N, const float *bias,
+                                const float *R, int ldr, float *C, int ldc, float *C_lo, int swiglu_H) {
+    pdl_trigger();
+    pdl_wait();
+    const int cols = swiglu_H ? swiglu_H : N;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)M * cols) return;
+    const int m = (int)(i / cols), c = (int)(i - (long)m * cols);
+    const size_t plane = (size_t)M * N;
+    if (swiglu_H) {
+        const int cg = 64 * (c >> 5) + (c & 31), cv = cg + 32;
+        const float *pg = part + (size_t)m * N + cg, *pv = part + (size_t)m * N + cv;
+        float g = pg[0], v = pv[0];
+        for (int sp = 1; sp < splits; ++sp) {
+            g = g + pg[sp * plane];
+            v = v + pv[sp * plane];
+        }
+        const float sv = silu(g + bias[c]) * (v + bias[swiglu_H + c]);
+        if (C_lo) {
+            const float h = tf32_round(sv);
+            C[(size_t)m * ldc + c] = h;
+            C_lo[(size_t)m * ldc + c] = tf32_round(sv - h);
+        } else {
+            C[(size_t)m * ldc + c] = sv;
+        }
+        return;
+    }
+    const float *pp = part + (size_t)m * N + c;
+    float o = pp[0];
+    for (int sp = 1; sp < splits; ++sp) o = o + pp[sp * plane];
+    if (bias) o = o + bias[c];
+    if (R) o = R[(size_t)m * ldr + c] + o;
+    C[(size_t)m * ldc + c] = o;
+}
+
 // ---- host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1227,14 +1378,14 @@ void tc_weights_free(TcWeights &w) {
     w.ready = false;
 }
 
-template <int BN>
+template <int BN, int MODE>
 cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, TcArgs a, int M,
                       cudaStream_t st) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
     if (attr_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Tile<BN>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
         attr_dev = dev;
@@ -1250,14 +1401,14 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
     }
     const long tiles = (long)tc_tiles_n(W.N, BN) * ((M + BM - 1) / BM);
     const long slots = (long)num_sms * Tile<BN>::CTAS_PER_SM;
-    unsigned grid = (unsigned)std::min<long>(tiles, slots);
+    unsigned grid = (unsigned)std::min<long>(a.splits > 0 ? tiles * a.splits : tiles, slots);
     a.skb = 0;
     a.sk_t0 = (int)tiles;
     // The A operand pair (hi + lo) of this projection; when it fits well
     // inside L2, CTAs far apart in the tile order lose nothing by reading
     // different rows of it, and every tile is spread by K.
     const bool a_in_l2 = (size_t)M * W.K * 8 <= ((size_t)48 << 20);
-    if (BN == 256 && !a.best_val && a.ws && a.flags && (tiles % slots != 0 || a_in_l2)) {
+    if (BN == 256 && !a.best_val && !(a.temperature > 0.0f) && a.ws && a.flags && (tiles % slots != 0 || a_in_l2)) {
         // Whole waves stay whole tiles (unless A fits in L2); the rest is
         // spread over every CTA in equal K-block ranges of at least 8 K-blocks.
         const long dp = a_in_l2 ? 0 : (tiles / slots) * slots;
@@ -1270,7 +1421,7 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
         a.sk_t0 = (int)dp;
         grid = (unsigned)(dp > 0 ? slots : ctas);
     }
-    return pdl_launch(tc_gemm_kernel<BN>, dim3(grid), dim3(THREADS), Tile<BN>::SMEM_BYTES, st, mAh, mAl,
+    return pdl_launch(tc_gemm_kernel<BN, MODE>, dim3(grid), dim3(THREADS), Tile<BN>::SMEM_BYTES, st, mAh, mAl,
                       *(const CUtensorMap *)mh, *(const CUtensorMap *)ml, a);
 }
 
@@ -1314,8 +1465,14 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     }
     alignas(64) CUtensorMap mAh, mAl;
     if (!make_map(&mAh, A_hi, M, K, BM) || !make_map(&mAl, A_lo, M, K, BM)) return cudaErrorInvalidValue;
+    const bool prep = ep.temperature > 0.0f;
+    if (prep && (bn == TC_PAIR || ep.swiglu || ep.best_val || ep.bias || ep.R || !ep.C || !ep.prep_max ||
+                 !ep.prep_pinf || !(ep.temperature < INFINITY) || (ep.pen_bits && ep.pen_words < (W.N + 31) / 32)))
+        return cudaErrorInvalidValue;
     TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err,
-              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 0, ep.ws, ep.flags, ep.l2hints ? 1 : 0};
+              ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 0, ep.ws, ep.flags, ep.l2hints ? 1 : 0,
+              prep ? ep.temperature : 0.0f, ep.rep_penalty, ep.pen_bits, ep.pen_words, ep.prep_max, ep.prep_pinf,
+              ep.handoff_wait_ns ? ep.handoff_wait_ns : WAIT_NS, ep.withhold_publish ? 1 : 0, 0, 0, nullptr};
     if (a.ws) {
         // Stream-K needs one partial slot and one counter per SM.
         const int sms = sm_count_cached();
@@ -1324,8 +1481,43 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
             a.flags = nullptr;
         }
     }
+    // One row of tiles that fills under half of the CTA slots: split K so
+    // that every SM streams its share of the weights (the regime of 9-128
+    // streams, where the projection is bound by the weight stream).
+    int splits = 0, kps = 0;
+    if (bn == 128 && ep.ws && M <= BM && !ep.best_val && !prep) {
+        const long slots = 2L * sm_count_cached();
+        const long tiles = tc_tiles_n(W.N, 128);
+        const int kblocks = (K + BK - 1) / BK;
+        if (tiles * 2 <= slots && kblocks >= 4) {
+            splits = (int)std::min<long>(kblocks / 2, std::max<long>(2, slots / tiles));
+            kps = (kblocks + splits - 1) / splits;
+            splits = (kblocks + kps - 1) / kps;
+            while (splits > 1 && (size_t)splits * M * W.N > ep.ws_floats) {
+                kps *= 2;
+                splits = (kblocks + kps - 1) / kps;
+            }
+            if (splits < 2) splits = 0;
+        }
+    }
+    if (ep.launches) *ep.launches += splits ? 2 : 1;
     if (bn == TC_PAIR) return launch_pair(mAh, mAl, W, a, M, st);
-    return bn == 256 ? launch_tc<256>(mAh, mAl, W, a, M, st) : launch_tc<128>(mAh, mAl, W, a, M, st);
+    if (splits) {
+        a.splits = splits;
+        a.kps = kps;
+        a.split_part = ep.ws;
+        cudaError_t e = launch_tc<128, MODE_SPLIT>(mAh, mAl, W, a, M, st);
+        if (e != cudaSuccess) return e;
+        const long outs = (long)M * (ep.swiglu ? W.pair_half : W.N);
+        return pdl_launch(splitk_reduce_k, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st,
+                          (const float *)ep.ws, splits, M, W.N, ep.bias, ep.R, ep.ldr, ep.C, ep.ldc, ep.C_lo,
+                          ep.swiglu ? W.pair_half : 0);
+    }
+    if (prep)
+        return bn == 256 ? launch_tc<256, MODE_PREP>(mAh, mAl, W, a, M, st)
+                         : launch_tc<128, MODE_PREP>(mAh, mAl, W, a, M, st);
+    return bn == 256 ? launch_tc<256, MODE_GENERAL>(mAh, mAl, W, a, M, st)
+                     : launch_tc<128, MODE_GENERAL>(mAh, mAl, W, a, M, st);
 }
 
 }  // namespace nk

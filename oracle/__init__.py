@@ -69,6 +69,7 @@ class SampleInfo(C.Structure):
         ("cdf_margin", C.c_double),
         ("cut_margin", C.c_double),
         ("top2_margin", C.c_double),
+        ("order_margin", C.c_double),
     ]
 
 

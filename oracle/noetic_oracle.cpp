@@ -670,6 +670,7 @@ uint32_t sample_impl(float *logits, uint64_t vocab, const orc_sample_cfg *cfg,
                      orc_sample_info *info) {
     if (vocab == 0) throw std::runtime_error("cannot sample from an empty vocabulary");
     orc_sample_info local{};
+    local.order_margin = INFINITY;
     if (std::isfinite(cfg->rep_penalty) && cfg->rep_penalty > 1.0f && cfg->rep_window > 0) {
         uint64_t start = n_hist > cfg->rep_window ? n_hist - cfg->rep_window : 0;
         for (uint64_t i = start; i < n_hist; ++i) {
@@ -759,6 +760,17 @@ uint32_t sample_impl(float *logits, uint64_t vocab, const orc_sample_cfg *cfg,
     (void)found;
     local.cdf_margin = margin / total;
     local.token = chosen;
+    {
+        uint64_t c = 0;
+        while (c + 1 < n_cand && idx[c] != chosen) ++c;
+        const double pc = (double)logits[idx[c]];
+        double om = INFINITY;
+        if (pc > 0.0) {
+            if (c > 0) om = std::min(om, ((double)logits[idx[c - 1]] - pc) / pc);
+            if (c + 1 < n_cand) om = std::min(om, (pc - (double)logits[idx[c + 1]]) / pc);
+        }
+        local.order_margin = om;
+    }
     if (info) *info = local;
     return chosen;
 }

@@ -62,6 +62,9 @@ typedef struct orc_sample_info {
     double cdf_margin;      /* distance of draw to the nearest CDF edge, / total */
     double cut_margin;      /* min |cumulative - top_p| at the cut and one entry before it */
     double top2_margin;     /* greedy: best - second best logit */
+    double order_margin;    /* min relative gap between the chosen probability and its
+                               neighbours in the sorted candidates (a swap of two nearly
+                               equal probabilities moves the CDF slots of both) */
 } orc_sample_info;
 
 const char *orc_last_error(void);

@@ -93,12 +93,44 @@ def test_c2_sampled_generate_at_full_shape(gpu, orc):
         for i in range(N):
             tok, info = orc.sample_token(lg, ocfg, [], r, info=True)
             if tok != int(out[s, i]):
-                assert info.cdf_margin < 1e-5 or info.cut_margin < 1e-6, (s, i)
+                # The device's logits differ from the oracle's within the
+                # logits tolerance, so a decision may flip only at a near-tie:
+                # a draw next to a CDF edge, a cut next to top_p, or the chosen
+                # probability next to an almost equal neighbour in the order.
+                assert info.cdf_margin < 1e-5 or info.cut_margin < 1e-6 or info.order_margin < 2e-4, (s, i)
                 soft += 1
             if i + 1 < N:
                 lg = od.step(int(out[s, i])).copy()
         assert r.s == [int(v) for v in rng[s]], s
-    assert soft <= 4
+    assert soft <= 41  # 1 % of the teacher-forced draws
+
+
+def test_c2_sampler_is_exact_on_the_device_logits(gpu, orc):
+    """The sampler alone at the C2 batch: every stream's logits of 48 steps
+    (device-computed, downloaded) sampled by the oracle give the device's
+    token and rng state exactly."""
+    kw = c1_cfg(dict)
+    _, gm = same_model(orc, gpu, kw, seed=0)
+    S, T = 256, 128
+    from noetic_b200 import prompts
+
+    ids = prompts.uniform_prompts(S, T, 1024, 2000)
+    dec = gpu.Decoder(gm, S)
+    lg = dec.prefill(ids).copy()
+    rng = prompts.rng_states(np.arange(S, dtype=np.uint64) + np.uint64(3000))
+    orngs = [orc.Rng(3000 + s) for s in range(S)]
+    ocfg = orc.SampleCfg(**C2_CFG)
+    differ = 0
+    for step in range(48):
+        tok = dec.sample(gpu.SampleCfg(**C2_CFG), rng)
+        for s in range(S):
+            t, info = orc.sample_token(lg[s].copy(), ocfg, [], orngs[s], info=True)
+            differ += int(t != int(tok[s]))
+            assert orngs[s].s == [int(v) for v in rng[s]], (step, s)
+        lg = dec.step(tok).copy()
+    # glibc's expf differs from the correctly rounded exp on ~0.07 % of
+    # arguments; a decision moves only if that changes a sum's rounding.
+    assert differ <= 2, differ
 
 
 def test_c4_headline_at_16384_streams(gpu, orc):

@@ -231,3 +231,39 @@ def test_fewer_streams_than_a_tile(gpu, orc, S):
     toks = ids[:, -1].copy()
     ga, gb = tc.step_greedy(toks).copy(), f32.step_greedy(toks).copy()
     assert (ga == gb).mean() > 0.95
+
+
+C5_WIDTHS = dict(vocab=16384, d_model=768, n_layer=2, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+
+
+@pytest.mark.parametrize("S", [64, 127, 512])
+def test_long_prompt_model_widths_at_serving_batches(gpu, orc, S):
+    """The long-prompt model's widths (d 768, H 2304, V 16384) at 64 / 127 /
+    512 streams.  Up to 128 streams every projection has one row of tiles and
+    is split along K over the SMs (pieces summed in a fixed order by a
+    reduction kernel); the result matches the f32 engine and the oracle, and
+    two decoders agree bit for bit."""
+    om, gm = same_model(orc, gpu, C5_WIDTHS, seed=3)
+    T = 3
+    ids = _ids(S, T, C5_WIDTHS["vocab"], 6000)
+    tc, tc2, f32 = gpu.Decoder(gm, S), gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    f32.set_engine(1)
+    tc.profile_begin()
+    for t in range(T):
+        a = tc.step(ids[:, t]).copy()
+        a2 = tc2.step(ids[:, t]).copy()
+        b = f32.step(ids[:, t])
+        assert np.array_equal(a, a2), t
+        assert np.abs(a - b).max() <= 1e-4, t
+    assert tc.profile_end()["tensor_core"]
+    sa, ha = tc.get_state()
+    sb, hb = f32.get_state()
+    assert np.array_equal(ha, hb) and state_rel_err(sa, sb) <= 1e-5
+    for s in [0, S - 1]:
+        od = orc.Decoder(om)
+        for t in range(T):
+            ref = od.step(ids[s, t])
+        assert np.abs(a[s] - ref).max() <= 1e-3, s
+    toks = ids[:, -1].copy()
+    ga, gb = tc.step_greedy(toks).copy(), f32.step_greedy(toks).copy()
+    assert (ga == gb).mean() > 0.95
