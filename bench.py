@@ -38,6 +38,7 @@ MODEL_SEED = 2
 STREAMS = 16384
 PROMPT_LEN = 64
 PROMPT_SEED_BASE = 5000
+SAMPLED_TOKENS = 8
 WORKLOAD = "d1024 L24 E=d V32768 (seed 2), 16384 streams x 64-token uniform prompts, greedy decode"
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 TRAFFIC_PATH = os.path.join(ROOT, "profiles", "traffic.json")
@@ -818,6 +819,39 @@ def run_ours(args, rank, world, local_rank):
                                    "us_per_token": us_m, "launches_per_token": launches_m,
                                    "frac": (weight_bytes + state_bytes) / (us_m * 1e-6) / 1e9 / peaks["hbm_gbs"]}}
 
+    # ---- sampled decode at the headline shape: SampleCfg::default_cfg
+    # (temperature 0.9, top_k 40, top_p 0.95, repetition penalty 1.1 over 64)
+    # through generate, whose logits projection carries the penalty,
+    # temperature and row maxima into the sampler; 1-token prompts, so the
+    # call is one prompt step and SAMPLED_TOKENS sampled tokens per stream.
+    sampled = None
+    if not args.no_configs:
+        default_cfg = nb.SampleCfg.default_cfg()
+        one = np.ascontiguousarray(ids[:, :1])
+        lens1 = np.ones(count, np.uint32)
+        seeds = np.arange(first, first + count, dtype=np.uint64) + np.uint64(3000)
+        from noetic_b200.prompts import rng_states
+
+        dec.generate(one, lens1, 2, default_cfg, rng_states(seeds))  # sizes the sampler's buffers
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        dec.generate(one, lens1, SAMPLED_TOKENS, default_cfg, rng_states(seeds))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        gen_ms = max_over_ranks(e0.elapsed_time(e1))
+        dec.profile_begin()
+        dec.generate(one, lens1, SAMPLED_TOKENS, default_cfg, rng_states(seeds))
+        sprof = dec.profile_end()
+        barrier()
+        sampled = {"workload": (f"headline model, {n_streams} streams, 1-token prompts, {SAMPLED_TOKENS} tokens "
+                                f"sampled with SampleCfg::default_cfg (T 0.9, top_k 40, top_p 0.95, "
+                                f"penalty 1.1 / 64) through generate"),
+                   "tokens_per_s": n_streams * SAMPLED_TOKENS / (gen_ms / 1000.0), "ms": gen_ms,
+                   "sampler_ms_per_token": sprof["sample_ms"] / SAMPLED_TOKENS,
+                   "sampler_share": sprof["sample_ms"] / gen_ms if gen_ms > 0 else None,
+                   "note": "sampler time from its own CUDA events in a second, profiled run"}
+
     configs = None
     if rank == 0 and world == 1 and not args.no_configs:
         configs = run_configs(args)
@@ -878,6 +912,7 @@ def run_ours(args, rank, world, local_rank):
                          "proj_launches_per_step": prof["proj_launches"] / args.steps},
             "clocks": clocks,
             "batch1": batch1,
+            "sampled": sampled,
             "configs": configs,
             "cpu_baseline": cpu_baseline,
             "setup": {"init_s": round(init_s, 2)},

@@ -231,7 +231,11 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * its first grid-barrier arrival (every CTA's bounded wait runs out: code
  * 113); those waits are bounded at 2 ms instead of 1 s.  The call returns
  * NK_ERR_DEVICE; the decoder stays usable (restore its state with
- * nk_decoder_set_state: the failed step's results are not valid). */
+ * nk_decoder_set_state: the failed step's results are not valid).
+ * Bit 14: stand-alone RMSNorm kernels in the tensor-core decode step instead
+ * of the default folded form (each residual projection's epilogue writes the
+ * next projection's gain-scaled operand and the rows' sums of squares, and
+ * the consumer scales its rows by the RMSNorm factor). */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

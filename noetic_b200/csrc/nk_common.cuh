@@ -6,13 +6,18 @@
 
 namespace nk {
 
-// tensor.rs:276-283: the branchy stable sigmoid.  CUDA's expf is used (the
-// reference calls the platform libm expf); results agree within expf's
-// error bound, not bit-for-bit.
+// tensor.rs:276-283: the branchy stable sigmoid, 1 / (1 + e^-x) for x >= 0
+// and e^x / (1 + e^x) below, written without a branch: e = exp(-|x|) is the
+// exponential either branch takes, and the numerator is 1 or e, so each
+// lane performs exactly its branch's operations while a warp with inputs of
+// both signs runs one exp and one division instead of both paths.  CUDA's
+// expf is used (the reference calls the platform libm expf); results agree
+// within expf's error bound, not bit-for-bit.  NaN propagates as in the
+// reference's second branch.
 __device__ __forceinline__ float sigmoid(float x) {
-    if (x >= 0.0f) return 1.0f / (1.0f + expf(-x));
-    float e = expf(x);
-    return e / (1.0f + e);
+    const bool pos = x >= 0.0f;
+    const float e = expf(pos ? -x : x);
+    return (pos ? 1.0f : e) / (1.0f + e);
 }
 
 __device__ __forceinline__ float silu(float x) { return x * sigmoid(x); }

@@ -190,6 +190,9 @@ cudaError_t sample_rows(float *logits, int S, int V, SampleParams cfg, const uin
                         const uint32_t *history_len, int history_stride, uint64_t *rng,
                         uint32_t *out, int *err, void *ws, size_t ws_bytes, cudaStream_t st,
                         const SamplePrepared *prep = nullptr);
+// Token collection of generate: out[s * n_new + *column] = tok[s], then
+// *column += 1 (two launches; graph-capturable, the column lives on the device).
+cudaError_t collect_tokens(const uint32_t *tok, uint32_t *out, int S, int n_new, int *column, cudaStream_t st);
 // bits [S][words] = the distinct tokens < V of each stream's last rep_window
 // history entries (all zero when the penalty is off), for the sampling
 // epilogue of the logits projection.

@@ -84,6 +84,24 @@ struct TcEpilogue {
     // Incremented by the number of kernels tc_gemm launched (nullable): one,
     // or two when a single row of tiles is split along K and reduced.
     uint64_t *launches = nullptr;
+    // Set (nullable) to the number of argmax / sampling partials per row the
+    // launch wrote: tc_argmax_parts(N, bn), or ceil(N / 1024) when a small
+    // projection was split along K.
+    int *parts_out = nullptr;
+    // RMSNorm folded into the projections (tensor.rs:298-312).  Consumer:
+    // with rs_parts ([M, rs_nparts] partial sums of squares of the
+    // un-normalised rows x), the A operand is the split of x * gain and each
+    // accumulator row is multiplied by 1 / sqrt(sum / rs_d + rs_eps) before
+    // the bias.  Producer (store mode): nx_hi / nx_lo [M, N] receive the
+    // split of x * nx_gain of the stored rows x, and nx_ss [M, ceil(N / 32)]
+    // each row's sum of squares per 32-column chunk.
+    const float *rs_parts = nullptr;
+    int rs_nparts = 0;
+    int rs_d = 0;
+    float rs_eps = 0.0f;
+    float *nx_hi = nullptr, *nx_lo = nullptr;
+    const float *nx_gain = nullptr;
+    float *nx_ss = nullptr;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.

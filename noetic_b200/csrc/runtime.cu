@@ -546,6 +546,10 @@ struct nk_decoder {
     size_t p_ids_cap = 0;
     // 3xTF32 activation operand pair (decode) and the fused argmax partials
     float *ahi = nullptr, *alo = nullptr;
+    // RMSNorm folded into the projections: the normalised operand's pair
+    // (split of x * gain, [S, d]) and the rows' partial sums of squares
+    // ([S, ceil(d / 32)]) the producing epilogue writes
+    float *nhi = nullptr, *nlo = nullptr, *nss = nullptr;
     float *best_val = nullptr;
     uint32_t *best_idx = nullptr;
     // prefill operand pair
@@ -598,7 +602,8 @@ struct nk_decoder {
             if (p) cudaFree(p);
         for (void *p : {(void *)ahi, (void *)alo, (void *)best_val, (void *)best_idx, (void *)p_ahi, (void *)p_alo,
                         (void *)players_dev, (void *)pws, (void *)ksplit_ws, (void *)ksplit_flags, samp_ws,
-                        (void *)pen_bits, (void *)prep_max, (void *)prep_pinf})
+                        (void *)pen_bits, (void *)prep_max, (void *)prep_pinf, (void *)nhi, (void *)nlo,
+                        (void *)nss})
             if (p) cudaFree(p);
         for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
         for (cudaEvent_t e : samp_ev) cudaEventDestroy(e);
@@ -692,6 +697,7 @@ struct SampScope {
 // recovery) runs without a fault and without a hang.
 constexpr int ENGINE_WITHHOLD_PUBLISH = 4096;
 constexpr int ENGINE_WITHHOLD_ARRIVAL = 8192;
+constexpr int ENGINE_NO_FOLD = 16384;  // stand-alone RMSNorm kernels instead of the folded form
 constexpr uint64_t TEST_WAIT_NS = 2000000ull;
 void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
     if (dec->engine & ENGINE_WITHHOLD_PUBLISH) {
@@ -710,9 +716,34 @@ int pick_bn(const nk_decoder *dec, int M, int N, bool argmax = false) {
     return nk::tc_pick_bn(M, N, false, !argmax && !(dec->engine & 256));
 }
 
+// RMSNorm folded into a tensor-core projection: `rs` (the partial sums of
+// squares of the rows whose gain-scaled split is the A operand) makes it a
+// consumer; `nx_gain` makes a store-mode projection the producer of the
+// next one's operand and sums.
+struct Fold {
+    const float *rs = nullptr;
+    const float *nx_gain = nullptr;
+};
+void apply_fold(nk_decoder *dec, const Fold *f, nk::TcEpilogue &ep) {
+    if (!f) return;
+    const int d = (int)dec->model->d();
+    if (f->rs) {
+        ep.rs_parts = f->rs;
+        ep.rs_nparts = (d + 31) / 32;
+        ep.rs_d = d;
+        ep.rs_eps = dec->model->cfg.eps;
+    }
+    if (f->nx_gain) {
+        ep.nx_hi = dec->nhi;
+        ep.nx_lo = dec->nlo;
+        ep.nx_gain = f->nx_gain;
+        ep.nx_ss = dec->nss;
+    }
+}
+
 // C = A.W^T (+bias) (R + ...), A read from `a` in the form `tc` selects.
 void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W, const nk::TcOperand *Wtc,
-             int N, const float *bias, float *C, const float *R) {
+             int N, const float *bias, float *C, const float *R, const Fold *fold = nullptr) {
     ProfScope prof(dec, M, N, K, R != nullptr, bias != nullptr);
     if (tc) {
         nk::TcEpilogue ep;
@@ -727,6 +758,7 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         ep.flags = dec->ksplit_flags;
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
         test_controls(dec, ep);
+        apply_fold(dec, fold, ep);
         ep.launches = &dec->launches;
         cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, N), dec->stream, dec->err),
                    "tcgen05 projection");
@@ -745,7 +777,7 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
 // `gated`'s pair, which may be the A operand this projection is reading.
 // Otherwise the product goes to `scratch` and a row kernel applies SwiGLU.
 Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W, const nk::TcOperand *Wtc,
-                   int H, const float *bias, float *scratch, const Act &gated, bool t_dn) {
+                   int H, const float *bias, float *scratch, const Act &gated, bool t_dn, const Fold *fold = nullptr) {
     if (tc && Wtc->pair_half == H) {
         ProfScope prof(dec, M, 2 * H, K, false, true);
         nk::TcEpilogue ep;
@@ -758,6 +790,7 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
         ep.flags = dec->ksplit_flags;
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
         test_controls(dec, ep);
+        apply_fold(dec, fold, ep);
         Act out = gated;
         if (t_dn) {
             out = Act{nullptr, scratch, scratch + (size_t)M * H};
@@ -773,7 +806,7 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
         return out;
     }
     if (tc && Wtc->pair_half) fail(NK_ERR_INVALID, "interleaved up_proj operand with a different hidden width");
-    project(dec, tc, a, M, K, W, Wtc, 2 * H, bias, scratch, nullptr);
+    project(dec, tc, a, M, K, W, Wtc, 2 * H, bias, scratch, nullptr, fold);
     launch_ok(dec, nk::swiglu_rows(scratch, gated.out(t_dn), M, H, dec->stream), "swiglu");
     return gated;
 }
@@ -781,9 +814,10 @@ Act project_swiglu(nk_decoder *dec, bool tc, const Act &a, int M, int K, const f
 // tokens[m] = argmax_n (A.W^T)[m, n] without storing the product when the
 // tensor-core engine runs it (first strict maximum, tensor.rs:354-365).
 void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W,
-                    const nk::TcOperand *Wtc, int N, uint32_t *tokens) {
+                    const nk::TcOperand *Wtc, int N, uint32_t *tokens, const Fold *fold = nullptr) {
     if (tc) {
         const int bn = pick_bn(dec, M, N, true);
+        int parts = 0;
         {
             ProfScope prof(dec, M, N, K, false, false);
             nk::TcEpilogue ep;
@@ -791,10 +825,16 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
             ep.best_idx = dec->best_idx;
             ep.l2hints = false;  // the tied embedding (268 MB as hi + lo) does not fit L2
             ep.launches = &dec->launches;
+            ep.parts_out = &parts;
+            if (!(dec->engine & 256)) {  // small projections split along K use the workspace
+                ep.ws = dec->ksplit_ws;
+                ep.ws_floats = nk::tc_stream_k_ws_floats();
+            }
+            apply_fold(dec, fold, ep);
             cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, bn, dec->stream, dec->err), "tcgen05 projection");
             dec->prof_tc = dec->prof_tc || dec->profiling;
         }
-        launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, nk::tc_argmax_parts(N, bn), M, tokens, dec->stream),
+        launch_ok(dec, nk::argmax_partials(dec->best_val, dec->best_idx, parts, M, tokens, dec->stream),
                   "argmax partials");
     } else {
         project(dec, false, a, M, K, W, Wtc, N, nullptr, dec->logits, nullptr);
@@ -804,11 +844,12 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
 
 // Logits projection with the sampling epilogue (pen(logit) / temperature
 // into dec->logits, part maxima and +inf counts); returns the part count.
-int project_sample_prep(nk_decoder *dec, const Act &a, int M, int K, const nk::TcOperand *Wtc, int N) {
+int project_sample_prep(nk_decoder *dec, const Act &a, int M, int K, const nk::TcOperand *Wtc, int N,
+                        const Fold *fold = nullptr) {
     const nk::SampleParams &sp = *dec->fuse_sample;
     int bn = pick_bn(dec, M, N, true);
     if (bn == nk::TC_PAIR) bn = 256;
-    const int parts = nk::tc_argmax_parts(N, bn);
+    int parts = 0;
     ProfScope prof(dec, M, N, K, false, false);
     nk::TcEpilogue ep;
     ep.C = dec->logits;
@@ -820,6 +861,12 @@ int project_sample_prep(nk_decoder *dec, const Act &a, int M, int K, const nk::T
     ep.pen_words = (N + 31) / 32;
     ep.prep_max = dec->prep_max;
     ep.prep_pinf = dec->prep_pinf;
+    ep.parts_out = &parts;
+    if (!(dec->engine & 256)) {  // small projections split along K use the workspace
+        ep.ws = dec->ksplit_ws;
+        ep.ws_floats = nk::tc_stream_k_ws_floats();
+    }
+    apply_fold(dec, fold, ep);
     ep.launches = &dec->launches;
     cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, bn, dec->stream, dec->err), "tcgen05 logits + sampling epilogue");
     dec->prof_tc = dec->prof_tc || dec->profiling;
@@ -1038,6 +1085,23 @@ void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint
 // Decoder::step over every stream (infer.rs:106-200), tokens on the device.
 // With tokens_out, the step ends in the greedy choice (sample_token with
 // greedy and no penalty); the logits are then stored only if want_logits.
+// Whether the step folds RMSNorm into the projections: every projection on
+// the tensor cores with the SwiGLU operand interleaved, widths on the
+// 32-column grid; engine bit 14 keeps the stand-alone RMSNorm kernels.
+bool fold_norms(const nk_decoder *dec) {
+    const nk_model *m = dec->model;
+    if (dec->engine & ENGINE_NO_FOLD) return false;
+    const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(), V = (int)m->cfg.vocab;
+    if (d % 32 != 0 || m->cfg.n_layer == 0) return false;
+    for (size_t i = 0; i < 4 * m->cfg.n_layer + 1; ++i)
+        if (!tc_op(const_cast<nk_model *>(m), i)) return false;
+    const nk::TcOperand *w_up = tc_op(const_cast<nk_model *>(m), 2);
+    return w_up->pair_half == H && use_tc(dec, S, 3 * E, d, tc_op(const_cast<nk_model *>(m), 0)) &&
+           use_tc(dec, S, d, E, tc_op(const_cast<nk_model *>(m), 1)) && use_tc(dec, S, 2 * H, d, w_up) &&
+           use_tc(dec, S, d, H, tc_op(const_cast<nk_model *>(m), 3)) &&
+           use_tc(dec, S, V, d, tc_op(const_cast<nk_model *>(m), 4 * m->cfg.n_layer));
+}
+
 void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint32_t *tokens_out) {
     dec->fused_parts = 0;
     if (use_small(dec)) {
@@ -1051,6 +1115,44 @@ void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint3
     const Act nrm{dec->nrm, dec->ahi, dec->alo}, gated{dec->g, dec->ahi, dec->alo};
     launch_ok(dec, nk::embed_rows(tokens, m->dp(m->emb), dec->x, S, d, V, dec->err, st), "embed");
     launch_ok(dec, nk::advance_heads(dec->heads, nullptr, S, k, st), "advance heads");
+    if (fold_norms(dec)) {
+        // RMSNorm folded into the projections: each residual projection's
+        // epilogue writes the next normalisation's operand (split of x *
+        // gain) and the rows' sums of squares, and the consuming projection
+        // scales its rows by 1 / sqrt(ms / d + eps).  Only the first layer's
+        // input norm runs as its own kernel.
+        const Act nx{nullptr, dec->nhi, dec->nlo};
+        const LayerIx &L0 = m->layers[0];
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L0.n1), m->cfg.eps, nx.out(true), S, d, st), "rmsnorm");
+        for (uint64_t l = 0; l < m->cfg.n_layer; ++l) {
+            const LayerIx &L = m->layers[l];
+            const Fold f_in{l ? dec->nss : nullptr, nullptr}, f_out{nullptr, m->dp(L.n2)}, f_up{dec->nss, nullptr},
+                f_dn{nullptr, l + 1 < m->cfg.n_layer ? m->dp(m->layers[l + 1].n1) : m->dp(m->norm_f)};
+            project(dec, true, nx, S, d, m->dp(L.in_w), tc_op(m, 4 * l + 0), 3 * E, m->dp(L.in_b), dec->u, nullptr,
+                    &f_in);
+            launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w), m->dp(L.conv_b),
+                                          gated.out(true), S, E, k, st), "ssm step");
+            project(dec, true, gated, S, E, m->dp(L.out_w), tc_op(m, 4 * l + 1), d, m->dp(L.out_b), dec->x, dec->x,
+                    &f_out);
+            const Act s_act = project_swiglu(dec, true, nx, S, d, m->dp(L.up_w), tc_op(m, 4 * l + 2), H,
+                                             m->dp(L.up_b), dec->u, gated, true, &f_up);
+            project(dec, true, s_act, S, H, m->dp(L.down_w), tc_op(m, 4 * l + 3), d, m->dp(L.down_b), dec->x, dec->x,
+                    &f_dn);
+        }
+        const nk::TcOperand *w_lg = tc_op(m, 4 * m->cfg.n_layer);
+        const Fold f_lg{dec->nss, nullptr};
+        if (want_logits || !tokens_out) {
+            if (dec->fuse_sample && !tokens_out) {
+                dec->fused_parts = project_sample_prep(dec, nx, S, d, w_lg, V, &f_lg);
+                return;
+            }
+            project(dec, true, nx, S, d, m->dp(m->emb), w_lg, V, nullptr, dec->logits, nullptr, &f_lg);
+            if (tokens_out) launch_ok(dec, nk::argmax_rows(dec->logits, tokens_out, S, V, st), "argmax");
+        } else {
+            project_argmax(dec, true, nx, S, d, m->dp(m->emb), w_lg, V, tokens_out, &f_lg);
+        }
+        return;
+    }
     for (uint64_t l = 0; l < m->cfg.n_layer; ++l) {
         const LayerIx &L = m->layers[l];
         const nk::TcOperand *w_in = tc_op(m, 4 * l + 0), *w_out = tc_op(m, 4 * l + 1), *w_up = tc_op(m, 4 * l + 2),
@@ -1784,6 +1886,9 @@ nk_status nk_decoder_create(nk_model *model, uint32_t n_streams, nk_decoder **ou
         const size_t act_w = std::max({d, E, H});
         dalloc(&dec->ahi, S * act_w, "operand hi");
         dalloc(&dec->alo, S * act_w, "operand lo");
+        dalloc(&dec->nhi, S * d, "normalised operand hi");
+        dalloc(&dec->nlo, S * d, "normalised operand lo");
+        dalloc(&dec->nss, S * ((d + 31) / 32), "row sums of squares");
         const size_t tiles = std::max<size_t>({(size_t)nk::tc_argmax_parts((int)V, 128),
                                                (size_t)nk::small_logit_tiles((int)V),
                                                (size_t)nk::persistent_partials()});
@@ -2081,8 +2186,17 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
         }
         int prep_parts = 0;  // parts of the last step's sampling epilogue (0: plain logits)
         uint32_t *tok = dec->tok_b, *spare = dec->tok_a;
-        for (uint32_t gi = 0; gi < n_new; ++gi) {
-            if (gi == 0 || !greedy_fast) {
+        int *d_col = nullptr;  // the output column collect_tokens writes next
+        dalloc(&d_col, 1, "token column");
+        std::unique_ptr<int, void (*)(int *)> own_col(d_col, [](int *p) { cudaFree(p); });
+        cuda_check(cudaMemsetAsync(d_col, 0, sizeof(int), dec->stream), "clear token column");
+        // One token of every stream: draw (except on greedy argmax steps,
+        // whose token the previous step's epilogue already chose), collect,
+        // history, then the step that produces the next logits.  `direct`
+        // launches the step's kernels without the decoder's own step graphs
+        // (inside a capture).
+        auto iteration = [&](bool draw, bool step, bool direct) {
+            if (draw) {
                 SampScope prof(dec);
                 const nk::SamplePrepared prep{dec->prep_max, dec->prep_pinf, prep_parts};
                 launch_ok(dec, nk::sample_rows(dec->logits, (int)S, V, sp, use_hist ? dec->hist : nullptr,
@@ -2091,14 +2205,14 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
                                                prep_parts ? &prep : nullptr),
                           "sample");
             }
-            cuda_check(cudaMemcpy2DAsync(d_out + gi, (size_t)n_new * sizeof(uint32_t), tok, sizeof(uint32_t),
-                                         sizeof(uint32_t), S, cudaMemcpyDeviceToDevice, dec->stream), "collect tokens");
+            launch_ok(dec, nk::collect_tokens(tok, d_out, (int)S, (int)n_new, d_col, dec->stream), "collect tokens", 2);
             if (W > 0) launch_ok(dec, nk::history_push(dec->hist, dec->hist_len, tok, (int)S, (int)W, dec->stream), "history");
-            if (gi + 1 == n_new) break;
+            if (!step) return;
             if (greedy_fast) {
-                step_device(dec, tok, false, spare);
+                if (direct) eager_step(dec, tok, false, spare);
+                else step_device(dec, tok, false, spare);
                 std::swap(tok, spare);
-                continue;
+                return;
             }
             if (!cfg->greedy && !unfused) {
                 dec->fuse_penalty = use_hist;
@@ -2108,7 +2222,7 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
                               "penalty bitmap");
                 dec->fuse_sample = &sp;
                 try {
-                    step_device(dec, tok, true, nullptr);
+                    direct ? eager_step(dec, tok, true, nullptr) : step_device(dec, tok, true, nullptr);
                 } catch (...) {
                     dec->fuse_sample = nullptr;
                     throw;
@@ -2116,7 +2230,65 @@ nk_status nk_decoder_generate(nk_decoder *dec, const uint32_t *ids, const uint32
                 dec->fuse_sample = nullptr;
                 prep_parts = dec->fused_parts;
             } else {
-                step_device(dec, tok, true, nullptr);
+                direct ? eager_step(dec, tok, true, nullptr) : step_device(dec, tok, true, nullptr);
+            }
+        };
+        // The middle iterations are identical launch sequences: from the
+        // third on they replay a CUDA graph of one iteration (two for greedy
+        // argmax steps, whose token buffers alternate), so the host launch
+        // cost of the ~30 kernels of a step is paid once.  Profiled calls run
+        // eagerly.
+        struct BodyGraph {
+            uint32_t *tok;
+            cudaGraphExec_t exec;
+            uint64_t launches;
+        };
+        struct Bodies {
+            cudaStream_t st;
+            std::vector<BodyGraph> v;
+            ~Bodies() {
+                if (v.empty()) return;
+                cudaStreamSynchronize(st);
+                for (auto &b : v) cudaGraphExecDestroy(b.exec);
+            }
+        } bodies_guard{dec->stream, {}};
+        std::vector<BodyGraph> &bodies = bodies_guard.v;
+        {
+            for (uint32_t gi = 0; gi < n_new; ++gi) {
+                const bool draw = gi == 0 || !greedy_fast, step = gi + 1 < n_new;
+                if (gi < 2 || !step || dec->profiling) {
+                    iteration(draw, step, false);
+                    continue;
+                }
+                BodyGraph *bg = nullptr;
+                for (auto &b : bodies)
+                    if (b.tok == tok) bg = &b;
+                if (!bg) {
+                    uint32_t *tok0 = tok;
+                    const uint64_t before = dec->launches;
+                    cudaGraph_t graph = nullptr;
+                    cuda_check(cudaStreamBeginCapture(dec->stream, cudaStreamCaptureModeThreadLocal),
+                               "cudaStreamBeginCapture");
+                    try {
+                        iteration(draw, step, true);
+                    } catch (...) {
+                        cudaStreamEndCapture(dec->stream, &graph);
+                        if (graph) cudaGraphDestroy(graph);
+                        cudaGetLastError();
+                        throw;
+                    }
+                    cuda_check(cudaStreamEndCapture(dec->stream, &graph), "cudaStreamEndCapture");
+                    cudaGraphExec_t exec = nullptr;
+                    cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+                    cudaGraphDestroy(graph);
+                    cuda_check(e, "cudaGraphInstantiate");
+                    bodies.push_back({tok0, exec, dec->launches - before});
+                    cuda_check(cudaGraphLaunch(exec, dec->stream), "cudaGraphLaunch");
+                    continue;
+                }
+                cuda_check(cudaGraphLaunch(bg->exec, dec->stream), "cudaGraphLaunch");
+                dec->launches += bg->launches;
+                if (greedy_fast) std::swap(tok, spare);
             }
         }
         if (n_new)
@@ -2186,7 +2358,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 16383) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 32767) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

@@ -66,6 +66,7 @@ constexpr int IPT = 4;           // elements per thread in a tile
 constexpr int TILE = ST * IPT;   // elements per tile
 constexpr int CH = 4096;         // keys sorted in shared memory at once
 constexpr int STACK = 4 * 256 + 16;
+constexpr int SEQ_CHUNK = 64;    // terms one warp adds one by one where crossings cluster
 constexpr uint32_t FULL = 0xffffffffu;
 constexpr uint32_t GRID_TOP = 1u << 24;  // s / u reaches 2^24 when s leaves its binade
 constexpr int SAT = 1 << 25;             // saturation of grid increments ("leaves the binade")
@@ -176,7 +177,7 @@ __device__ __forceinline__ Map2 map_then(Map2 A, Map2 B) {
     return r;
 }
 
-// The binade of s > 0: s = N * 2^(E - 23), N < 2^24.  Subnormals and the
+// The binade of s >= 0: s = N * 2^(E - 23), N < 2^24.  Zero, subnormals and the
 // first normal binade share the grid 2^-149 (E = -126, N = the bit pattern).
 struct Grid {
     int E;
@@ -226,39 +227,47 @@ __device__ __forceinline__ uint32_t grid_threshold(float thr, int E) {
 // j with s_{j+1} >= thr and returns j (sm.sval = s_{j+1}); else returns -1.
 // Bit-identical to the sequential loop (see the file comment).
 template <class Get>
-__device__ int seq_add_tile(const Get &get, int n, float thr, SampSmem &sm) {
+__device__ int seq_add_tile(const Get &get, int n, float thr, SampSmem &sm, bool first_tile = true) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int pos = 0;
+    // The running sum's binade crossings cluster where it is still small
+    // compared with the terms (the first few dozen terms of a sum); there one
+    // warp adds the terms one by one, every lane holding the same running sum
+    // (cheaper than a block scan per crossing), and the block scan takes over
+    // once crossings are far apart.
+    bool one_by_one = first_tile;
     for (;;) {
         __syncthreads();
         const float s = sm.sval;
         if (pos >= n) return -1;
-        if (s == 0.0f) {
-            // +0 + x == x for x >= 0: zeros leave s at zero, and the first
-            // non-zero element becomes s.  With thr <= 0 the first element
-            // already reaches it.
-            int first = pos;
-            if (thr > 0.0f) {
-                int mine = INT_MAX;
-                for (int j = pos + tid; j < n; j += ST)
-                    if (get(j) > 0.0f) {
-                        mine = j;
-                        break;
+        if (one_by_one) {
+            const int m = min(SEQ_CHUNK, n - pos);
+            if (warp == 0) {
+                float acc = s;
+                int found = INT_MAX;
+                for (int b = 0; b < m && found == INT_MAX; b += 32) {
+                    const float x = b + lane < m ? get(pos + b + lane) : 0.0f;
+                    for (int k = 0; k < 32 && b + k < m; ++k) {
+                        acc = __fadd_rn(acc, __shfl_sync(FULL, x, k));
+                        if (acc >= thr) {
+                            found = pos + b + k;
+                            break;
+                        }
                     }
-                first = block_reduce(mine, [](int x, int y) { return x < y ? x : y; }, sm.redi);
-                if (first == INT_MAX) {
-                    pos = n;
-                    continue;
+                }
+                if (lane == 0) {
+                    sm.sval = acc;
+                    sm.ev = found;
                 }
             }
-            const float s1 = get(first);
             __syncthreads();
-            if (tid == 0) sm.sval = s1;
-            if (s1 >= thr) {
+            const int f = sm.ev;
+            if (f != INT_MAX) {
                 __syncthreads();
-                return first;
+                return f;
             }
-            pos = first + 1;
+            pos += m;
+            one_by_one = false;
             continue;
         }
         const Grid g = grid_of(s);
@@ -325,6 +334,7 @@ __device__ int seq_add_tile(const Get &get, int n, float thr, SampSmem &sm) {
             __syncthreads();
             return ev;
         }
+        one_by_one = ev - pos < SEQ_CHUNK;  // crossings close together
         pos = ev + 1;
     }
 }
@@ -431,7 +441,7 @@ template <class Get>
 __device__ int nucleus_walk(const Get &get, int n, float top_p, SampSmem &sm) {
     for (int b = 0; b < n; b += TILE) {
         const int m = min(TILE, n - b);
-        const int j = seq_add_tile([&](int i) { return get(b + i); }, m, top_p, sm);
+        const int j = seq_add_tile([&](int i) { return get(b + i); }, m, top_p, sm, b == 0);
         if (j >= 0) return b + j + 1;
     }
     return -1;
@@ -580,7 +590,7 @@ __device__ void sample_one(const SampleArgs &a, int s, SampSmem &sm) {
                 logits[b + j] = e;
                 tilebuf[j] = e;
             }
-            seq_add_tile([&](int j) { return tilebuf[j]; }, n, INFINITY, sm);
+            seq_add_tile([&](int j) { return tilebuf[j]; }, n, INFINITY, sm, b == 0);
         }
         __syncthreads();
         const float sum = sm.sval;
@@ -869,6 +879,16 @@ __global__ void pen_bitmap_k(const uint32_t *__restrict__ history, const uint32_
     }
 }
 
+// out[s * n_new + *column] = tok[s]; the column counter advances in a
+// separate launch (collect_next_k) so that every thread reads the same one.
+__global__ void collect_tokens_k(const uint32_t *__restrict__ tok, uint32_t *__restrict__ out, int S, int n_new,
+                                 const int *__restrict__ column) {
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = *column;
+    if (s < S && c >= 0 && c < n_new) out[(size_t)s * n_new + c] = tok[s];
+}
+__global__ void collect_next_k(int *column) { *column += 1; }
+
 __global__ void __launch_bounds__(ST) sample_rows_k(SampleArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SampSmem &sm = *reinterpret_cast<SampSmem *>(smem_raw);
@@ -903,6 +923,15 @@ size_t sample_ws_bytes(int S, int V, SampleParams cfg, size_t budget) {
     size_t ctas = std::min<size_t>((size_t)S, (size_t)resident_ctas());
     if (budget) ctas = std::max<size_t>(1, std::min(ctas, budget / per));
     return ctas * per;
+}
+
+cudaError_t collect_tokens(const uint32_t *tok, uint32_t *out, int S, int n_new, int *column, cudaStream_t st) {
+    if (S <= 0) return cudaSuccess;
+    collect_tokens_k<<<(S + 255) / 256, 256, 0, st>>>(tok, out, S, n_new, column);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    collect_next_k<<<1, 1, 0, st>>>(column);
+    return cudaGetLastError();
 }
 
 cudaError_t sample_pen_bitmap(const uint32_t *history, const uint32_t *history_len, int history_stride,

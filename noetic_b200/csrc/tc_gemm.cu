@@ -54,6 +54,8 @@ namespace {
 // stages of 32 KiB, 256 TMEM columns each, so one CTA's epilogue overlaps the
 // other's main loop and small grids still cover every SM).
 constexpr int BM = 128, BK = 16;
+constexpr int SPLIT_MAX_M = 512;  // rows up to which small projections are split along K
+constexpr int ROWRED_COLS = 1024; // columns per partial of the split-K argmax / sampling reduction
 constexpr int SWIZZLE_BYTES = BK * 4;                       // 64
 constexpr int ATOM_BYTES = 8 * SWIZZLE_BYTES;               // 8 rows: 512
 constexpr int A_BYTES = BM * BK * 4;                       // 8 KiB
@@ -135,7 +137,32 @@ struct TcArgs {
     int splits;
     int kps;
     float *split_part;
+    // RMSNorm folded into the neighbouring projections (tensor.rs:298-312):
+    // a consumer (rs_parts != null) multiplies each accumulator row by
+    // 1 / sqrt(ms / rs_d + rs_eps), ms = the sum of rs_parts[row][0 ..
+    // rs_nparts) in order; its A operand is the split of x * gain.  A
+    // producer (store mode, nx_hi != null) also writes that operand for the
+    // next projection, nx = split(x * nx_gain) ([M, N]), and per row and
+    // 32-column chunk the sum of x^2 into nx_ss[row * nx_nparts + chunk].
+    const float *rs_parts;
+    int rs_nparts;
+    int rs_d;
+    float rs_eps;
+    float *nx_hi, *nx_lo;
+    const float *nx_gain;
+    float *nx_ss;
+    int nx_nparts;
 };
+
+// 1 / sqrt(ms / d + eps) of a row from its partial sums of squares (1 when
+// the projection's input was normalised already).
+__device__ __forceinline__ float folded_row_scale(const TcArgs &p, int row) {
+    if (!p.rs_parts || row >= p.M) return 1.0f;
+    const float *pp = p.rs_parts + (size_t)row * p.rs_nparts;
+    float ms = 0.0f;
+    for (int i = 0; i < p.rs_nparts; ++i) ms = ms + pp[i];
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ms, (float)p.rs_d), p.rs_eps)));
+}
 
 // infer.rs:239-247 then 253-256 for one logit: the repetition penalty when
 // the token is in the history window, then the temperature division.
@@ -319,7 +346,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // Kernel variants: the general projection (store / SwiGLU / argmax
 // epilogues, stream-K), the logits projection with the sampling epilogue,
 // and split-K pieces; separate instantiations keep each one's registers.
-constexpr int MODE_GENERAL = 0, MODE_PREP = 1, MODE_SPLIT = 2;
+constexpr int MODE_GENERAL = 0, MODE_PREP = 1, MODE_SPLIT = 2, MODE_FOLD = 3;
+// Variants that carry the folded RMSNorm (its row scale, and the next
+// projection's operand and sums of squares).
+constexpr bool mode_folds(int mode) { return mode == MODE_PREP || mode == MODE_FOLD; }
 
 template <int BN, int MODE = MODE_GENERAL>
 __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, int q, int lane, int m0, int n0,
@@ -353,6 +383,9 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
         }
         return;
     }
+    constexpr bool FOLD = mode_folds(MODE);
+    float rscale = 1.0f;  // this lane's row: the folded RMSNorm scale
+    if constexpr (FOLD) rscale = folded_row_scale(p, row);
     if (stg && !argmax_mode) {
         const uint64_t pol_out = policy_evict_first();
         // Transpose each 32 x 32 chunk through this warp's shared buffer
@@ -387,6 +420,13 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                             a[jj + 2] = a[jj + 2] + pa.z; a[jj + 3] = a[jj + 3] + pa.w;
                             b[jj] = b[jj] + pb.x; b[jj + 1] = b[jj + 1] + pb.y;
                             b[jj + 2] = b[jj + 2] + pb.z; b[jj + 3] = b[jj + 3] + pb.w;
+                        }
+                    }
+                    if constexpr (FOLD) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            a[jj] = a[jj] * rscale;
+                            b[jj] = b[jj] * rscale;
                         }
                     }
                     const int j = j0 + sub;
@@ -440,7 +480,7 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                     (p.pen_bits && row < p.M) ? p.pen_bits[(size_t)row * p.pen_words + (nb >> 5)] : 0u;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const float y = sample_prep(v[j] + corr[j], (pw >> j) & 1u, p);
+                    const float y = sample_prep((v[j] + corr[j]) * rscale, (pw >> j) & 1u, p);
                     v[j] = y;
                     corr[j] = 0.0f;
                     if (nb + j < p.N) {
@@ -489,15 +529,33 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                 for (int r = 0; r < 32; ++r)
                     rv[r] = (rbase + r < p.M && cok) ? p.R[(size_t)(rbase + r) * p.ldr + col] : 0.0f;
             }
+            const float gcol = (FOLD && p.nx_hi && cok) ? p.nx_gain[col] : 0.0f;
 #pragma unroll
             for (int r = 0; r < 32; ++r) {
                 const int grow = rbase + r;
                 float o = stg[r * 32 + 4 * ((lane >> 2) ^ (r & 7)) + (lane & 3)];
+                if constexpr (MODE == MODE_FOLD) {  // (the sampling epilogue scaled in the first stage)
+                    if (p.rs_parts) o = o * __shfl_sync(0xffffffffu, rscale, r);
+                }
                 if (grow < p.M && cok) {
                     if (p.bias) o = o + bcol;
                     if (p.R) o = rv[r] + o;
                     if (p.l2hints) st_stream(p.C + (size_t)grow * p.ldc + col, o, pol_out);
                     else p.C[(size_t)grow * p.ldc + col] = o;
+                }
+                if constexpr (FOLD) {
+                    if (p.nx_hi) {
+                        // The next projection's operand x * gain, and the
+                        // row's sum of squares over these 32 columns.
+                        const bool ok = grow < p.M && cok;
+                        if (ok) {
+                            const float y = o * gcol, h = tf32_round(y);
+                            st_stream(p.nx_hi + (size_t)grow * p.N + col, h, pol_out);
+                            st_stream(p.nx_lo + (size_t)grow * p.N + col, tf32_round(y - h), pol_out);
+                        }
+                        const float sq = warp_sum(ok ? o * o : 0.0f);
+                        if (lane == 0 && grow < p.M) p.nx_ss[(size_t)grow * p.nx_nparts + ((n0 + c0) >> 5)] = sq;
+                    }
                 }
             }
             __syncwarp();
@@ -521,6 +579,13 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
             tmem_ld16(ta + BN + 32 + sub, t);
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) b[jj] = b[jj] + t[jj];
+            if constexpr (FOLD) {
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) {
+                    a[jj] = a[jj] * rscale;
+                    b[jj] = b[jj] * rscale;
+                }
+            }
             if (row < p.M) {
                 const int j = j0 + sub;
                 float *out = p.C + (size_t)row * p.ldc + j;
@@ -553,6 +618,10 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
         tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = v[j] + corr[j];
+        if constexpr (FOLD) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = v[j] * rscale;
+        }
         const int nb = n0 + c0;
         if constexpr (MODE == MODE_PREP) {
             const uint32_t pw = (p.pen_bits && row < p.M) ? p.pen_bits[(size_t)row * p.pen_words + (nb >> 5)] : 0u;
@@ -575,6 +644,28 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
                     best = o;
                     best_n = (uint32_t)(nb + j);
                 }
+            }
+            continue;
+        }
+        if (FOLD && p.nx_hi) {
+            // The stored x, the next projection's operand x * gain and the
+            // row's sum of squares over these 32 columns (in column order).
+            if (row < p.M) {
+                float sq = 0.0f;
+                for (int j = 0; j < 32; ++j) {
+                    const int n = nb + j;
+                    if (n < p.N) {
+                        float o = v[j];
+                        if (p.bias) o = o + p.bias[n];
+                        if (p.R) o = p.R[(size_t)row * p.ldr + n] + o;
+                        p.C[(size_t)row * p.ldc + n] = o;
+                        const float y = o * p.nx_gain[n], h = tf32_round(y);
+                        p.nx_hi[(size_t)row * p.N + n] = h;
+                        p.nx_lo[(size_t)row * p.N + n] = tf32_round(y - h);
+                        sq = sq + o * o;
+                    }
+                }
+                p.nx_ss[(size_t)row * p.nx_nparts + (nb >> 5)] = sq;
             }
             continue;
         }
@@ -1188,16 +1279,18 @@ __global__ void split_tf32_t_k(const float *__restrict__ src, int rows, int cols
 // of the interleaved operand (output channel j: gate column 64 (j / 32) +
 // j % 32, value column 32 later), with the same f32 operations as the
 // single-piece epilogues.
-__global__ void splitk_reduce_k(const float *__restrict__ part, int splits, int M, int N, const float *bias,
-                                const float *R, int ldr, float *C, int ldc, float *C_lo, int swiglu_H) {
+__global__ void splitk_reduce_k(const float *__restrict__ part, int splits, TcArgs p) {
     pdl_trigger();
     pdl_wait();
+    const int M = p.M, N = p.N, swiglu_H = p.swiglu_H;
     const int cols = swiglu_H ? swiglu_H : N;
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long)M * cols) return;
-    const int m = (int)(i / cols), c = (int)(i - (long)m * cols);
+    const bool valid = i < (long)M * cols;
+    const int m = valid ? (int)(i / cols) : 0, c = valid ? (int)(i - (long)m * cols) : 0;
     const size_t plane = (size_t)M * N;
+    const float rscale = valid ? folded_row_scale(p, m) : 1.0f;
     if (swiglu_H) {
+        if (!valid) return;
         const int cg = 64 * (c >> 5) + (c & 31), cv = cg + 32;
         const float *pg = part + (size_t)m * N + cg, *pv = part + (size_t)m * N + cv;
         float g = pg[0], v = pv[0];
@@ -1205,22 +1298,117 @@ __global__ void splitk_reduce_k(const float *__restrict__ part, int splits, int 
             g = g + pg[sp * plane];
             v = v + pv[sp * plane];
         }
-        const float sv = silu(g + bias[c]) * (v + bias[swiglu_H + c]);
-        if (C_lo) {
+        if (p.rs_parts) {
+            g = g * rscale;
+            v = v * rscale;
+        }
+        const float sv = silu(g + p.bias[c]) * (v + p.bias[swiglu_H + c]);
+        if (p.C_lo) {
             const float h = tf32_round(sv);
-            C[(size_t)m * ldc + c] = h;
-            C_lo[(size_t)m * ldc + c] = tf32_round(sv - h);
+            p.C[(size_t)m * p.ldc + c] = h;
+            p.C_lo[(size_t)m * p.ldc + c] = tf32_round(sv - h);
         } else {
-            C[(size_t)m * ldc + c] = sv;
+            p.C[(size_t)m * p.ldc + c] = sv;
         }
         return;
     }
-    const float *pp = part + (size_t)m * N + c;
-    float o = pp[0];
-    for (int sp = 1; sp < splits; ++sp) o = o + pp[sp * plane];
-    if (bias) o = o + bias[c];
-    if (R) o = R[(size_t)m * ldr + c] + o;
-    C[(size_t)m * ldc + c] = o;
+    float o = 0.0f;
+    if (valid) {
+        const float *pp = part + (size_t)m * N + c;
+        o = pp[0];
+        for (int sp = 1; sp < splits; ++sp) o = o + pp[sp * plane];
+        if (p.rs_parts) o = o * rscale;
+        if (p.bias) o = o + p.bias[c];
+        if (p.R) o = p.R[(size_t)m * p.ldr + c] + o;
+        p.C[(size_t)m * p.ldc + c] = o;
+    }
+    if (p.nx_hi) {
+        // Folded RMSNorm producer (N % 32 == 0: a warp holds 32 consecutive
+        // columns of one row): the next operand and the chunk's sum of squares.
+        if (valid) {
+            const float y = o * p.nx_gain[c], h = tf32_round(y);
+            p.nx_hi[(size_t)m * N + c] = h;
+            p.nx_lo[(size_t)m * N + c] = tf32_round(y - h);
+        }
+        const float sq = warp_sum(valid ? o * o : 0.0f);
+        if ((threadIdx.x & 31) == 0 && valid) p.nx_ss[(size_t)m * p.nx_nparts + (c >> 5)] = sq;
+    }
+}
+
+// Split-K reduction of the argmax and sampling epilogues: block (chunk,
+// row) sums the pieces of ROWRED_COLS columns of one row in split order,
+// then either (argmax) records the first maximum of the chunk (NaN skipped)
+// or (PREP) writes pen(sum) / temperature and records the maximum of the
+// finite values and the +inf count; partial (row, chunk) goes to slot
+// row * parts + chunk, the layout the tile epilogues use.
+template <bool PREP>
+__global__ void __launch_bounds__(256) splitk_rowred_k(const float *__restrict__ part, int splits, int M, int N,
+                                                        TcArgs p, int parts) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.y, chunk = blockIdx.x;
+    const int c0 = chunk * ROWRED_COLS, c1 = min(N, c0 + ROWRED_COLS);
+    const size_t plane = (size_t)M * N;
+    const float rscale = folded_row_scale(p, row);
+    float best = -INFINITY;
+    uint32_t tag = PREP ? 0u : 0xFFFFFFFFu;  // +inf count, or the first maximum's column
+    for (int c = c0 + (int)threadIdx.x; c < c1; c += blockDim.x) {
+        const float *pp = part + (size_t)row * N + c;
+        float o = pp[0];
+        for (int sp = 1; sp < splits; ++sp) o = o + pp[sp * plane];
+        if (p.rs_parts) o = o * rscale;
+        if constexpr (PREP) {
+            const bool pen = p.pen_bits && ((p.pen_bits[(size_t)row * p.pen_words + (c >> 5)] >> (c & 31)) & 1u);
+            const float y = sample_prep(o, pen, p);
+            p.C[(size_t)row * p.ldc + c] = y;
+            if (y == INFINITY) ++tag;
+            if (isfinite(y) && y > best) best = y;
+        } else {
+            if (!isnan(o) && o > best) {  // columns ascend per thread: the first maximum stays
+                best = o;
+                tag = (uint32_t)c;
+            }
+        }
+    }
+    __shared__ float sb[8];
+    __shared__ uint32_t st[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const uint32_t ot = __shfl_xor_sync(0xffffffffu, tag, o);
+        if constexpr (PREP) {
+            best = fmaxf(best, ob);
+            tag += ot;
+        } else if (ob > best || (ob == best && ot < tag)) {
+            best = ob;
+            tag = ot;
+        }
+    }
+    if (lane == 0) {
+        sb[warp] = best;
+        st[warp] = tag;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
+            if constexpr (PREP) {
+                best = fmaxf(best, sb[w]);
+                tag += st[w];
+            } else if (sb[w] > best || (sb[w] == best && st[w] < tag)) {
+                best = sb[w];
+                tag = st[w];
+            }
+        }
+        const size_t slot = (size_t)row * parts + chunk;
+        if constexpr (PREP) {
+            p.prep_max[slot] = best;
+            p.prep_pinf[slot] = tag;
+        } else {
+            p.best_val[slot] = best;
+            p.best_idx[slot] = tag;
+        }
+    }
 }
 
 // ---- host side
@@ -1292,10 +1480,12 @@ int tc_pick_bn(int M, int N, bool allow_pair, bool stream_k) {
     const long tiles256 = (long)((N + 255) / 256) * ((M + BM - 1) / BM);
     const long pair_tiles = (long)((N + 255) / 256) * ((M + 255) / 256);
     if (allow_pair && N >= 256 && pair_tiles >= 2L * (num_sms / 2)) return TC_PAIR;
-    // One row of tiles (M <= 128, e.g. decode of 9-128 streams): the
-    // projection streams its weights with few CTAs, and 128-wide tiles give
-    // twice as many (measured 19 % faster per decode step at 64 streams).
+    // One row of tiles (M <= 128, e.g. decode of 9-128 streams), or a small
+    // projection of at most SPLIT_MAX_M rows whose 128-wide tiles fill under
+    // half of the CTA slots: 128-wide tiles, split along K over the SMs by
+    // tc_gemm (every epilogue mode).
     if (N < 256 || M <= BM) return 128;
+    if (M <= SPLIT_MAX_M && (long)((N + 127) / 128) * ((M + BM - 1) / BM) <= num_sms) return 128;
     if (stream_k) return 256;
     const double e256 =
         (double)tiles256 / ((double)((tiles256 + num_sms - 1) / num_sms) * num_sms);
@@ -1472,7 +1662,14 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     TcArgs a{ep.C, ep.ldc, M, W.N, K, ep.bias, ep.R, ep.ldr, ep.best_val, ep.best_idx, tc_argmax_parts(W.N, bn), err,
               ep.swiglu ? W.pair_half : 0, ep.C_lo, 0, 0, ep.ws, ep.flags, ep.l2hints ? 1 : 0,
               prep ? ep.temperature : 0.0f, ep.rep_penalty, ep.pen_bits, ep.pen_words, ep.prep_max, ep.prep_pinf,
-              ep.handoff_wait_ns ? ep.handoff_wait_ns : WAIT_NS, ep.withhold_publish ? 1 : 0, 0, 0, nullptr};
+              ep.handoff_wait_ns ? ep.handoff_wait_ns : WAIT_NS, ep.withhold_publish ? 1 : 0, 0, 0, nullptr,
+              ep.rs_parts, ep.rs_nparts, ep.rs_d, ep.rs_eps, ep.nx_hi, ep.nx_lo, ep.nx_gain, ep.nx_ss,
+              (W.N + 31) / 32};
+    const bool fold = ep.rs_parts || ep.nx_hi;
+    if (fold && (bn == TC_PAIR || (ep.rs_parts && (ep.rs_nparts <= 0 || ep.rs_d <= 0)) ||
+                 (ep.nx_hi && (!ep.nx_lo || !ep.nx_gain || !ep.nx_ss || ep.swiglu || ep.best_val || prep ||
+                               W.N % 32 != 0))))
+        return cudaErrorInvalidValue;
     if (a.ws) {
         // Stream-K needs one partial slot and one counter per SM.
         const int sms = sm_count_cached();
@@ -1485,9 +1682,9 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
     // that every SM streams its share of the weights (the regime of 9-128
     // streams, where the projection is bound by the weight stream).
     int splits = 0, kps = 0;
-    if (bn == 128 && ep.ws && M <= BM && !ep.best_val && !prep) {
+    if (bn == 128 && ep.ws && M <= SPLIT_MAX_M) {
         const long slots = 2L * sm_count_cached();
-        const long tiles = tc_tiles_n(W.N, 128);
+        const long tiles = (long)tc_tiles_n(W.N, 128) * ((M + BM - 1) / BM);
         const int kblocks = (K + BK - 1) / BK;
         if (tiles * 2 <= slots && kblocks >= 4) {
             splits = (int)std::min<long>(kblocks / 2, std::max<long>(2, slots / tiles));
@@ -1501,21 +1698,38 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
         }
     }
     if (ep.launches) *ep.launches += splits ? 2 : 1;
+    if (ep.parts_out) *ep.parts_out = splits ? (W.N + ROWRED_COLS - 1) / ROWRED_COLS : tc_argmax_parts(W.N, bn);
     if (bn == TC_PAIR) return launch_pair(mAh, mAl, W, a, M, st);
     if (splits) {
         a.splits = splits;
         a.kps = kps;
         a.split_part = ep.ws;
+        a.best_val = nullptr;  // the pieces write raw sums; the reduction applies the epilogue
+        a.temperature = 0.0f;
         cudaError_t e = launch_tc<128, MODE_SPLIT>(mAh, mAl, W, a, M, st);
         if (e != cudaSuccess) return e;
+        if (ep.best_val || prep) {
+            TcArgs r = a;
+            r.best_val = ep.best_val;
+            r.best_idx = ep.best_idx;
+            r.temperature = prep ? ep.temperature : 0.0f;
+            const int parts = (W.N + ROWRED_COLS - 1) / ROWRED_COLS;
+            const dim3 grid((unsigned)parts, (unsigned)M);
+            return prep ? pdl_launch(splitk_rowred_k<true>, grid, dim3(256), 0, st, (const float *)ep.ws, splits, M,
+                                     W.N, r, parts)
+                        : pdl_launch(splitk_rowred_k<false>, grid, dim3(256), 0, st, (const float *)ep.ws, splits, M,
+                                     W.N, r, parts);
+        }
         const long outs = (long)M * (ep.swiglu ? W.pair_half : W.N);
         return pdl_launch(splitk_reduce_k, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st,
-                          (const float *)ep.ws, splits, M, W.N, ep.bias, ep.R, ep.ldr, ep.C, ep.ldc, ep.C_lo,
-                          ep.swiglu ? W.pair_half : 0);
+                          (const float *)ep.ws, splits, a);
     }
     if (prep)
         return bn == 256 ? launch_tc<256, MODE_PREP>(mAh, mAl, W, a, M, st)
                          : launch_tc<128, MODE_PREP>(mAh, mAl, W, a, M, st);
+    if (fold)
+        return bn == 256 ? launch_tc<256, MODE_FOLD>(mAh, mAl, W, a, M, st)
+                         : launch_tc<128, MODE_FOLD>(mAh, mAl, W, a, M, st);
     return bn == 256 ? launch_tc<256, MODE_GENERAL>(mAh, mAl, W, a, M, st)
                      : launch_tc<128, MODE_GENERAL>(mAh, mAl, W, a, M, st);
 }

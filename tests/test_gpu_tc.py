@@ -267,3 +267,32 @@ def test_long_prompt_model_widths_at_serving_batches(gpu, orc, S):
     toks = ids[:, -1].copy()
     ga, gb = tc.step_greedy(toks).copy(), f32.step_greedy(toks).copy()
     assert (ga == gb).mean() > 0.95
+
+
+@pytest.mark.parametrize("S", [64, 384, 2048])
+def test_folded_rmsnorm_matches_standalone_norms(gpu, orc, S):
+    """RMSNorm folded into the projections (the default tensor-core step)
+    against the stand-alone RMSNorm kernels (engine bit 14) and the oracle, at
+    split-K (64, 384 streams) and stream-K (2048) tilings, greedy steps
+    included."""
+    kw = dict(vocab=2048, d_model=512, n_layer=3, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=21)
+    T = 3
+    ids = _ids(S, T, kw["vocab"], 900)
+    fold, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    plain.set_engine(16384)
+    for t in range(T):
+        a = fold.step(ids[:, t]).copy()
+        b = plain.step(ids[:, t])
+        assert np.abs(a - b).max() <= 1e-4, t
+    sa, _ = fold.get_state()
+    sb, _ = plain.get_state()
+    assert state_rel_err(sa, sb) <= 1e-5
+    for s in [0, S - 1]:
+        od = orc.Decoder(om)
+        for t in range(T):
+            ref = od.step(ids[s, t])
+        assert np.abs(a[s] - ref).max() <= 1e-3, s
+    toks = ids[:, -1].copy()
+    ga, gb = fold.step_greedy(toks).copy(), plain.step_greedy(toks).copy()
+    assert (ga == gb).mean() > 0.95
