@@ -229,6 +229,10 @@ def run_reference(args, rank):
         "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_cpu_baseline:
+        # Context only (not the reference's design): every host core decoding
+        # its own stream at once.
+        line["cpu_baseline"]["stream_parallel"] = cpu_stream_parallel_rate()
     print(json.dumps(line), flush=True)
 
 

@@ -697,7 +697,11 @@ struct SampScope {
 // recovery) runs without a fault and without a hang.
 constexpr int ENGINE_WITHHOLD_PUBLISH = 4096;
 constexpr int ENGINE_WITHHOLD_ARRIVAL = 8192;
-constexpr int ENGINE_NO_FOLD = 16384;  // stand-alone RMSNorm kernels instead of the folded form
+// RMSNorm folded into the projection epilogues (opt-in): measured slower on
+// B200 (77 vs 70 ms per step at 16384 streams, 12.7 vs 10.9 at 2048), since
+// the 256-wide tile's epilogue is not overlapped with the next tile's main
+// loop and the extra stores lengthen it by more than the norm kernels cost.
+constexpr int ENGINE_FOLD = 16384;
 constexpr uint64_t TEST_WAIT_NS = 2000000ull;
 void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
     if (dec->engine & ENGINE_WITHHOLD_PUBLISH) {
@@ -997,9 +1001,17 @@ nk::SmallStepArgs small_args(nk_decoder *dec, const uint32_t *tokens, uint32_t *
     return a;
 }
 
+// The persistent step kernel for 1-4 streams when the weights are large
+// (each of its 2L + 1 grid-wide phases costs a few microseconds of
+// synchronisation, repaid when every phase streams megabytes of weights);
+// models of under PERSISTENT_MIN_BYTES of weights (L2-resident, e.g. the
+// d192 / 3-layer model: 33 us per token against 56 us) take the fused
+// small-batch kernels.  Engine bit 6 forces the persistent kernel.
+constexpr size_t PERSISTENT_MIN_BYTES = (size_t)96 << 20;
 bool use_persistent(const nk_decoder *dec) {
     const nk_model *m = dec->model;
-    return !(dec->engine & 1024) && !(dec->engine & 8) &&
+    const bool big = m->arena_floats * sizeof(float) >= PERSISTENT_MIN_BYTES;
+    return !(dec->engine & 1024) && !(dec->engine & 8) && (big || (dec->engine & 64)) &&
            nk::persistent_step_supported((int)dec->S, (int)m->d(), (int)m->e(), (int)m->hidden(), (int)m->k(),
                                          (int)m->cfg.vocab, (int)m->cfg.n_layer);
 }
@@ -1085,12 +1097,12 @@ void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint
 // Decoder::step over every stream (infer.rs:106-200), tokens on the device.
 // With tokens_out, the step ends in the greedy choice (sample_token with
 // greedy and no penalty); the logits are then stored only if want_logits.
-// Whether the step folds RMSNorm into the projections: every projection on
-// the tensor cores with the SwiGLU operand interleaved, widths on the
-// 32-column grid; engine bit 14 keeps the stand-alone RMSNorm kernels.
+// Whether the step folds RMSNorm into the projections (engine bit 14):
+// every projection on the tensor cores with the SwiGLU operand interleaved,
+// widths on the 32-column grid.
 bool fold_norms(const nk_decoder *dec) {
     const nk_model *m = dec->model;
-    if (dec->engine & ENGINE_NO_FOLD) return false;
+    if (!(dec->engine & ENGINE_FOLD) || (dec->engine & 128)) return false;  // (no folded CTA-pair epilogue)
     const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(), V = (int)m->cfg.vocab;
     if (d % 32 != 0 || m->cfg.n_layer == 0) return false;
     for (size_t i = 0; i < 4 * m->cfg.n_layer + 1; ++i)

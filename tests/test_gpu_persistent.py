@@ -1,4 +1,5 @@
-"""The single persistent decode-step kernel (the default for 1..4 streams:
+"""The single persistent decode-step kernel (the default for 1..4 streams of
+models with 96 MiB of weights or more, forced here by engine bit 6:
 weights streamed through a shared-memory ring, two grid barriers per layer,
 a fixed-point residual accumulator) against the oracle and against the
 multi-kernel small-batch step (engine bit 10)."""
@@ -10,7 +11,7 @@ from conftest import c1_cfg, same_model, state_rel_err, tiny_cfg
 
 pytestmark = pytest.mark.gpu
 
-PERSISTENT = 64  # engine bit: the whole step as one persistent kernel (default)
+PERSISTENT = 64  # engine bit: the whole step as one persistent kernel
 MULTI = 1024  # engine bit: no persistent kernel
 
 
