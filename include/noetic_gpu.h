@@ -239,7 +239,9 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * gain-scaled operand and the rows' sums of squares, and the consumer scales
  * its rows by the RMSNorm factor) instead of the stand-alone kernels; 47
  * fewer launches per step, but measured slower on B200 because the longer
- * epilogue is not overlapped with the main loop. */
+ * epilogue is not overlapped with the main loop.
+ * Bit 15: the 256-wide projection epilogues store from the threads through
+ * a transposing buffer instead of the default bulk tensor stores. */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

@@ -102,6 +102,9 @@ struct TcEpilogue {
     float *nx_hi = nullptr, *nx_lo = nullptr;
     const float *nx_gain = nullptr;
     float *nx_ss = nullptr;
+    // 256-wide store / SwiGLU / sampling epilogues write through bulk tensor
+    // stores (C 16-byte aligned, ldc a multiple of 4) unless this is set.
+    bool no_tma_store = false;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.

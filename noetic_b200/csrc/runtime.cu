@@ -695,6 +695,7 @@ struct SampScope {
 // skips its first grid-barrier arrival, and the waits are bounded at 2 ms,
 // so the failure path (an expired wait reported as an error code, then
 // recovery) runs without a fault and without a hang.
+constexpr int ENGINE_NO_TMA_STORE = 32768;  // epilogue stores from the threads instead of bulk stores
 constexpr int ENGINE_WITHHOLD_PUBLISH = 4096;
 constexpr int ENGINE_WITHHOLD_ARRIVAL = 8192;
 // RMSNorm folded into the projection epilogues (opt-in): measured slower on
@@ -704,6 +705,7 @@ constexpr int ENGINE_WITHHOLD_ARRIVAL = 8192;
 constexpr int ENGINE_FOLD = 16384;
 constexpr uint64_t TEST_WAIT_NS = 2000000ull;
 void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
+    if (dec->engine & ENGINE_NO_TMA_STORE) ep.no_tma_store = true;
     if (dec->engine & ENGINE_WITHHOLD_PUBLISH) {
         ep.withhold_publish = true;
         ep.handoff_wait_ns = TEST_WAIT_NS;
@@ -871,6 +873,7 @@ int project_sample_prep(nk_decoder *dec, const Act &a, int M, int K, const nk::T
         ep.ws_floats = nk::tc_stream_k_ws_floats();
     }
     apply_fold(dec, fold, ep);
+    test_controls(dec, ep);
     ep.launches = &dec->launches;
     cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, bn, dec->stream, dec->err), "tcgen05 logits + sampling epilogue");
     dec->prof_tc = dec->prof_tc || dec->profiling;
@@ -2370,7 +2373,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 32767) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 65535) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

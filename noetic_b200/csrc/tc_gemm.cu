@@ -152,6 +152,10 @@ struct TcArgs {
     const float *nx_gain;
     float *nx_ss;
     int nx_nparts;
+    // 1: the 256-wide store and SwiGLU epilogues write each 32 x 32 chunk
+    // with a TMA bulk store from the warp's staging buffer (mapC / mapClo),
+    // so the stores drain while the next tile's MMAs run.
+    int tma_store;
 };
 
 // 1 / sqrt(ms / d + eps) of a row from its partial sums of squares (1 when
@@ -287,6 +291,22 @@ __device__ __forceinline__ void st_stream(float *p, float v, uint64_t pol) {
     asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
 }
 
+// Bulk tensor store of a 32 x 32 f32 box (128-byte swizzle, the staging
+// buffer's layout) at column x (a multiple of 32: 16-byte aligned) and row y
+// (>= 0); rows and columns past the tensor are not written.
+__device__ __forceinline__ void tma_store_box(const CUtensorMap *map, uint32_t src, int x, int y, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;"
+        ::"l"((uint64_t)map), "r"(src), "r"(x), "r"(y), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until this thread's bulk stores have read their shared-memory source.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until this thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // K-major operand with the 64-byte swizzle (layout type 4): rows of 64 bytes,
 // 8-row groups ATOM_BYTES apart.
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
@@ -346,7 +366,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 // Kernel variants: the general projection (store / SwiGLU / argmax
 // epilogues, stream-K), the logits projection with the sampling epilogue,
 // and split-K pieces; separate instantiations keep each one's registers.
-constexpr int MODE_GENERAL = 0, MODE_PREP = 1, MODE_SPLIT = 2, MODE_FOLD = 3;
+constexpr int MODE_GENERAL = 0, MODE_PREP = 1, MODE_SPLIT = 2, MODE_FOLD = 3, MODE_TMA = 4;
+// MODE_TMA: the general projection whose 256-wide store and SwiGLU
+// epilogues write through bulk tensor stores (stream-K partial tiles still
+// take the staged transposed writes).
 // Variants that carry the folded RMSNorm (its row scale, and the next
 // projection's operand and sums of squares).
 constexpr bool mode_folds(int mode) { return mode == MODE_PREP || mode == MODE_FOLD; }
@@ -355,7 +378,8 @@ template <int BN, int MODE = MODE_GENERAL>
 __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, int q, int lane, int m0, int n0,
                                               int c_begin, int c_end, bool argmax_mode, bool vec, float &best,
                                               uint32_t &best_n, float *stg, const float *parts = nullptr,
-                                              int nparts = 0, float *part_out = nullptr, int split = -1) {
+                                              int nparts = 0, float *part_out = nullptr, int split = -1,
+                                              const CUtensorMap *mapC = nullptr, const CUtensorMap *mapClo = nullptr) {
     const int row = m0 + q * 32 + lane;
     if constexpr (MODE == MODE_SPLIT) {
         // Split-K piece: the raw sum of both accumulator chains, rows < M.
@@ -386,13 +410,168 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
     constexpr bool FOLD = mode_folds(MODE);
     float rscale = 1.0f;  // this lane's row: the folded RMSNorm scale
     if constexpr (FOLD) rscale = folded_row_scale(p, row);
+    if ((MODE == MODE_TMA || MODE == MODE_PREP) && stg && !argmax_mode && p.tma_store && !part_out) {
+        // Each 32 x 32 chunk is finished in registers (lane = row: both
+        // accumulator chains, then the stream-K partials in order, the bias,
+        // the residual, or the SwiGLU) and written by one bulk tensor store
+        // from this warp's staging buffer, whose float4 slots are XOR-swizzled
+        // by row exactly as the 128-byte TMA swizzle lays out a 32-float box.
+        // The warp waits only until the previous store has read the buffer.
+        const uint64_t pol_out = policy_evict_first();
+        const int rbase = m0 + q * 32;
+        const uint32_t stg_s = smem_u32(stg);
+        auto stage_row = [&](const float (&o)[32]) {
+            if (lane == 0) bulk_wait_read();
+            __syncwarp();
+#pragma unroll
+            for (int c4 = 0; c4 < 8; ++c4)
+                *reinterpret_cast<float4 *>(stg + lane * 32 + 4 * (c4 ^ (lane & 7))) =
+                    make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+            fence_async_smem();
+            __syncwarp();
+        };
+        if (p.swiglu_H) {
+            for (int c0 = c_begin; c0 < c_end; c0 += 64) {
+                if (n0 + c0 >= p.N) break;  // warp-uniform
+                const int j0 = (n0 + c0) >> 1;
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0;
+                float sv[32];
+#pragma unroll
+                for (int sub = 0; sub < 32; sub += 16) {
+                    float a[16], b[16], t[16];
+                    tmem_ld16(ta + sub, a);
+                    tmem_ld16(ta + BN + sub, t);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) a[jj] = a[jj] + t[jj];
+                    tmem_ld16(ta + 32 + sub, b);
+                    tmem_ld16(ta + BN + 32 + sub, t);
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj) b[jj] = b[jj] + t[jj];
+                    for (int ks = 0; ks < nparts; ++ks) {
+                        const float *pt = parts + (size_t)ks * BM * BN + (size_t)(q * 32 + lane) * BN + c0 + sub;
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj += 4) {
+                            const float4 pa = *reinterpret_cast<const float4 *>(pt + jj);
+                            const float4 pb = *reinterpret_cast<const float4 *>(pt + 32 + jj);
+                            a[jj] = a[jj] + pa.x; a[jj + 1] = a[jj + 1] + pa.y;
+                            a[jj + 2] = a[jj + 2] + pa.z; a[jj + 3] = a[jj + 3] + pa.w;
+                            b[jj] = b[jj] + pb.x; b[jj + 1] = b[jj + 1] + pb.y;
+                            b[jj + 2] = b[jj + 2] + pb.z; b[jj + 3] = b[jj + 3] + pb.w;
+                        }
+                    }
+                    if constexpr (FOLD) {
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj) {
+                            a[jj] = a[jj] * rscale;
+                            b[jj] = b[jj] * rscale;
+                        }
+                    }
+                    const int j = j0 + sub;
+#pragma unroll
+                    for (int jj = 0; jj < 16; ++jj)
+                        sv[sub + jj] = silu(a[jj] + p.bias[j + jj]) * (b[jj] + p.bias[p.swiglu_H + j + jj]);
+                }
+                if (p.C_lo) {
+                    float hv[32];
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) {
+                        hv[jj] = tf32_round(sv[jj]);
+                        sv[jj] = tf32_round(sv[jj] - hv[jj]);
+                    }
+                    stage_row(hv);
+                    if (lane == 0) {
+                        tma_store_box(mapC, stg_s, j0, rbase, pol_out);
+                        bulk_commit();
+                    }
+                    stage_row(sv);
+                    if (lane == 0) {
+                        tma_store_box(mapClo, stg_s, j0, rbase, pol_out);
+                        bulk_commit();
+                    }
+                } else {
+                    stage_row(sv);
+                    if (lane == 0) {
+                        tma_store_box(mapC, stg_s, j0, rbase, pol_out);
+                        bulk_commit();
+                    }
+                }
+            }
+            return;
+        }
+        for (int c0 = c_begin; c0 < c_end; c0 += 32) {
+            if (n0 + c0 >= p.N) break;  // warp-uniform
+            const int nb = n0 + c0;
+            float v[32], corr[32];
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+            tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN + c0), corr);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = v[j] + corr[j];
+            if constexpr (MODE == MODE_PREP) {
+                const uint32_t pw =
+                    (p.pen_bits && row < p.M) ? p.pen_bits[(size_t)row * p.pen_words + (nb >> 5)] : 0u;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float y = sample_prep(v[j] * rscale, (pw >> j) & 1u, p);
+                    v[j] = y;
+                    if (nb + j < p.N) {
+                        if (y == INFINITY) ++best_n;
+                        if (isfinite(y) && y > best) best = y;
+                    }
+                }
+            } else {
+                for (int ks = 0; ks < nparts; ++ks) {
+                    const float *pt = parts + (size_t)ks * BM * BN + (size_t)(q * 32 + lane) * BN + c0;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 pv = *reinterpret_cast<const float4 *>(pt + j);
+                        v[j] = v[j] + pv.x;
+                        v[j + 1] = v[j + 1] + pv.y;
+                        v[j + 2] = v[j + 2] + pv.z;
+                        v[j + 3] = v[j + 3] + pv.w;
+                    }
+                }
+                if constexpr (FOLD) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = v[j] * rscale;
+                }
+                if (p.bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (nb + j < p.N) v[j] = v[j] + p.bias[nb + j];
+                }
+                if (p.R && row < p.M) {
+                    const float *rr = p.R + (size_t)row * p.ldr + nb;
+                    if (vec && nb + 32 <= p.N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            const float4 r4 = *reinterpret_cast<const float4 *>(rr + j);
+                            v[j] = r4.x + v[j];
+                            v[j + 1] = r4.y + v[j + 1];
+                            v[j + 2] = r4.z + v[j + 2];
+                            v[j + 3] = r4.w + v[j + 3];
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (nb + j < p.N) v[j] = rr[j] + v[j];
+                    }
+                }
+            }
+            stage_row(v);
+            if (lane == 0) {
+                tma_store_box(mapC, stg_s, nb, rbase, pol_out);
+                bulk_commit();
+            }
+        }
+        return;
+    }
     if (stg && !argmax_mode) {
         const uint64_t pol_out = policy_evict_first();
         // Transpose each 32 x 32 chunk through this warp's shared buffer
         // (float4 slots XOR-swizzled by row: conflict-free both ways), then
         // lane = column, so every load and store is one 128-byte row segment.
         const int rbase = m0 + q * 32;
-        if (p.swiglu_H && !part_out) {
+        if (MODE != MODE_TMA && p.swiglu_H && !part_out) {
             // 64-column blocks: 32 gate columns, then the 32 value columns of
             // the same channels; both accumulator chains summed first.
             for (int c0 = c_begin; c0 < c_end; c0 += 64) {
@@ -501,7 +680,7 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
             __syncwarp();
             const int col = n0 + c0 + lane;
             const bool cok = col < p.N;
-            if (part_out) {
+            if (MODE == MODE_TMA || part_out) {  // (MODE_TMA reaches here only for partial tiles)
 #pragma unroll 8
                 for (int r = 0; r < 32; ++r)
                     part_out[(size_t)(q * 32 + r) * BN + c0 + lane] = stg[r * 32 + 4 * ((lane >> 2) ^ (r & 7)) + (lane & 3)];
@@ -706,7 +885,8 @@ __device__ __forceinline__ void epilogue_cols(const TcArgs &p, uint32_t tmem, in
 template <int BN, int MODE>
 __global__ void __launch_bounds__(THREADS, Tile<BN>::CTAS_PER_SM)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
-               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl, TcArgs p) {
+               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
+               const __grid_constant__ CUtensorMap mapC, const __grid_constant__ CUtensorMap mapClo, TcArgs p) {
     using T = Tile<BN>;
     constexpr int STAGES = T::STAGES, STAGE_BYTES = T::STAGE_BYTES, B_BYTES = T::B_BYTES;
     constexpr uint32_t TMEM_COLS = T::TMEM_COLS, IDESC = T::IDESC;
@@ -922,7 +1102,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             float *stg =
                 BN == 256 ? reinterpret_cast<float *>(smem + STAGES * STAGE_BYTES) + (warp - 4) * 1024 : nullptr;
             epilogue_cols<BN, MODE>(p, tmem, q, lane, m0, n0, half * COLS, (half + 1) * COLS, argmax_mode, vec, best, best_n,
-                              stg, parts, pc.np > 0 ? pc.np : 0, part_out, pc.split);
+                              stg, parts, pc.np > 0 ? pc.np : 0, part_out, pc.split, &mapC, &mapClo);
             // TMEM of this piece fully read: hand the accumulators back.
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
@@ -963,6 +1143,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 p.prep_pinf[slot] = best_n;
             }
         }
+        // Every bulk store this warp issued has completed before the CTA
+        // exits (its staging buffer stays valid, and the next kernel's reads
+        // see the outputs).
+        if (BN == 256 && p.tma_store && lane == 0) bulk_wait_all();
+        __syncwarp();
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -1427,6 +1612,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // 2-D f32 map over [rows, cols] (cols contiguous), box {BK, box_rows}, 64B
 // swizzle, zero fill outside the tensor.
+// 2-D f32 map over [rows, cols] with row stride ld floats, box {32, 32},
+// 128-byte swizzle: the epilogue's bulk stores.
+bool make_store_map(CUtensorMap *map, const float *base, int rows, int cols, int ld) {
+    auto fn = encode_fn();
+    if (!fn || ld % 4 != 0 || ((uintptr_t)base & 15) != 0) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * sizeof(float)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 bool make_map(CUtensorMap *map, const float *base, int rows, int cols, int box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
@@ -1570,7 +1770,7 @@ void tc_weights_free(TcWeights &w) {
 
 template <int BN, int MODE>
 cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, TcArgs a, int M,
-                      cudaStream_t st) {
+                      cudaStream_t st, const CUtensorMap *mC = nullptr, const CUtensorMap *mClo = nullptr) {
     static thread_local int attr_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1611,8 +1811,12 @@ cudaError_t launch_tc(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOp
         a.sk_t0 = (int)dp;
         grid = (unsigned)(dp > 0 ? slots : ctas);
     }
+    // Unused maps are passed as copies of an operand map (never read).
+    if (BN != 256 || !mC) a.tma_store = 0;
+    const CUtensorMap &oc = a.tma_store ? *mC : mAh;
+    const CUtensorMap &ocl = a.tma_store && mClo ? *mClo : oc;
     return pdl_launch(tc_gemm_kernel<BN, MODE>, dim3(grid), dim3(THREADS), Tile<BN>::SMEM_BYTES, st, mAh, mAl,
-                      *(const CUtensorMap *)mh, *(const CUtensorMap *)ml, a);
+                      *(const CUtensorMap *)mh, *(const CUtensorMap *)ml, oc, ocl, a);
 }
 
 cudaError_t launch_pair(const CUtensorMap &mAh, const CUtensorMap &mAl, const TcOperand &W, TcArgs a, int M,
@@ -1664,7 +1868,7 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
               prep ? ep.temperature : 0.0f, ep.rep_penalty, ep.pen_bits, ep.pen_words, ep.prep_max, ep.prep_pinf,
               ep.handoff_wait_ns ? ep.handoff_wait_ns : WAIT_NS, ep.withhold_publish ? 1 : 0, 0, 0, nullptr,
               ep.rs_parts, ep.rs_nparts, ep.rs_d, ep.rs_eps, ep.nx_hi, ep.nx_lo, ep.nx_gain, ep.nx_ss,
-              (W.N + 31) / 32};
+              (W.N + 31) / 32, 0};
     const bool fold = ep.rs_parts || ep.nx_hi;
     if (fold && (bn == TC_PAIR || (ep.rs_parts && (ep.rs_nparts <= 0 || ep.rs_d <= 0)) ||
                  (ep.nx_hi && (!ep.nx_lo || !ep.nx_gain || !ep.nx_ss || ep.swiglu || ep.best_val || prep ||
@@ -1724,12 +1928,28 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
         return pdl_launch(splitk_reduce_k, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st,
                           (const float *)ep.ws, splits, a);
     }
+    // Bulk-store epilogue for 256-wide tiles (store, SwiGLU and sampling
+    // modes): the output as a tensor of [M, cols] with row stride ldc.
+    alignas(64) CUtensorMap mC, mClo;
+    const CUtensorMap *pC = nullptr, *pClo = nullptr;
+    if (bn == 256 && !ep.no_tma_store && ep.C && !ep.best_val && !(ep.nx_hi)) {
+        const int cols = ep.swiglu ? W.pair_half : W.N;
+        if (make_store_map(&mC, ep.C, M, cols, ep.ldc) &&
+            (!ep.C_lo || make_store_map(&mClo, ep.C_lo, M, cols, ep.ldc))) {
+            pC = &mC;
+            pClo = ep.C_lo ? &mClo : nullptr;
+            a.tma_store = 1;
+        }
+    }
     if (prep)
-        return bn == 256 ? launch_tc<256, MODE_PREP>(mAh, mAl, W, a, M, st)
+        return bn == 256 ? launch_tc<256, MODE_PREP>(mAh, mAl, W, a, M, st, pC, pClo)
                          : launch_tc<128, MODE_PREP>(mAh, mAl, W, a, M, st);
-    if (fold)
+    if (fold) {
+        a.tma_store = 0;
         return bn == 256 ? launch_tc<256, MODE_FOLD>(mAh, mAl, W, a, M, st)
                          : launch_tc<128, MODE_FOLD>(mAh, mAl, W, a, M, st);
+    }
+    if (bn == 256 && a.tma_store) return launch_tc<256, MODE_TMA>(mAh, mAl, W, a, M, st, pC, pClo);
     return bn == 256 ? launch_tc<256, MODE_GENERAL>(mAh, mAl, W, a, M, st)
                      : launch_tc<128, MODE_GENERAL>(mAh, mAl, W, a, M, st);
 }
