@@ -268,8 +268,8 @@ nk_status nk_decoder_profile_end(nk_decoder *dec, nk_profile *out);
 
 /* scan_adjoint (scan.rs:227-260), the reverse-mode gradient of the
  * recurrence: c_t = g_t + a_{t+1} c_{t+1} with c_T = 0, over [batch, t, d]
- * host arrays (layout (b*t + i)*d + j); chunked = 1 uses the three-pass
- * time-parallel form (equal to the sequential one within f32 rounding).
+ * host arrays (layout (b*t + i)*d + j); chunked = 1 uses the time-parallel
+ * form of nk_scan_device (equal to the sequential one within f32 rounding).
  * The _device form takes device pointers and a CUDA stream.
  * batch * t * d <= 2^37, else NK_ERR_INVALID. */
 nk_status nk_scan_adjoint(const float *a, const float *g, float *c, uint64_t batch, uint64_t t, uint64_t d,
@@ -351,13 +351,17 @@ nk_status nk_adamw_step_device(float *val, const float *grad, float *m, float *v
 /* scan_sequential / scan_chunked (scan.rs:35-57, 98-225):
  * h[b,t,j] = a[b,t,j] * h[b,t-1,j] + b[b,t,j], h[b,-1,j] = 0, layout
  * (b*T + t)*D + j.  Host pointers; runs on `device`.  chunked != 0 selects
- * the time-chunked associative scan.  batch * t * d <= 2^37 (checked
- * without wrap-around), else NK_ERR_INVALID. */
+ * the time-chunked associative scan: for d >= 16 one kernel that passes the
+ * state between time blocks of 128 steps by decoupled look-back (each
+ * element read and written once), else the three-pass form.  batch * t * d
+ * <= 2^37 (checked without wrap-around), else NK_ERR_INVALID. */
 nk_status nk_scan(const float *a, const float *b, float *h, uint64_t batch, uint64_t t,
                   uint64_t d, int chunked, int device);
 
-/* Same on device pointers, asynchronous on `stream` (cudaStream_t, may be
- * NULL for the legacy default stream). */
+/* Same on device pointers, on `stream` (cudaStream_t, may be NULL for the
+ * legacy default stream): asynchronous for chunked = 0; chunked != 0 waits
+ * for the stream, and returns NK_ERR_DEVICE (code 131) if a time block's
+ * look-back wait expired (bounded at 1 s). */
 nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t,
                          uint64_t d, int chunked, void *stream);
 
@@ -366,9 +370,10 @@ nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batc
  * middle of their work: a host whose own pool allocator owns the whole
  * device memory budget (a stray cudaMalloc there can fail or fragment the
  * pool), or a latency-critical loop that cannot afford the device-wide
- * synchronisation cudaMalloc / cudaFree may cause.  It computes what
- * nk_scan_device(..., chunked = 1, ...) computes, on device pointers,
- * asynchronously on `stream`, but its scratch is a fixed array of
+ * synchronisation cudaMalloc / cudaFree may cause.  It computes the
+ * three-pass time-chunked scan (equal to nk_scan_device(..., chunked = 1,
+ * ...) within f32 rounding), on device pointers, asynchronously on
+ * `stream`, but its scratch is a fixed array of
  * NK_SCAN_NOALLOC_SCRATCH_FLOATS floats (12 MiB) inside the library's device
  * image, which every GPU that loads the library holds until the process
  * exits.  Limit: batch * ceil(t / NK_SCAN_TIME_BLOCK) * d <= 1048576

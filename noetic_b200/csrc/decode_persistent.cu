@@ -53,6 +53,10 @@
 #include "nk_common.cuh"
 #include "nk_kernels.h"
 
+#ifndef ACC_REPLICAS
+#define ACC_REPLICAS 4
+#endif
+
 namespace nk {
 
 namespace {
@@ -69,6 +73,7 @@ constexpr int MAXR = 4;                      // streams
 constexpr int MAXD = 2048;                   // model width
 constexpr double FX_ONE = 4294967296.0;      // fixed-point scale 2^32
 constexpr int PACE_CHUNKS = 2;               // weight copies in flight per CTA
+constexpr int NREP = ACC_REPLICAS;           // accumulator replicas (CTA c adds into replica c % NREP)
 
 struct PersistParams {
     const uint32_t *tokens;
@@ -206,11 +211,14 @@ __device__ __forceinline__ void cursor_next(const PersistParams &p, const Persis
 
 // acc[r] = w . act[r] over d (act rows d floats apart), warp-wide: every
 // lane gets the sums.
+// Each lane keeps one partial sum per float4 component (four independent
+// multiply-add chains instead of one), added as (x + y) + (z + w) at the end.
 template <int MR>
 __device__ __forceinline__ void dot_row(const float *w, const float *act, int d, float (&acc)[MR]) {
     const int lane = threadIdx.x & 31;
+    float4 part[MR];
 #pragma unroll
-    for (int r = 0; r < MR; ++r) acc[r] = 0.0f;
+    for (int r = 0; r < MR; ++r) part[r] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int d4 = d >> 2;
 #pragma unroll 4
     for (int k4 = lane; k4 < d4; k4 += 32) {
@@ -218,16 +226,14 @@ __device__ __forceinline__ void dot_row(const float *w, const float *act, int d,
 #pragma unroll
         for (int r = 0; r < MR; ++r) {
             const float4 a = *reinterpret_cast<const float4 *>(act + r * d + 4 * k4);
-            float s = acc[r];
-            s = fmaf(wv.x, a.x, s);
-            s = fmaf(wv.y, a.y, s);
-            s = fmaf(wv.z, a.z, s);
-            s = fmaf(wv.w, a.w, s);
-            acc[r] = s;
+            part[r].x = fmaf(wv.x, a.x, part[r].x);
+            part[r].y = fmaf(wv.y, a.y, part[r].y);
+            part[r].z = fmaf(wv.z, a.z, part[r].z);
+            part[r].w = fmaf(wv.w, a.w, part[r].w);
         }
     }
 #pragma unroll
-    for (int r = 0; r < MR; ++r) acc[r] = warp_sum(acc[r]);
+    for (int r = 0; r < MR; ++r) acc[r] = warp_sum((part[r].x + part[r].y) + (part[r].z + part[r].w));
 }
 
 // The same sum with act held in registers: a[r * (AREGS / MR) + i] is
@@ -247,16 +253,16 @@ __device__ __forceinline__ void dot_row_reg(const float *w, const float4 (&a)[AR
     }
 #pragma unroll
     for (int r = 0; r < MR; ++r) {
-        float s = 0.0f;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < A; ++i) {
             const float4 x = a[r * A + i];
-            s = fmaf(wv[i].x, x.x, s);
-            s = fmaf(wv[i].y, x.y, s);
-            s = fmaf(wv[i].z, x.z, s);
-            s = fmaf(wv[i].w, x.w, s);
+            s.x = fmaf(wv[i].x, x.x, s.x);
+            s.y = fmaf(wv[i].y, x.y, s.y);
+            s.z = fmaf(wv[i].z, x.z, s.z);
+            s.w = fmaf(wv[i].w, x.w, s.w);
         }
-        acc[r] = s;
+        acc[r] = (s.x + s.y) + (s.z + s.w);
     }
 #pragma unroll
     for (int r = 0; r < MR; ++r) acc[r] = warp_sum(acc[r]);
@@ -467,9 +473,9 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
             const int layer = q >> 1;
             const PersistLayer *L = kind < 2 ? &layers[layer] : nullptr;
             const Phase ph = make_phase(p, L, kind);
-            const long long *acc_in = p.acc + (size_t)(q % 3) * accsz;
-            long long *acc_out = p.acc + (size_t)((q + 1) % 3) * accsz;
-            long long *acc_clear = p.acc + (size_t)((q + 2) % 3) * accsz;
+            const long long *acc_in = p.acc + (size_t)(q % 3) * NREP * accsz;
+            long long *acc_out = p.acc + ((size_t)((q + 1) % 3) * NREP + blockIdx.x % NREP) * accsz;
+            long long *acc_clear = p.acc + (size_t)((q + 2) % 3) * NREP * accsz;
             float *state = kind == 0 ? p.state + (size_t)layer * M * (kk + 1) * E : nullptr;
             const float *ops = opsb + (size_t)(q & 1) * p.ops_cap;
             issue_ops(q + 1);
@@ -502,8 +508,18 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                                 xv[i] = __ldg(reinterpret_cast<const float4 *>(p.emb + (size_t)s_tok[r] * d + 4 * c4));
                             } else {
                                 const long long *src = acc_in + (size_t)r * d + 4 * c4;
-                                const longlong2 a0 = __ldcg(reinterpret_cast<const longlong2 *>(src));
-                                const longlong2 a1 = __ldcg(reinterpret_cast<const longlong2 *>(src + 2));
+                                longlong2 a0 = __ldcg(reinterpret_cast<const longlong2 *>(src));
+                                longlong2 a1 = __ldcg(reinterpret_cast<const longlong2 *>(src + 2));
+#pragma unroll
+                                for (int rp = 1; rp < NREP; ++rp) {
+                                    const longlong2 b0 = __ldcg(reinterpret_cast<const longlong2 *>(src + rp * accsz));
+                                    const longlong2 b1 =
+                                        __ldcg(reinterpret_cast<const longlong2 *>(src + rp * accsz + 2));
+                                    a0.x += b0.x;
+                                    a0.y += b0.y;
+                                    a1.x += b1.x;
+                                    a1.y += b1.y;
+                                }
                                 xv[i] = make_float4(from_fx(a0.x), from_fx(a0.y), from_fx(a1.x), from_fx(a1.y));
                             }
                         }
@@ -525,7 +541,8 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                                 const int n = 4 * c4 + e;
                                 if (n >= dN0 && n < dN1) {
                                     fx_add(acc_out + (size_t)r * d + n, vv[e] + obias[n - dN0]);
-                                    acc_clear[(size_t)r * d + n] = 0;
+#pragma unroll
+                                    for (int rp = 0; rp < NREP; ++rp) acc_clear[rp * accsz + (size_t)r * d + n] = 0;
                                 }
                             }
                         }
@@ -762,7 +779,7 @@ __global__ void __launch_bounds__(PTHREADS, 1) decode_step_persistent_k(const __
                 }
                 p.tokens_out[tid] = (b == -INFINITY || bi == 0xFFFFFFFFu) ? 0u : bi;
             }
-            for (int b = 0; b < 3; ++b)
+            for (int b = 0; b < 3 * NREP; ++b)
                 for (int t = tid; t < (M * d) / 2; t += CTHREADS)
                     __stcg(reinterpret_cast<longlong2 *>(p.acc + (size_t)b * accsz) + t, make_longlong2(0, 0));
             if (tid == 0) {
@@ -832,7 +849,7 @@ cudaError_t launch_mr(const PersistStepArgs &a, cudaStream_t st) {
     p.best_idx = a.best_idx;
     p.err = a.err;
     p.acc = reinterpret_cast<long long *>(a.ws);
-    p.sync = reinterpret_cast<uint32_t *>(p.acc + (size_t)3 * MAXR * a.d);
+    p.sync = reinterpret_cast<uint32_t *>(p.acc + (size_t)3 * NREP * MAXR * a.d);
     p.layers = a.layers;
     p.M = a.M;
     p.d = a.d;
@@ -890,7 +907,7 @@ __global__ void transpose_k(const float *__restrict__ in, float *__restrict__ ou
 
 int persistent_partials() { return sm_count(); }
 
-size_t persistent_ws_bytes(int d) { return (size_t)3 * MAXR * d * sizeof(long long) + 2 * sizeof(uint32_t); }
+size_t persistent_ws_bytes(int d) { return (size_t)3 * NREP * MAXR * d * sizeof(long long) + 2 * sizeof(uint32_t); }
 
 bool persistent_step_supported(int M, int d, int E, int H, int k, int V, int n_layer) {
     if (M < 1 || M > MAXR || n_layer < 1 || k < 1 || k > KCONV || V < 1 || E < 1 || H < 1) return false;

@@ -7,6 +7,7 @@
 
 #include <algorithm>
 
+#include "nk_chain.cuh"
 #include "nk_common.cuh"
 #include "nk_kernels.h"
 
@@ -423,6 +424,148 @@ __global__ void ssm_chunk_fix_k(const float *__restrict__ u, float *__restrict__
     }
 }
 
+// ---- one-pass time-parallel prefill: the scan of the chunk's positions in
+// one kernel, carries between time blocks by decoupled look-back
+// (nk_chain.cuh).  A CTA of OP_WARPS warps takes OP_TB positions of one chain
+// (a stream and 32 consecutive channels, lane = channel); warp w holds
+// positions [w OP_TW, (w+1) OP_TW) of the block in registers.  Each position's
+// v, z and o are read once and its gated output written once.
+constexpr int OP_WARPS = 8, OP_TW = 16, OP_TB = OP_WARPS * OP_TW;
+constexpr int OP_ERR = 131;  // look-back wait expired
+
+template <int KW>
+__global__ void __launch_bounds__(OP_WARPS * 32) ssm_onepass_k(
+    const float *__restrict__ u, float *__restrict__ state, const uint32_t *__restrict__ heads,
+    const uint32_t *__restrict__ lens, int t0, int tc, const float *__restrict__ conv_w,
+    const float *__restrict__ conv_b, RowOut yout, int E, int k, int ngrp, int n_chains, ChainWs ws, int *err) {
+    __shared__ int s_tk;
+    __shared__ float sA[OP_WARPS][32], sB[OP_WARPS][32], s_cin[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) s_tk = atomicAdd(ws.ticket, 1);
+    __syncthreads();
+    const int tk = s_tk;
+    const int blk = tk / n_chains, chain = tk - blk * n_chains;
+    const int s = chain / ngrp, j = (chain - s * ngrp) * 32 + lane;
+    const bool col = j < E;
+    int nv = (int)lens[s] - t0;
+    nv = nv < 0 ? 0 : (nv > tc ? tc : nv);
+    const int p0 = blk * OP_TB + warp * OP_TW;
+    const int left = col ? nv - p0 : 0;
+    const int nw = left <= 0 ? 0 : left >= OP_TW ? OP_TW : left;  // valid positions of the warp
+    const float *ur = u + (size_t)s * tc * 3 * E;
+    float *ring = state + (size_t)s * (k + 1) * E;
+    const uint32_t head0 = heads[s];
+    const size_t ybase = (size_t)s * tc * E + j;
+
+    // Decay and input of the warp's positions; m becomes the inclusive decay
+    // product, v the local state (from zero).
+    float m[OP_TW], v[OP_TW], o[OP_TW];
+    if (nw > 0) {
+        const float bias = conv_b[j];
+        constexpr int W = KW > 0 ? KW : 1;
+        float cw[W], win[W];
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+            cw[q] = q < k ? conv_w[(size_t)q * E + j] : 0.0f;
+            win[q] = (KW > 0 && q + 1 < k) ? raw_v(ur, ring, head0, k, p0 - 1 - q, E, j) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < OP_TW; ++i) {
+            const bool ok = i < nw;
+            const float *row = ur + (size_t)(p0 + i) * 3 * E;
+            v[i] = ok ? __ldcs(row + j) : 0.0f;
+            m[i] = ok ? __ldcs(row + E + j) : 0.0f;
+            o[i] = ok ? __ldcs(row + 2 * E + j) : 0.0f;
+        }
+#pragma unroll
+        for (int i = 0; i < OP_TW; ++i) {
+            if (i >= nw) {
+                m[i] = 1.0f;
+                v[i] = 0.0f;
+                continue;
+            }
+            float sum = bias;
+            if constexpr (KW > 0) {
+#pragma unroll
+                for (int q = W - 1; q > 0; --q) win[q] = win[q - 1];
+                win[0] = v[i];
+#pragma unroll
+                for (int q = 0; q < W; ++q)
+                    if (q < k) sum = sum + cw[q] * win[q];
+            } else {
+                for (int q = 0; q < k; ++q)
+                    sum = sum + conv_w[(size_t)q * E + j] *
+                                    (q == 0 ? v[i] : raw_v(ur, ring, head0, k, p0 + i - q, E, j));
+            }
+            const float value = silu(sum);
+            const float decay = sigmoid(m[i]);
+            m[i] = decay;
+            v[i] = (1.0f - decay) * value;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < OP_TW; ++i) {
+            m[i] = 1.0f;
+            v[i] = 0.0f;
+            o[i] = 0.0f;
+        }
+    }
+    // h = decay h + (1 - decay) value (model.rs:156-163) from h = 0.
+    float h = 0.0f, P = 1.0f;
+#pragma unroll
+    for (int i = 0; i < OP_TW; ++i) {
+        h = m[i] * h + v[i];
+        v[i] = h;
+        P = P * m[i];
+        m[i] = P;
+    }
+    sA[warp][lane] = P;
+    sB[warp][lane] = h;
+    __syncthreads();
+    if (warp == 0) {
+        float eA = 1.0f, eB = 0.0f;
+#pragma unroll
+        for (int w = 0; w < OP_WARPS; ++w) {
+            const float wA = sA[w][lane], wB = sB[w][lane];
+            sA[w][lane] = eA;
+            sB[w][lane] = eB;
+            eB = fmaf(wA, eB, wB);
+            eA = wA * eA;
+        }
+        // A chain starts from the layer's recurrent state.
+        const float first = (tk < n_chains && col) ? ring[(size_t)k * E + j] : 0.0f;
+        s_cin[lane] = chain_carry(ws, tk, n_chains, eA, eB, first, OP_ERR, err);
+    }
+    __syncthreads();
+    if (!col) return;
+    const float e = fmaf(sA[warp][lane], s_cin[lane], sB[warp][lane]);
+    float hlast = 0.0f;
+#pragma unroll
+    for (int i = 0; i < OP_TW; ++i) {
+        const int p = p0 + i;
+        if (p >= tc) break;
+        if (i < nw) {
+            const float hv = fmaf(m[i], e, v[i]);
+            if (p == nv - 1) hlast = hv;
+            put(yout, ybase + (size_t)p * E, hv * silu(o[i]));
+        } else {
+            put(yout, ybase + (size_t)p * E, 0.0f);
+        }
+    }
+    if (nw > 0 && p0 + nw == nv) {
+        // The warp holding the last valid position writes h and the conv ring
+        // back to the state (raw v of positions nv-1 .. nv-k, gathered first).
+        const uint32_t head1 = (uint32_t)((head0 + (uint64_t)nv) % (uint32_t)k);
+        float wv[KMAX];
+        for (int q = 0; q < k; ++q) wv[q] = raw_v(ur, ring, head0, k, nv - 1 - q, E, j);
+        for (int q = 0; q < k; ++q) {
+            const uint32_t slot = (head1 + (uint32_t)k - (uint32_t)q) % (uint32_t)k;
+            ring[(size_t)slot * E + j] = wv[q];
+        }
+        ring[(size_t)k * E + j] = hlast;
+    }
+}
+
 template <int VW>
 __global__ void swiglu_k(const float *__restrict__ up, RowOut out, int M, int H) {
     const int j = (blockIdx.x * blockDim.x + threadIdx.x) * VW;
@@ -767,6 +910,36 @@ cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *he
                                                                        blkH, carry, S, E, k, nblk);
     ssm_chunk_fix_k<<<blocks_for(n, 128), 128, 0, st>>>(u, state, heads, lens, t0, tc, y, yout, carry,
                                                         S, E, k, nblk);
+    return cudaGetLastError();
+}
+
+static size_t onepass_slots(int S, int E, int tc) {
+    return (size_t)S * (size_t)((E + 31) / 32) * (size_t)((tc + OP_TB - 1) / OP_TB);
+}
+
+size_t ssm_prefill_onepass_scratch_bytes(int S, int E, int tc) { return chain_ws_bytes(onepass_slots(S, E, tc)); }
+
+cudaError_t ssm_prefill_onepass(const float *u, float *state, const uint32_t *heads, const uint32_t *lens, int t0,
+                                int tc, const float *conv_w, const float *conv_b, RowOut yout, void *scratch, int S,
+                                int E, int k, int *err, cudaStream_t st) {
+    if ((int64_t)S * E == 0 || tc == 0) return cudaSuccess;
+    if (k > KMAX) return cudaErrorInvalidValue;
+    const size_t slots = onepass_slots(S, E, tc);
+    if (slots > (size_t)INT32_MAX) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(scratch, 0, chain_ws_bytes(slots), st);
+    if (e != cudaSuccess) return e;
+    const ChainWs ws = chain_ws(scratch, slots);
+    const int ngrp = (E + 31) / 32, nc = S * ngrp;
+    const dim3 grid((unsigned)slots), block(OP_WARPS * 32);
+    if (k <= 4)
+        ssm_onepass_k<4><<<grid, block, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, yout, E, k, ngrp, nc,
+                                                 ws, err);
+    else if (k <= 8)
+        ssm_onepass_k<8><<<grid, block, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, yout, E, k, ngrp, nc,
+                                                 ws, err);
+    else
+        ssm_onepass_k<0><<<grid, block, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, yout, E, k, ngrp, nc,
+                                                 ws, err);
     return cudaGetLastError();
 }
 

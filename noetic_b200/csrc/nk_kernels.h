@@ -78,6 +78,14 @@ cudaError_t ssm_prefill_chunked(const float *u, float *state, const uint32_t *he
                                 const float *conv_b, float *y, RowOut yout, float *scratch, int S, int E,
                                 int k, cudaStream_t st);
 size_t ssm_prefill_chunked_scratch_floats(int S, int E, int tc);
+// Same result in one kernel: time blocks of 128 positions of 32 channels
+// with carries by decoupled look-back; v, z and o read once, the gated output
+// written once.  scratch of ssm_prefill_onepass_scratch_bytes (cleared by the
+// call); an expired look-back wait writes 131 to *err.
+cudaError_t ssm_prefill_onepass(const float *u, float *state, const uint32_t *heads, const uint32_t *lens, int t0,
+                                int tc, const float *conv_w, const float *conv_b, RowOut yout, void *scratch, int S,
+                                int E, int k, int *err, cudaStream_t st);
+size_t ssm_prefill_onepass_scratch_bytes(int S, int E, int tc);
 
 // s[m,j] = SiLU(up[m,j]) * up[m,H+j] (infer.rs:188-190).
 cudaError_t swiglu_rows(const float *up, RowOut s, int M, int H, cudaStream_t st);
@@ -218,6 +226,16 @@ cudaError_t scan_sequential(const float *a, const float *b, float *h, int64_t ba
 cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch, int64_t t,
                          int64_t d, float *scratch, cudaStream_t st);
 size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d);
+// One-pass chunked scan (forward, or the adjoint when `adjoint`): one kernel
+// with decoupled look-back between time blocks; scratch of
+// scan_onepass_scratch_bytes, cleared by the call itself.  After the stream
+// has synchronised, scan_onepass_status reads the scratch's error word (0, or
+// 131 when a look-back wait expired).  Suited to d >= 16.
+bool scan_onepass_suits(int64_t batch, int64_t t, int64_t d);
+size_t scan_onepass_scratch_bytes(int64_t batch, int64_t t, int64_t d);
+cudaError_t scan_onepass(const float *a, const float *b, float *h, int64_t batch, int64_t t, int64_t d, bool adjoint,
+                         void *scratch, cudaStream_t st);
+int scan_onepass_status(const void *scratch);
 
 // Largest array the stand-alone ops take: 2^37 floats (512 GB, more than a
 // device holds), so element counts, byte counts and every grid derived from

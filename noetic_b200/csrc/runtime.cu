@@ -966,7 +966,8 @@ void check_err_flag(nk_decoder *dec) {
         cuda_check(cudaStreamSynchronize(dec->stream), "cudaStreamSynchronize");
         fail(NK_ERR_DEVICE, "a kernel reported an error (code " + std::to_string(h) +
                                 ": 1 invalid token, 2 bounded draw, 101-104 tensor-core pipeline wait expired, 105-108 CTA-pair pipeline wait expired, 111-113 "
-                                "persistent step wait expired, 121-123 stream-K hand-off wait expired, 3 non-finite logit in "
+                                "persistent step wait expired, 121-123 stream-K hand-off wait expired, 131 prefill scan look-back wait "
+                                "expired, 3 non-finite logit in "
                                 "softmax_ce)");
     }
 }
@@ -1241,8 +1242,12 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
     bool chunked = (size_t)S * E < 148 * 512 && tc > 64;
     if (dec->engine & 2) chunked = true;
     if (dec->engine & 4) chunked = false;
+    // The one-pass form when at least half of each warp's 32 lanes carry a
+    // channel, else the three-pass form.
+    const bool onepass = chunked && E >= 16;
     if (chunked) {
-        const size_t need = nk::ssm_prefill_chunked_scratch_floats(S, E, tc);
+        const size_t need = onepass ? (nk::ssm_prefill_onepass_scratch_bytes(S, E, tc) + 3) / 4
+                                    : nk::ssm_prefill_chunked_scratch_floats(S, E, tc);
         if (need > dec->p_scan_floats) {
             if (dec->p_scan) cudaFree(dec->p_scan), dec->p_scan = nullptr;
             dalloc(&dec->p_scan, need, "prefill scan scratch");
@@ -1263,7 +1268,12 @@ void prefill_device(nk_decoder *dec, const uint32_t *d_ids, const uint32_t *d_le
                        t_up = use_tc(dec, R, 2 * H, d, w_up), t_dn = use_tc(dec, R, d, H, w_dn);
             launch_ok(dec, nk::rmsnorm_rows(dec->p_x, m->dp(L.n1), m->cfg.eps, nrm.out(t_in), R, d, st), "rmsnorm");
             project(dec, t_in, nrm, R, d, m->dp(L.in_w), w_in, 3 * E, m->dp(L.in_b), dec->p_u, nullptr);
-            if (chunked)
+            if (onepass)
+                launch_ok(dec, nk::ssm_prefill_onepass(dec->p_u, dec->layer_state(l), dec->heads, d_lens, (int)t0, tcc,
+                                                       m->dp(L.conv_w), m->dp(L.conv_b), gated.out(t_out), dec->p_scan,
+                                                       S, E, k, dec->err, st),
+                          "prefill scan");
+            else if (chunked)
                 launch_ok(dec, nk::ssm_prefill_chunked(dec->p_u, dec->layer_state(l), dec->heads, d_lens, (int)t0, tcc,
                                                        m->dp(L.conv_w), m->dp(L.conv_b), dec->p_y, gated.out(t_out),
                                                        dec->p_scan, S, E, k, st),
@@ -2481,6 +2491,33 @@ struct ScratchLease {
         if (own) cudaFree(own);
     }
 };
+
+// The time-chunked scan (or its adjoint) of nk_scan_device: the one-pass
+// kernel where it suits the shape, else the three-pass form; synchronises
+// the stream and reports an expired look-back wait as NK_ERR_DEVICE.
+void chunked_scan(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d, bool adjoint,
+                  cudaStream_t st) {
+    const int64_t B = (int64_t)batch, T = (int64_t)t, D = (int64_t)d;
+    const char *what = adjoint ? "scan adjoint" : "scan";
+    if (nk::scan_onepass_suits(B, T, D)) {
+        ScratchLease lease(nk::scan_onepass_scratch_bytes(B, T, D), "scan scratch");
+        cudaError_t e = nk::scan_onepass(a, b, h, B, T, D, adjoint, lease.ptr, st);
+        cudaError_t e2 = cudaStreamSynchronize(st);
+        cuda_check(e, what);
+        cuda_check(e2, what);
+        const int status = nk::scan_onepass_status(lease.ptr);
+        if (status != 0)
+            fail(NK_ERR_DEVICE, std::string(what) + ": device error code " + std::to_string(status) +
+                                    " (131: a time block's look-back wait expired)");
+        return;
+    }
+    ScratchLease lease(nk::scan_chunked_scratch_floats(B, T, D) * sizeof(float), "scan scratch");
+    cudaError_t e = adjoint ? nk::scan_adjoint_chunked(a, b, h, B, T, D, (float *)lease.ptr, st)
+                            : nk::scan_chunked(a, b, h, B, T, D, (float *)lease.ptr, st);
+    cudaError_t e2 = cudaStreamSynchronize(st);
+    cuda_check(e, what);
+    cuda_check(e2, what);
+}
 }  // namespace
 
 nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batch, uint64_t t, uint64_t d,
@@ -2495,12 +2532,7 @@ nk_status nk_scan_device(const float *a, const float *b, float *h, uint64_t batc
             cuda_check(nk::scan_sequential(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan");
             return;
         }
-        ScratchLease lease(nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d) * sizeof(float),
-                           "scan scratch");
-        cudaError_t e = nk::scan_chunked(a, b, h, (int64_t)batch, (int64_t)t, (int64_t)d, (float *)lease.ptr, st);
-        cudaError_t e2 = cudaStreamSynchronize(st);
-        cuda_check(e, "scan");
-        cuda_check(e2, "scan sync");
+        chunked_scan(a, b, h, batch, t, d, false, st);
     });
 }
 
@@ -2516,12 +2548,7 @@ nk_status nk_scan_adjoint_device(const float *a, const float *g, float *c, uint6
             cuda_check(nk::scan_adjoint_sequential(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, st), "scan adjoint");
             return;
         }
-        ScratchLease lease(nk::scan_chunked_scratch_floats((int64_t)batch, (int64_t)t, (int64_t)d) * sizeof(float),
-                           "scan scratch");
-        cudaError_t e = nk::scan_adjoint_chunked(a, g, c, (int64_t)batch, (int64_t)t, (int64_t)d, (float *)lease.ptr, st);
-        cudaError_t e2 = cudaStreamSynchronize(st);
-        cuda_check(e, "scan adjoint");
-        cuda_check(e2, "scan adjoint sync");
+        chunked_scan(a, g, c, batch, t, d, true, st);
     });
 }
 

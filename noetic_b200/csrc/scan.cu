@@ -11,12 +11,18 @@
 //        (A_R A_L, A_R B_L + B_R), giving the carry entering each block;
 //     3. fold h_t += (prod_{r<=t} a_r) * carry_in, stopping once the product
 //        reaches zero.
+// scan_onepass: the same block decomposition with the carries passed between
+//   consecutive time blocks by decoupled look-back inside one kernel, so
+//   every element is read and written once (12 bytes of HBM traffic).
 //   The reference flushes decay products below 1e-30 to zero to dodge slow
 //   x86 denormals; GPU denormal arithmetic is full speed, so products decay
 //   naturally (values below 1e-30 times an O(1) carry cannot move an f32 h
 //   of the same row beyond rounding).
 
+#include <algorithm>
+
 #include "../../include/noetic_gpu.h"
+#include "nk_chain.cuh"
 #include "nk_common.cuh"
 #include "nk_kernels.h"
 
@@ -259,6 +265,142 @@ __global__ void adj_fix_k(const float *__restrict__ a, float *__restrict__ c, co
     }
 }
 
+// ---- one-pass form: every element is read once and written once.
+//
+// A block is OP_TB consecutive steps of one chain (one batch entry, 32
+// channels: lane = channel, so every row access is one 128-byte segment);
+// warp w of a CTA holds steps [w OP_TW, (w+1) OP_TW) of it in registers.
+// Each warp scans its steps from a zero state, the warps' maps compose in
+// shared memory into the block's map, the block's entering state comes from
+// its predecessors by decoupled look-back (nk_chain.cuh), and every step is
+// finished as local + (product of the multipliers up to it) * entering
+// state, the same fold as the three-pass form, before its single store.
+// ADJ = the adjoint, walking down in time: step t takes the carry x, writes
+// c_t = g_t + x and passes a_t c_t on.
+//
+// The CTAs are persistent and take blocks from the ticket counter; each
+// issues the loads of its next block before it waits on the current block's
+// look-back, so the wait overlaps a block of reads.
+constexpr int OP_WARPS = 8, OP_TW = 16, OP_TB = OP_WARPS * OP_TW;
+constexpr int OP_ERR = 131;  // look-back wait expired
+
+struct OpShape {
+    const float *a, *b;
+    float *h;
+    int64_t t, d, ngrp, n_chains, slots;
+};
+
+// Element offset of step 0 of the warp's part of block tk, and its count of
+// existing steps (step i sits at o0 + i * (ADJ ? -d : d)).
+template <bool ADJ>
+__device__ __forceinline__ int op_locate(const OpShape &sh, int64_t tk, int64_t &o0) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t blk = tk / sh.n_chains, chain = tk - blk * sh.n_chains;
+    const int64_t bi = chain / sh.ngrp, j = (chain - bi * sh.ngrp) * 32 + lane;
+    const int64_t q0 = blk * OP_TB + (int64_t)warp * OP_TW;
+    const int64_t left = sh.t - q0;
+    o0 = (bi * sh.t + (ADJ ? sh.t - 1 - q0 : q0)) * sh.d + j;
+    return j >= sh.d || left <= 0 ? 0 : left >= OP_TW ? OP_TW : (int)left;
+}
+
+template <bool ADJ>
+__device__ __forceinline__ void op_load(const OpShape &sh, int64_t tk, float (&m)[OP_TW], float (&v)[OP_TW]) {
+    int64_t o0 = 0;
+    const int nv = tk < sh.slots ? op_locate<ADJ>(sh, tk, o0) : 0;
+    const int64_t sd = ADJ ? -sh.d : sh.d;
+#pragma unroll
+    for (int i = 0; i < OP_TW; ++i) {
+        const bool ok = i < nv;
+        m[i] = ok ? __ldcs(sh.a + o0 + i * sd) : 1.0f;
+        v[i] = ok ? __ldcs(sh.b + o0 + i * sd) : 0.0f;
+    }
+}
+
+struct OpShared {
+    float sA[OP_WARPS][32], sB[OP_WARPS][32], cin[32];
+    int next;
+};
+
+template <bool ADJ>
+__device__ __forceinline__ void op_finish(const OpShape &sh, const ChainWs &ws, OpShared &sm, int64_t tk,
+                                          float (&m)[OP_TW], float (&v)[OP_TW]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Local scan; m[i] becomes the factor of the entering state in step i's
+    // output: the inclusive product (forward) or the exclusive one (adjoint).
+    float s = 0.0f, P = 1.0f;
+#pragma unroll
+    for (int i = 0; i < OP_TW; ++i) {
+        if (ADJ) {
+            const float out = v[i] + s;
+            v[i] = out;
+            s = m[i] * out;
+            const float pe = P;
+            P = P * m[i];
+            m[i] = pe;
+        } else {
+            s = m[i] * s + v[i];
+            v[i] = s;
+            P = P * m[i];
+            m[i] = P;
+        }
+    }
+    sm.sA[warp][lane] = P;
+    sm.sB[warp][lane] = s;
+    __syncthreads();
+    if (warp == 0) {
+        // Warp maps in order: (sA, sB)[w] becomes the map from the block's
+        // entering state to warp w's; (eA, eB) ends as the block's map.
+        float eA = 1.0f, eB = 0.0f;
+#pragma unroll
+        for (int w = 0; w < OP_WARPS; ++w) {
+            const float wA = sm.sA[w][lane], wB = sm.sB[w][lane];
+            sm.sA[w][lane] = eA;
+            sm.sB[w][lane] = eB;
+            eB = fmaf(wA, eB, wB);
+            eA = wA * eA;
+        }
+        sm.cin[lane] = chain_carry(ws, tk, sh.n_chains, eA, eB, 0.0f, OP_ERR, nullptr);
+    }
+    __syncthreads();
+    const float e = fmaf(sm.sA[warp][lane], sm.cin[lane], sm.sB[warp][lane]);
+    int64_t o0 = 0;
+    const int nv = op_locate<ADJ>(sh, tk, o0);
+    const int64_t sd = ADJ ? -sh.d : sh.d;
+#pragma unroll
+    for (int i = 0; i < OP_TW; ++i)
+        if (i < nv) __stcs(sh.h + o0 + i * sd, fmaf(m[i], e, v[i]));
+}
+
+template <bool ADJ>
+__global__ void __launch_bounds__(OP_WARPS * 32, 2) scan_onepass_k(const OpShape sh, ChainWs ws) {
+    __shared__ OpShared sm;
+    float m0[OP_TW], v0[OP_TW], m1[OP_TW], v1[OP_TW];
+    if (threadIdx.x == 0) sm.next = atomicAdd(ws.ticket, 1);
+    __syncthreads();
+    int64_t tk = sm.next;
+    op_load<ADJ>(sh, tk, m0, v0);
+    // Two blocks per trip so that both register sets stay statically indexed.
+    // Every thread reads sm.next after the barrier that follows its write and
+    // before the barriers inside op_finish, which precede the next write.
+    while (tk < sh.slots) {
+        __syncthreads();
+        if (threadIdx.x == 0) sm.next = atomicAdd(ws.ticket, 1);
+        __syncthreads();
+        int64_t tn = sm.next;
+        op_load<ADJ>(sh, tn, m1, v1);
+        op_finish<ADJ>(sh, ws, sm, tk, m0, v0);
+        tk = tn;
+        if (tk >= sh.slots) break;
+        __syncthreads();
+        if (threadIdx.x == 0) sm.next = atomicAdd(ws.ticket, 1);
+        __syncthreads();
+        tn = sm.next;
+        op_load<ADJ>(sh, tn, m0, v0);
+        op_finish<ADJ>(sh, ws, sm, tk, m1, v1);
+        tk = tn;
+    }
+}
+
 }  // namespace
 
 size_t scan_chunked_scratch_floats(int64_t batch, int64_t t, int64_t d) {
@@ -283,6 +425,52 @@ cudaError_t scan_chunked(const float *a, const float *b, float *h, int64_t batch
     scan_carry_k<<<blocks_for(batch * d, 128), 128, 0, st>>>(blkA, blkB, carry, batch, d, nblk);
     scan_fix_k<<<blocks_for(per, 128), 128, 0, st>>>(a, h, carry, batch, t, d, nblk);
     return cudaGetLastError();
+}
+
+size_t scan_onepass_slots(int64_t batch, int64_t t, int64_t d) {
+    return (size_t)batch * (size_t)((d + 31) / 32) * (size_t)((t + OP_TB - 1) / OP_TB);
+}
+
+bool scan_onepass_suits(int64_t batch, int64_t t, int64_t d) {
+    // At least half of every warp's lanes carry a channel, and the chain
+    // scratch stays a few percent of the data.
+    return batch * t * d > 0 && d >= 16;
+}
+
+size_t scan_onepass_scratch_bytes(int64_t batch, int64_t t, int64_t d) {
+    return chain_ws_bytes(scan_onepass_slots(batch, t, d));
+}
+
+cudaError_t scan_onepass(const float *a, const float *b, float *h, int64_t batch, int64_t t, int64_t d, bool adjoint,
+                         void *scratch, cudaStream_t st) {
+    if (batch * t * d == 0) return cudaSuccess;
+    const size_t slots = scan_onepass_slots(batch, t, d);
+    const int64_t ngrp = (d + 31) / 32;
+    cudaError_t e = cudaMemsetAsync(scratch, 0, chain_ws_bytes(slots), st);
+    if (e != cudaSuccess) return e;
+    const ChainWs ws = chain_ws(scratch, slots);
+    const OpShape sh{a, b, h, t, d, ngrp, batch * ngrp, (int64_t)slots};
+    // Persistent grid: the CTAs resident at once (two per SM), at most one per block.
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 1;
+    }
+    const unsigned grid = (unsigned)std::min<size_t>(slots, (size_t)2 * sms);
+    if (adjoint)
+        scan_onepass_k<true><<<grid, OP_WARPS * 32, 0, st>>>(sh, ws);
+    else
+        scan_onepass_k<false><<<grid, OP_WARPS * 32, 0, st>>>(sh, ws);
+    return cudaGetLastError();
+}
+
+int scan_onepass_status(const void *scratch) {
+    int v = 0;
+    if (cudaMemcpy(&v, reinterpret_cast<const int *>(scratch) + 1, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+        return -1;
+    return v;
 }
 
 cudaError_t scan_adjoint_sequential(const float *a, const float *g, float *c, int64_t batch, int64_t t, int64_t d,

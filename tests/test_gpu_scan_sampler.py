@@ -160,3 +160,38 @@ def test_scan_adjoint_linearity_at_size(gpu):
     assert np.abs(c12 - (c1 + c2)).max() <= 1e-5 * scale
     cs = gpu.scan_adjoint(a, g1, batch, t, d, chunked=False)
     assert np.abs(cs - c1).max() <= 1e-4 * np.abs(cs).max()
+
+
+@pytest.mark.parametrize("adjoint", [False, True])
+def test_one_pass_scan_block_edges(gpu, orc, adjoint):
+    """The one-pass chunked scan (time blocks of 128 steps of 32 channels,
+    carries by look-back) on shapes that cross every edge it has: lengths
+    around a block (127, 128, 129), many blocks (4097), channel counts that
+    leave a partial lane group (16, 33, 100), against the oracle's sequential
+    scan (tolerance 1e-4, scan.rs:286) and against the three-pass form of the
+    no-allocation entry point."""
+    rs = np.random.default_rng(17 + int(adjoint))
+    for batch, t, d in [(1, 1, 16), (2, 127, 33), (3, 128, 32), (1, 129, 100), (2, 4097, 48), (1, 300, 768)]:
+        n = batch * t * d
+        a = rs.uniform(0.01, 0.99, n).astype(np.float32)
+        b = rs.standard_normal(n).astype(np.float32)
+        if adjoint:
+            ref = orc.scan_adjoint(a, b, batch, t, d)
+            got = gpu.scan_adjoint(a, b, batch, t, d, chunked=True)
+        else:
+            ref = orc.scan_sequential(a, b, batch, t, d, 1)
+            got = gpu.scan_chunked(a, b, batch, t, d)
+        assert np.abs(got - ref).max() < 1e-4, (batch, t, d)
+
+
+def test_one_pass_scan_slow_decay_long_rows(gpu, orc):
+    # Decays near 1 carry the state across every block of a 20000-step row,
+    # so each block's entering state depends on all its predecessors.
+    rs = np.random.default_rng(29)
+    batch, t, d = 2, 20000, 32
+    n = batch * t * d
+    a = rs.uniform(0.995, 0.9999, n).astype(np.float32)
+    b = (rs.standard_normal(n) * 0.01).astype(np.float32)
+    ref = orc.scan_sequential(a, b, batch, t, d, 1)
+    got = gpu.scan_chunked(a, b, batch, t, d)
+    assert np.abs(got - ref).max() < 1e-4 * max(1.0, float(np.abs(ref).max()))
