@@ -566,6 +566,160 @@ __global__ void __launch_bounds__(OP_WARPS * 32) ssm_onepass_k(
     }
 }
 
+// The same prefill with each block staged in shared memory: the v rows of
+// the block and of the OP_HALO positions before it, and its z and o rows,
+// arrive by 16-byte cp.async (every row segment is 128 bytes of one
+// position); each warp scans its positions there in place (v becomes the
+// local state, z the decay product) and writes each gated output once.
+// Needs E % 4 == 0, a 16-byte aligned u and conv widths k <= OP_HALO.
+constexpr int OP_HALO = 8;
+constexpr size_t OP_SMEM_BYTES = (size_t)(OP_HALO + 3 * OP_TB) * 32 * sizeof(float);
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(src)
+                 : "memory");
+}
+
+template <int KW>
+__global__ void __launch_bounds__(OP_WARPS * 32) ssm_onepass_smem_k(
+    const float *__restrict__ u, float *__restrict__ state, const uint32_t *__restrict__ heads,
+    const uint32_t *__restrict__ lens, int t0, int tc, const float *__restrict__ conv_w,
+    const float *__restrict__ conv_b, RowOut yout, int E, int k, int ngrp, int n_chains, ChainWs ws, int *err) {
+    extern __shared__ __align__(16) float op_smem[];
+    float(*tv)[32] = reinterpret_cast<float(*)[32]>(op_smem);                       // [OP_HALO + OP_TB]
+    float(*tz)[32] = reinterpret_cast<float(*)[32]>(op_smem + (OP_HALO + OP_TB) * 32);  // [OP_TB]
+    float(*to)[32] = reinterpret_cast<float(*)[32]>(op_smem + (OP_HALO + 2 * OP_TB) * 32);
+    __shared__ int s_tk;
+    __shared__ float sA[OP_WARPS][32], sB[OP_WARPS][32], s_cin[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) s_tk = atomicAdd(ws.ticket, 1);
+    __syncthreads();
+    const int tk = s_tk;
+    const int blk = tk / n_chains, chain = tk - blk * n_chains;
+    const int s = chain / ngrp, j0 = (chain - s * ngrp) * 32, j = j0 + lane;
+    int nv = (int)lens[s] - t0;
+    nv = nv < 0 ? 0 : (nv > tc ? tc : nv);
+    const int pb = blk * OP_TB;  // the block's first position
+    const float *ur = u + (size_t)s * tc * 3 * E;
+    float *ring = state + (size_t)s * (k + 1) * E;
+    const uint32_t head0 = heads[s];
+    // Rows: v of positions pb - OP_HALO .. pb + OP_TB - 1, z and o of the
+    // block's positions; positions before the chunk come from the ring.
+    for (int idx = threadIdx.x; idx < (OP_HALO + 3 * OP_TB) * 8; idx += OP_WARPS * 32) {
+        const int row = idx >> 3, seg = idx & 7, jj = j0 + 4 * seg;
+        float *dst;
+        int p, f;
+        if (row < OP_HALO + OP_TB) {
+            dst = &tv[row][4 * seg];
+            p = pb - OP_HALO + row;
+            f = 0;
+        } else if (row < OP_HALO + 2 * OP_TB) {
+            dst = &tz[row - OP_HALO - OP_TB][4 * seg];
+            p = pb + row - OP_HALO - OP_TB;
+            f = 1;
+        } else {
+            dst = &to[row - OP_HALO - 2 * OP_TB][4 * seg];
+            p = pb + row - OP_HALO - 2 * OP_TB;
+            f = 2;
+        }
+        if (jj < E && p >= 0 && p < nv) {
+            cp_async16(dst, ur + (size_t)p * 3 * E + (size_t)f * E + jj);
+        } else {
+            float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (jj < E && p < 0 && p >= -(k - 1) && f == 0) {
+                const uint32_t slot = (uint32_t)(((int)head0 + 1 + p + 2 * k) % k);
+                val = *reinterpret_cast<const float4 *>(ring + (size_t)slot * E + jj);
+            }
+            *reinterpret_cast<float4 *>(dst) = val;
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    const int r0 = warp * OP_TW;  // the warp's first row in the block
+    const int left = j < E ? nv - (pb + r0) : 0;
+    const int nw = left <= 0 ? 0 : left >= OP_TW ? OP_TW : left;  // valid positions of the warp
+    constexpr int W = KW > 0 ? KW : OP_HALO;
+    float cw[W], win[W];
+    const float bias = j < E ? conv_b[j] : 0.0f;
+#pragma unroll
+    for (int q = 0; q < W; ++q) {
+        cw[q] = (q < k && j < E) ? conv_w[(size_t)q * E + j] : 0.0f;
+        // before position r0 is shifted in, win[q] = v at r0 - 1 - q
+        win[q] = q + 1 < k ? tv[OP_HALO + r0 - 1 - q][lane] : 0.0f;
+    }
+    __syncthreads();  // every warp holds its window before rows turn into states
+    float h = 0.0f, P = 1.0f;
+#pragma unroll 4
+    for (int i = 0; i < OP_TW; ++i) {
+        const int r = r0 + i;
+        float m = 1.0f, add = 0.0f;
+        if (i < nw) {
+#pragma unroll
+            for (int q = W - 1; q > 0; --q) win[q] = win[q - 1];
+            win[0] = tv[OP_HALO + r][lane];
+            float sum = bias;
+#pragma unroll
+            for (int q = 0; q < W; ++q)
+                if (q < k) sum = sum + cw[q] * win[q];
+            const float value = silu(sum);
+            m = sigmoid(tz[r][lane]);
+            add = (1.0f - m) * value;
+        }
+        // h = decay h + (1 - decay) value (model.rs:156-163) from h = 0.
+        h = m * h + add;
+        P = P * m;
+        tv[OP_HALO + r][lane] = h;
+        tz[r][lane] = P;
+    }
+    sA[warp][lane] = P;
+    sB[warp][lane] = h;
+    __syncthreads();
+    if (warp == 0) {
+        float eA = 1.0f, eB = 0.0f;
+#pragma unroll
+        for (int w = 0; w < OP_WARPS; ++w) {
+            const float wA = sA[w][lane], wB = sB[w][lane];
+            sA[w][lane] = eA;
+            sB[w][lane] = eB;
+            eB = fmaf(wA, eB, wB);
+            eA = wA * eA;
+        }
+        // A chain starts from the layer's recurrent state.
+        const float first = (tk < n_chains && j < E) ? ring[(size_t)k * E + j] : 0.0f;
+        s_cin[lane] = chain_carry(ws, tk, n_chains, eA, eB, first, OP_ERR, err);
+    }
+    __syncthreads();
+    if (j >= E) return;
+    const float e = fmaf(sA[warp][lane], s_cin[lane], sB[warp][lane]);
+    const size_t ybase = (size_t)s * tc * E + j;
+    float hlast = 0.0f;
+#pragma unroll 4
+    for (int i = 0; i < OP_TW; ++i) {
+        const int r = r0 + i, p = pb + r;
+        if (p >= tc) break;
+        if (i < nw) {
+            const float hv = fmaf(tz[r][lane], e, tv[OP_HALO + r][lane]);
+            if (p == nv - 1) hlast = hv;
+            put(yout, ybase + (size_t)p * E, hv * silu(to[r][lane]));
+        } else {
+            put(yout, ybase + (size_t)p * E, 0.0f);
+        }
+    }
+    if (nw > 0 && pb + r0 + nw == nv) {
+        // The warp holding the last valid position writes h and the conv ring
+        // back to the state (raw v of positions nv-1 .. nv-k, gathered first).
+        const uint32_t head1 = (uint32_t)((head0 + (uint64_t)nv) % (uint32_t)k);
+        float wv[OP_HALO];
+        for (int q = 0; q < k; ++q) wv[q] = raw_v(ur, ring, head0, k, nv - 1 - q, E, j);
+        for (int q = 0; q < k; ++q) {
+            const uint32_t slot = (head1 + (uint32_t)k - (uint32_t)q) % (uint32_t)k;
+            ring[(size_t)slot * E + j] = wv[q];
+        }
+        ring[(size_t)k * E + j] = hlast;
+    }
+}
+
 template <int VW>
 __global__ void swiglu_k(const float *__restrict__ up, RowOut out, int M, int H) {
     const int j = (blockIdx.x * blockDim.x + threadIdx.x) * VW;
@@ -931,6 +1085,20 @@ cudaError_t ssm_prefill_onepass(const float *u, float *state, const uint32_t *he
     const ChainWs ws = chain_ws(scratch, slots);
     const int ngrp = (E + 31) / 32, nc = S * ngrp;
     const dim3 grid((unsigned)slots), block(OP_WARPS * 32);
+    if (E % 4 == 0 && k <= OP_HALO && (reinterpret_cast<uintptr_t>(u) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(state) & 15) == 0) {
+        static bool attr_set[2] = {false, false};
+        auto kern = k <= 4 ? ssm_onepass_smem_k<4> : ssm_onepass_smem_k<8>;
+        bool &set = attr_set[k <= 4 ? 0 : 1];
+        if (!set) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)OP_SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+            set = true;
+        }
+        kern<<<grid, block, OP_SMEM_BYTES, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, yout, E, k, ngrp, nc,
+                                                 ws, err);
+        return cudaGetLastError();
+    }
     if (k <= 4)
         ssm_onepass_k<4><<<grid, block, 0, st>>>(u, state, heads, lens, t0, tc, conv_w, conv_b, yout, E, k, ngrp, nc,
                                                  ws, err);

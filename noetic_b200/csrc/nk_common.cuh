@@ -22,6 +22,32 @@ __device__ __forceinline__ float sigmoid(float x) {
 
 __device__ __forceinline__ float silu(float x) { return x * sigmoid(x); }
 
+// The recurrent branch of one decode step for one (stream, channel),
+// infer.rs:155-176: write v into the conv ring at `head` (the already
+// advanced slot), causal conv over the ring (taps q = 0..k-1, q ascending),
+// SiLU, sigmoid decay, h = decay h + (1 - decay) value, output gate.  ring is
+// the stream's layer state [k+1][E] (row k = h).  Returns the gated output.
+// The same operations, in the same order, as ssm_decode_k.  K > 0 fixes
+// the conv width at compile time (k_dyn must equal it); K = 0 takes k_dyn.
+template <int K>
+__device__ __forceinline__ float ssm_step_channel(float v, float z, float o, float *ring, uint32_t head, int k_dyn,
+                                                  int E, int j, const float *conv_w, const float *conv_b) {
+    const int k = K > 0 ? K : k_dyn;
+    float sum = conv_b[j] + conv_w[j] * v;
+    ring[(size_t)head * E + j] = v;
+#pragma unroll
+    for (int q = 1; q < (K > 0 ? K : 64); ++q) {
+        if (q >= k) break;
+        const uint32_t slot = (head + (uint32_t)k - (uint32_t)q) % (uint32_t)k;
+        sum = sum + conv_w[(size_t)q * E + j] * ring[(size_t)slot * E + j];
+    }
+    const float value = silu(sum);
+    const float decay = sigmoid(z);
+    const float h = decay * ring[(size_t)k * E + j] + (1.0f - decay) * value;
+    ring[(size_t)k * E + j] = h;
+    return h * silu(o);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

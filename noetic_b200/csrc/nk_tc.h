@@ -105,6 +105,27 @@ struct TcEpilogue {
     // 256-wide store / SwiGLU / sampling epilogues write through bulk tensor
     // stores (C 16-byte aligned, ldc a multiple of 4) unless this is set.
     bool no_tma_store = false;
+    // Work taken over by the split-K reduction when the projection is split
+    // along K (one row of tiles, M <= 512); *post_done (nullable) is set to 1
+    // when it was, else 0 and the caller runs the separate kernel.
+    //  - post_norm (store mode with N = d): after the row x is stored, its
+    //    RMSNorm x * r * gain, r = 1 / sqrt(mean(x^2) + eps) (tensor.rs:298-312,
+    //    the same operations as rmsnorm_rows), goes to post_norm_hi / _lo as
+    //    the 3xTF32 operand pair, or as f32 to post_norm_f32.
+    //  - post_ssm (store mode, N = 3E, no residual): instead of storing u, the
+    //    decode step's recurrent branch (infer.rs:155-176, as ssm_decode) runs
+    //    on the reduced (v, z, o) of each channel: conv ring, h update of
+    //    post_state [M][k+1][E] at post_heads, and the gated output to
+    //    post_g_hi / _lo (pair) or post_g_f32.
+    const float *post_norm_gain = nullptr;
+    float post_norm_eps = 0.0f;
+    float *post_norm_hi = nullptr, *post_norm_lo = nullptr, *post_norm_f32 = nullptr;
+    float *post_state = nullptr;
+    const uint32_t *post_heads = nullptr;
+    const float *post_conv_w = nullptr, *post_conv_b = nullptr;
+    int post_k = 0;
+    float *post_g_hi = nullptr, *post_g_lo = nullptr, *post_g_f32 = nullptr;
+    int *post_done = nullptr;
 };
 
 // Whether the tcgen05 engine takes a projection of this shape.

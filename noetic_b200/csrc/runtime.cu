@@ -703,6 +703,12 @@ constexpr int ENGINE_WITHHOLD_ARRIVAL = 8192;
 // the 256-wide tile's epilogue is not overlapped with the next tile's main
 // loop and the extra stores lengthen it by more than the norm kernels cost.
 constexpr int ENGINE_FOLD = 16384;
+// Engine bits 16 / 17: the split-K reductions of small projections do not
+// take over the next RMSNorm / the recurrent branch (separate kernels, as
+// above 512 streams).
+constexpr int ENGINE_NO_POST_NORM = 65536;
+constexpr int ENGINE_NO_POST_SSM = 131072;
+constexpr int POST_NORM_MIN_ROWS = 128;  // streams from which the reductions take over RMSNorm
 constexpr uint64_t TEST_WAIT_NS = 2000000ull;
 void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
     if (dec->engine & ENGINE_NO_TMA_STORE) ep.no_tma_store = true;
@@ -747,10 +753,24 @@ void apply_fold(nk_decoder *dec, const Fold *f, nk::TcEpilogue &ep) {
     }
 }
 
+// Work that the split-K reduction of a small projection may take over (see
+// TcEpilogue::post_*): the next RMSNorm after a residual projection, or the
+// recurrent branch after the input projection.
+struct Post {
+    const float *norm_gain = nullptr;
+    nk::RowOut norm_out{};
+    float *state = nullptr;
+    const float *conv_w = nullptr, *conv_b = nullptr;
+    nk::RowOut g_out{};
+};
+
 // C = A.W^T (+bias) (R + ...), A read from `a` in the form `tc` selects.
-void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W, const nk::TcOperand *Wtc,
-             int N, const float *bias, float *C, const float *R, const Fold *fold = nullptr) {
+// Returns whether the projection also did `post`'s work.
+bool project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *W, const nk::TcOperand *Wtc,
+             int N, const float *bias, float *C, const float *R, const Fold *fold = nullptr,
+             const Post *post = nullptr) {
     ProfScope prof(dec, M, N, K, R != nullptr, bias != nullptr);
+    int done = 0;
     if (tc) {
         nk::TcEpilogue ep;
         ep.C = C;
@@ -765,6 +785,26 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         ep.n_flags = nk_decoder::KSPLIT_FLAGS;
         test_controls(dec, ep);
         apply_fold(dec, fold, ep);
+        if (post && !(post->norm_gain ? (dec->engine & ENGINE_NO_POST_NORM) : (dec->engine & ENGINE_NO_POST_SSM))) {
+            const nk_model *m = dec->model;
+            if (post->norm_gain) {
+                ep.post_norm_gain = post->norm_gain;
+                ep.post_norm_eps = m->cfg.eps;
+                ep.post_norm_hi = post->norm_out.hi;
+                ep.post_norm_lo = post->norm_out.lo;
+                ep.post_norm_f32 = post->norm_out.f32;
+            } else if (post->state) {
+                ep.post_state = post->state;
+                ep.post_heads = dec->heads;
+                ep.post_conv_w = post->conv_w;
+                ep.post_conv_b = post->conv_b;
+                ep.post_k = (int)m->k();
+                ep.post_g_hi = post->g_out.hi;
+                ep.post_g_lo = post->g_out.lo;
+                ep.post_g_f32 = post->g_out.f32;
+            }
+            ep.post_done = &done;
+        }
         ep.launches = &dec->launches;
         cuda_check(nk::tc_gemm(a.hi, a.lo, M, K, *Wtc, ep, pick_bn(dec, M, N), dec->stream, dec->err),
                    "tcgen05 projection");
@@ -773,6 +813,7 @@ void project(nk_decoder *dec, bool tc, const Act &a, int M, int K, const float *
         nk::GemmArgs p{a.f32, K, W, K, C, N, M, N, K, bias, R, N};
         launch_ok(dec, nk::gemm_nt_simt(p, dec->stream), "f32 projection");
     }
+    return done != 0;
 }
 
 // s = SiLU(a) * b of up_proj (infer.rs:185-190) in the form the down
@@ -1169,25 +1210,51 @@ void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint3
         }
         return;
     }
+    const nk::TcOperand *w_lg = tc_op(m, 4 * m->cfg.n_layer);
+    const bool t_lg = use_tc(dec, S, V, d, w_lg);
+    // With few streams the projections are split along K, and their
+    // reductions also run the recurrent branch (input projection) or the
+    // next RMSNorm (residual projections); `normed` says that `nrm` holds the
+    // next norm of x already.
+    bool normed = false;
     for (uint64_t l = 0; l < m->cfg.n_layer; ++l) {
         const LayerIx &L = m->layers[l];
         const nk::TcOperand *w_in = tc_op(m, 4 * l + 0), *w_out = tc_op(m, 4 * l + 1), *w_up = tc_op(m, 4 * l + 2),
                             *w_dn = tc_op(m, 4 * l + 3);
         const bool t_in = use_tc(dec, S, 3 * E, d, w_in), t_out = use_tc(dec, S, d, E, w_out),
                    t_up = use_tc(dec, S, 2 * H, d, w_up), t_dn = use_tc(dec, S, d, H, w_dn);
-        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n1), m->cfg.eps, nrm.out(t_in), S, d, st), "rmsnorm");
-        project(dec, t_in, nrm, S, d, m->dp(L.in_w), w_in, 3 * E, m->dp(L.in_b), dec->u, nullptr);
-        launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w), m->dp(L.conv_b),
-                                      gated.out(t_out), S, E, k, st), "ssm step");
-        project(dec, t_out, gated, S, E, m->dp(L.out_w), w_out, d, m->dp(L.out_b), dec->x, dec->x);
-        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n2), m->cfg.eps, nrm.out(t_up), S, d, st), "rmsnorm");
+        if (!normed)
+            launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n1), m->cfg.eps, nrm.out(t_in), S, d, st), "rmsnorm");
+        Post p_ssm;
+        p_ssm.state = dec->layer_state(l);
+        p_ssm.conv_w = m->dp(L.conv_w);
+        p_ssm.conv_b = m->dp(L.conv_b);
+        p_ssm.g_out = gated.out(t_out);
+        if (!project(dec, t_in, nrm, S, d, m->dp(L.in_w), w_in, 3 * E, m->dp(L.in_b), dec->u, nullptr, nullptr,
+                     &p_ssm))
+            launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w), m->dp(L.conv_b),
+                                          gated.out(t_out), S, E, k, st), "ssm step");
+        // The norm-taking reduction runs one CTA per row: with fewer rows than
+        // SMs it is slower than the separate kernels (measured 1.070 vs 1.019
+        // ms per step at 64 streams, 1.657 vs 1.724 at 512).
+        const bool post_norm = S >= POST_NORM_MIN_ROWS;
+        Post p_n2;
+        p_n2.norm_gain = post_norm ? m->dp(L.n2) : nullptr;
+        p_n2.norm_out = nrm.out(t_up);
+        if (!project(dec, t_out, gated, S, E, m->dp(L.out_w), w_out, d, m->dp(L.out_b), dec->x, dec->x, nullptr,
+                     &p_n2))
+            launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(L.n2), m->cfg.eps, nrm.out(t_up), S, d, st), "rmsnorm");
         const Act s_act = project_swiglu(dec, t_up, nrm, S, d, m->dp(L.up_w), w_up, H, m->dp(L.up_b), dec->u, gated,
                                          t_dn);
-        project(dec, t_dn, s_act, S, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->x, dec->x);
+        Post p_next;
+        const bool last = l + 1 == m->cfg.n_layer;
+        p_next.norm_gain = !post_norm ? nullptr : last ? m->dp(m->norm_f) : m->dp(m->layers[l + 1].n1);
+        p_next.norm_out = nrm.out(last ? t_lg : use_tc(dec, S, 3 * E, d, tc_op(m, 4 * (l + 1))));
+        normed = project(dec, t_dn, s_act, S, H, m->dp(L.down_w), w_dn, d, m->dp(L.down_b), dec->x, dec->x, nullptr,
+                         &p_next);
     }
-    const nk::TcOperand *w_lg = tc_op(m, 4 * m->cfg.n_layer);
-    const bool t_lg = use_tc(dec, S, V, d, w_lg);
-    launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, nrm.out(t_lg), S, d, st), "rmsnorm");
+    if (!normed)
+        launch_ok(dec, nk::rmsnorm_rows(dec->x, m->dp(m->norm_f), m->cfg.eps, nrm.out(t_lg), S, d, st), "rmsnorm");
     if (want_logits || !tokens_out) {
         if (dec->fuse_sample && t_lg && !tokens_out) {
             dec->fused_parts = project_sample_prep(dec, nrm, S, d, w_lg, V);
@@ -2383,7 +2450,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 65535) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 262143) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

@@ -277,10 +277,6 @@ __global__ void adj_fix_k(const float *__restrict__ a, float *__restrict__ c, co
 // state, the same fold as the three-pass form, before its single store.
 // ADJ = the adjoint, walking down in time: step t takes the carry x, writes
 // c_t = g_t + x and passes a_t c_t on.
-//
-// The CTAs are persistent and take blocks from the ticket counter; each
-// issues the loads of its next block before it waits on the current block's
-// look-back, so the wait overlaps a block of reads.
 constexpr int OP_WARPS = 8, OP_TW = 16, OP_TB = OP_WARPS * OP_TW;
 constexpr int OP_ERR = 131;  // look-back wait expired
 
@@ -372,32 +368,104 @@ __device__ __forceinline__ void op_finish(const OpShape &sh, const ChainWs &ws, 
 }
 
 template <bool ADJ>
-__global__ void __launch_bounds__(OP_WARPS * 32, 2) scan_onepass_k(const OpShape sh, ChainWs ws) {
+__global__ void __launch_bounds__(OP_WARPS * 32) scan_onepass_k(const OpShape sh, ChainWs ws) {
     __shared__ OpShared sm;
-    float m0[OP_TW], v0[OP_TW], m1[OP_TW], v1[OP_TW];
+    float m[OP_TW], v[OP_TW];
     if (threadIdx.x == 0) sm.next = atomicAdd(ws.ticket, 1);
     __syncthreads();
-    int64_t tk = sm.next;
-    op_load<ADJ>(sh, tk, m0, v0);
-    // Two blocks per trip so that both register sets stay statically indexed.
-    // Every thread reads sm.next after the barrier that follows its write and
-    // before the barriers inside op_finish, which precede the next write.
-    while (tk < sh.slots) {
-        __syncthreads();
-        if (threadIdx.x == 0) sm.next = atomicAdd(ws.ticket, 1);
-        __syncthreads();
-        int64_t tn = sm.next;
-        op_load<ADJ>(sh, tn, m1, v1);
-        op_finish<ADJ>(sh, ws, sm, tk, m0, v0);
-        tk = tn;
-        if (tk >= sh.slots) break;
-        __syncthreads();
-        if (threadIdx.x == 0) sm.next = atomicAdd(ws.ticket, 1);
-        __syncthreads();
-        tn = sm.next;
-        op_load<ADJ>(sh, tn, m0, v0);
-        op_finish<ADJ>(sh, ws, sm, tk, m1, v1);
-        tk = tn;
+    const int64_t tk = sm.next;
+    op_load<ADJ>(sh, tk, m, v);
+    op_finish<ADJ>(sh, ws, sm, tk, m, v);
+}
+
+// The same scan with each block staged in shared memory: a CTA of SM_WARPS
+// warps takes SM_TB = SM_WARPS * SM_TW steps of one chain, copies the block's
+// a and b rows (128 bytes each) into shared memory with 16-byte cp.async,
+// scans there in place (b becomes the local state, a the factor of the
+// entering state), and stores each finished row once.  No block data sits in
+// registers, so a CTA's whole block is in flight at once and the occupancy is
+// set by shared memory.  Needs d % 4 == 0 and 16-byte aligned a, b.
+constexpr int SM_WARPS = 8, SM_TW = 16, SM_TB = SM_WARPS * SM_TW;
+static_assert(SM_TB == OP_TB, "both one-pass kernels take the same blocks");
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem_dst)),
+                 "l"(src)
+                 : "memory");
+}
+
+template <bool ADJ>
+__global__ void __launch_bounds__(SM_WARPS * 32) scan_onepass_smem_k(const OpShape sh, ChainWs ws) {
+    __shared__ __align__(16) float ta[SM_TB][32], tb[SM_TB][32];
+    __shared__ float sA[SM_WARPS][32], sB[SM_WARPS][32], s_cin[32];
+    __shared__ int s_tk;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) s_tk = atomicAdd(ws.ticket, 1);
+    __syncthreads();
+    const int64_t tk = s_tk;
+    const int64_t blk = tk / sh.n_chains, chain = tk - blk * sh.n_chains;
+    const int64_t bi = chain / sh.ngrp, j0 = (chain - bi * sh.ngrp) * 32;
+    const int64_t q0 = blk * SM_TB;
+    // Row r of the block is step q0 + r: time q0 + r (forward) or t - 1 - q0 - r.
+    for (int idx = threadIdx.x; idx < SM_TB * 8; idx += SM_WARPS * 32) {
+        const int r = idx >> 3, seg = idx & 7;
+        const int64_t q = q0 + r, j = j0 + 4 * seg;
+        if (q < sh.t && j < sh.d) {
+            const size_t o = ((size_t)bi * sh.t + (size_t)(ADJ ? sh.t - 1 - q : q)) * sh.d + j;
+            cp_async16(&ta[r][4 * seg], sh.a + o);
+            cp_async16(&tb[r][4 * seg], sh.b + o);
+        } else {
+            *reinterpret_cast<float4 *>(&ta[r][4 * seg]) = make_float4(1.f, 1.f, 1.f, 1.f);
+            *reinterpret_cast<float4 *>(&tb[r][4 * seg]) = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    // Local scan of the warp's rows from a zero state, in place.
+    float st = 0.0f, P = 1.0f;
+    const int r0 = warp * SM_TW;
+#pragma unroll 4
+    for (int i = 0; i < SM_TW; ++i) {
+        const float av = ta[r0 + i][lane], bv = tb[r0 + i][lane];
+        if (ADJ) {
+            const float out = bv + st;
+            tb[r0 + i][lane] = out;
+            ta[r0 + i][lane] = P;
+            st = av * out;
+            P = P * av;
+        } else {
+            st = av * st + bv;
+            P = P * av;
+            tb[r0 + i][lane] = st;
+            ta[r0 + i][lane] = P;
+        }
+    }
+    sA[warp][lane] = P;
+    sB[warp][lane] = st;
+    __syncthreads();
+    if (warp == 0) {
+        float eA = 1.0f, eB = 0.0f;
+#pragma unroll
+        for (int w = 0; w < SM_WARPS; ++w) {
+            const float wA = sA[w][lane], wB = sB[w][lane];
+            sA[w][lane] = eA;
+            sB[w][lane] = eB;
+            eB = fmaf(wA, eB, wB);
+            eA = wA * eA;
+        }
+        s_cin[lane] = chain_carry(ws, tk, sh.n_chains, eA, eB, 0.0f, OP_ERR, nullptr);
+    }
+    __syncthreads();
+    const float e = fmaf(sA[warp][lane], s_cin[lane], sB[warp][lane]);
+    const int64_t j = j0 + lane;
+    if (j < sh.d) {
+#pragma unroll 4
+        for (int i = 0; i < SM_TW; ++i) {
+            const int64_t q = q0 + r0 + i;
+            if (q >= sh.t) break;
+            __stcs(sh.h + ((size_t)bi * sh.t + (size_t)(ADJ ? sh.t - 1 - q : q)) * sh.d + j,
+                   fmaf(ta[r0 + i][lane], e, tb[r0 + i][lane]));
+        }
     }
 }
 
@@ -450,19 +518,17 @@ cudaError_t scan_onepass(const float *a, const float *b, float *h, int64_t batch
     if (e != cudaSuccess) return e;
     const ChainWs ws = chain_ws(scratch, slots);
     const OpShape sh{a, b, h, t, d, ngrp, batch * ngrp, (int64_t)slots};
-    // Persistent grid: the CTAs resident at once (two per SM), at most one per block.
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 1;
+    const bool staged = d % 4 == 0 && ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+    if (staged) {
+        if (adjoint)
+            scan_onepass_smem_k<true><<<(unsigned)slots, SM_WARPS * 32, 0, st>>>(sh, ws);
+        else
+            scan_onepass_smem_k<false><<<(unsigned)slots, SM_WARPS * 32, 0, st>>>(sh, ws);
+    } else if (adjoint) {
+        scan_onepass_k<true><<<(unsigned)slots, OP_WARPS * 32, 0, st>>>(sh, ws);
+    } else {
+        scan_onepass_k<false><<<(unsigned)slots, OP_WARPS * 32, 0, st>>>(sh, ws);
     }
-    const unsigned grid = (unsigned)std::min<size_t>(slots, (size_t)2 * sms);
-    if (adjoint)
-        scan_onepass_k<true><<<grid, OP_WARPS * 32, 0, st>>>(sh, ws);
-    else
-        scan_onepass_k<false><<<grid, OP_WARPS * 32, 0, st>>>(sh, ws);
     return cudaGetLastError();
 }
 

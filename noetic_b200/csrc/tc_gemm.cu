@@ -1464,6 +1464,22 @@ __global__ void split_tf32_t_k(const float *__restrict__ src, int rows, int cols
 // of the interleaved operand (output channel j: gate column 64 (j / 32) +
 // j % 32, value column 32 later), with the same f32 operations as the
 // single-piece epilogues.
+// part[0] + part[plane] + ... + part[(splits - 1) plane], added in that
+// order; the loads of eight pieces are issued before their adds, so a
+// reduction waits one memory round trip per eight pieces, not per piece.
+__device__ __forceinline__ float split_sum(const float *pp, int splits, size_t plane) {
+    float o = pp[0];
+    for (int s0 = 1; s0 < splits; s0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = s0 + e < splits ? pp[(size_t)(s0 + e) * plane] : 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            if (s0 + e < splits) o = o + v[e];
+    }
+    return o;
+}
+
 __global__ void splitk_reduce_k(const float *__restrict__ part, int splits, TcArgs p) {
     pdl_trigger();
     pdl_wait();
@@ -1477,12 +1493,8 @@ __global__ void splitk_reduce_k(const float *__restrict__ part, int splits, TcAr
     if (swiglu_H) {
         if (!valid) return;
         const int cg = 64 * (c >> 5) + (c & 31), cv = cg + 32;
-        const float *pg = part + (size_t)m * N + cg, *pv = part + (size_t)m * N + cv;
-        float g = pg[0], v = pv[0];
-        for (int sp = 1; sp < splits; ++sp) {
-            g = g + pg[sp * plane];
-            v = v + pv[sp * plane];
-        }
+        float g = split_sum(part + (size_t)m * N + cg, splits, plane);
+        float v = split_sum(part + (size_t)m * N + cv, splits, plane);
         if (p.rs_parts) {
             g = g * rscale;
             v = v * rscale;
@@ -1499,9 +1511,7 @@ __global__ void splitk_reduce_k(const float *__restrict__ part, int splits, TcAr
     }
     float o = 0.0f;
     if (valid) {
-        const float *pp = part + (size_t)m * N + c;
-        o = pp[0];
-        for (int sp = 1; sp < splits; ++sp) o = o + pp[sp * plane];
+        o = split_sum(part + (size_t)m * N + c, splits, plane);
         if (p.rs_parts) o = o * rscale;
         if (p.bias) o = o + p.bias[c];
         if (p.R) o = p.R[(size_t)m * p.ldr + c] + o;
@@ -1517,6 +1527,110 @@ __global__ void splitk_reduce_k(const float *__restrict__ part, int splits, TcAr
         }
         const float sq = warp_sum(valid ? o * o : 0.0f);
         if ((threadIdx.x & 31) == 0 && valid) p.nx_ss[(size_t)m * p.nx_nparts + (c >> 5)] = sq;
+    }
+}
+
+// Split-K reduction of a residual projection that also applies the next
+// RMSNorm: one CTA per row sums the pieces of all N columns as
+// splitk_reduce_k does, stores the row x, then computes r = 1 / sqrt(mean(x^2)
+// + eps) with the lane-strided sum of rmsnorm_k and writes x * r * gain.
+struct PostNorm {
+    const float *gain;
+    float eps;
+    float *hi, *lo, *f32;
+};
+
+__global__ void __launch_bounds__(256) splitk_reduce_norm_k(const float *__restrict__ part, int splits, TcArgs p,
+                                                             PostNorm pn) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float xrow[];
+    __shared__ float s_r;
+    const int m = blockIdx.x, N = p.N;
+    const size_t plane = (size_t)p.M * N;
+    const float rscale = folded_row_scale(p, m);
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+        float o = split_sum(part + (size_t)m * N + c, splits, plane);
+        if (p.rs_parts) o = o * rscale;
+        if (p.bias) o = o + p.bias[c];
+        if (p.R) o = p.R[(size_t)m * p.ldr + c] + o;
+        p.C[(size_t)m * p.ldc + c] = o;
+        xrow[c] = o;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float ms = 0.0f;
+        for (int j = threadIdx.x; j < N; j += 32) ms = fmaf(xrow[j], xrow[j], ms);
+        ms = warp_sum(ms);
+        if (threadIdx.x == 0) s_r = 1.0f / sqrtf(ms / (float)N + pn.eps);
+    }
+    __syncthreads();
+    const float r = s_r;
+    for (int c = threadIdx.x; c < N; c += blockDim.x) {
+        const float y = xrow[c] * r * pn.gain[c];
+        const size_t o = (size_t)m * N + c;
+        if (pn.hi) {
+            const float h = tf32_round(y);
+            pn.hi[o] = h;
+            pn.lo[o] = tf32_round(y - h);
+        } else {
+            pn.f32[o] = y;
+        }
+    }
+}
+
+// Split-K reduction of the input projection (N = 3E) that runs the decode
+// step's recurrent branch on each channel's reduced (v, z, o) instead of
+// storing u.
+struct PostSsm {
+    float *state;
+    const uint32_t *heads;
+    const float *conv_w, *conv_b;
+    int k, E;
+    float *hi, *lo, *f32;
+};
+
+template <int K>
+__global__ void __launch_bounds__(256) splitk_reduce_ssm_k(const float *__restrict__ part, int splits, TcArgs p,
+                                                            PostSsm ps) {
+    pdl_trigger();
+    pdl_wait();
+    const int E = ps.E, k = ps.k;
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long)p.M * E) return;
+    const int m = (int)(i / E), j = (int)(i - (long)m * E);
+    const size_t plane = (size_t)p.M * p.N;
+    const float *row = part + (size_t)m * p.N + j;
+    const float rscale = folded_row_scale(p, m);
+    // The three columns (v, z, o) of the channel, each summed over the pieces
+    // in split order; the loads of eight pieces of all three go out together.
+    float u[3] = {row[0], row[E], row[2 * E]};
+    for (int s0 = 1; s0 < splits; s0 += 8) {
+        float t[3][8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int f = 0; f < 3; ++f) t[f][e] = s0 + e < splits ? row[(size_t)(s0 + e) * plane + f * E] : 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+#pragma unroll
+            for (int f = 0; f < 3; ++f)
+                if (s0 + e < splits) u[f] = u[f] + t[f][e];
+    }
+#pragma unroll
+    for (int f = 0; f < 3; ++f) {
+        if (p.rs_parts) u[f] = u[f] * rscale;
+        if (p.bias) u[f] = u[f] + p.bias[f * E + j];
+    }
+    float *ring = ps.state + (size_t)m * (k + 1) * E;
+    const float gv = ssm_step_channel<K>(u[0], u[1], u[2], ring, ps.heads[m], k, E, j, ps.conv_w, ps.conv_b);
+    const size_t o = (size_t)m * E + j;
+    if (ps.hi) {
+        const float h = tf32_round(gv);
+        ps.hi[o] = h;
+        ps.lo[o] = tf32_round(gv - h);
+    } else {
+        ps.f32[o] = gv;
     }
 }
 
@@ -1538,9 +1652,7 @@ __global__ void __launch_bounds__(256) splitk_rowred_k(const float *__restrict__
     float best = -INFINITY;
     uint32_t tag = PREP ? 0u : 0xFFFFFFFFu;  // +inf count, or the first maximum's column
     for (int c = c0 + (int)threadIdx.x; c < c1; c += blockDim.x) {
-        const float *pp = part + (size_t)row * N + c;
-        float o = pp[0];
-        for (int sp = 1; sp < splits; ++sp) o = o + pp[sp * plane];
+        float o = split_sum(part + (size_t)row * N + c, splits, plane);
         if (p.rs_parts) o = o * rscale;
         if constexpr (PREP) {
             const bool pen = p.pen_bits && ((p.pen_bits[(size_t)row * p.pen_words + (c >> 5)] >> (c & 31)) & 1u);
@@ -1844,6 +1956,7 @@ cudaError_t launch_pair(const CUtensorMap &mAh, const CUtensorMap &mAl, const Tc
 
 cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const TcOperand &W, const TcEpilogue &ep,
                     int bn, cudaStream_t st, int *err) {
+    if (ep.post_done) *ep.post_done = 0;
     if (W.K != K || M <= 0 || (bn != 128 && bn != 256 && bn != TC_PAIR)) return cudaErrorInvalidValue;
     // SwiGLU mode and the interleaved operand go together; argmax never with it.
     if (ep.swiglu != (W.pair_half > 0) || (ep.swiglu && (ep.best_val || !ep.bias))) return cudaErrorInvalidValue;
@@ -1923,6 +2036,30 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
                                      W.N, r, parts)
                         : pdl_launch(splitk_rowred_k<false>, grid, dim3(256), 0, st, (const float *)ep.ws, splits, M,
                                      W.N, r, parts);
+        }
+        if (!ep.swiglu && !ep.nx_hi && ep.post_norm_gain && (ep.post_norm_hi ? ep.post_norm_lo != nullptr
+                                                                              : ep.post_norm_f32 != nullptr)) {
+            const PostNorm pn{ep.post_norm_gain, ep.post_norm_eps, ep.post_norm_hi, ep.post_norm_lo,
+                              ep.post_norm_f32};
+            if (ep.post_done) *ep.post_done = 1;
+            return pdl_launch(splitk_reduce_norm_k, dim3((unsigned)M), dim3(256), (size_t)W.N * sizeof(float), st,
+                              (const float *)ep.ws, splits, a, pn);
+        }
+        if (!ep.swiglu && !ep.nx_hi && !ep.R && ep.post_state && W.N % 3 == 0 && ep.post_heads && ep.post_conv_w &&
+            ep.post_conv_b && ep.post_k >= 1 && (ep.post_g_hi ? ep.post_g_lo != nullptr : ep.post_g_f32 != nullptr)) {
+            const int E = W.N / 3;
+            const PostSsm ps{ep.post_state, ep.post_heads, ep.post_conv_w, ep.post_conv_b, ep.post_k, E,
+                             ep.post_g_hi, ep.post_g_lo, ep.post_g_f32};
+            if (ep.post_done) *ep.post_done = 1;
+            const long outs = (long)M * E;
+            const dim3 grid((unsigned)((outs + 255) / 256));
+            const float *part = ep.ws;
+            switch (ps.k) {
+                case 2: return pdl_launch(splitk_reduce_ssm_k<2>, grid, dim3(256), 0, st, part, splits, a, ps);
+                case 3: return pdl_launch(splitk_reduce_ssm_k<3>, grid, dim3(256), 0, st, part, splits, a, ps);
+                case 4: return pdl_launch(splitk_reduce_ssm_k<4>, grid, dim3(256), 0, st, part, splits, a, ps);
+                default: return pdl_launch(splitk_reduce_ssm_k<0>, grid, dim3(256), 0, st, part, splits, a, ps);
+            }
         }
         const long outs = (long)M * (ep.swiglu ? W.pair_half : W.N);
         return pdl_launch(splitk_reduce_k, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st,

@@ -295,3 +295,39 @@ def test_folded_rmsnorm_matches_standalone_norms(gpu, orc, S):
     toks = ids[:, -1].copy()
     ga, gb = fold.step_greedy(toks).copy(), plain.step_greedy(toks).copy()
     assert (ga == gb).mean() > 0.95
+
+
+@pytest.mark.parametrize("S", [16, 64, 512])
+def test_split_k_reductions_take_over_norm_and_recurrence(gpu, orc, S):
+    """When the projections are split along K (up to 512 streams here), the
+    input projection's reduction also runs the recurrent branch and, from 128
+    streams on, the residual projections' reductions the next RMSNorm.  Both repeat the
+    separate kernels' operations (ssm_decode, rmsnorm_rows), so the steps
+    equal those with the separate kernels (engine bits 16, 17) -- logits, greedy
+    tokens and every layer's state -- and the oracle within tolerance."""
+    kw = dict(vocab=4096, d_model=768, n_layer=3, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
+    om, gm = same_model(orc, gpu, kw, seed=23)
+    T = 3
+    ids = _ids(S, T, kw["vocab"], 910)
+    fused, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
+    fused.set_engine(0)
+    plain.set_engine(65536 | 131072)
+    n0, p0 = fused.launch_count(), plain.launch_count()
+    for t in range(T):
+        a = fused.step(ids[:, t]).copy()
+        b = plain.step(ids[:, t])
+        assert np.abs(a - b).max() <= 1e-6 * max(1.0, float(np.abs(b).max())), t
+    # Per layer and step the ssm step's launch is saved, from 128 streams on
+    # also the two RMSNorms' (below that the separate norms are faster).
+    saved = 3 * (3 if S >= 128 else 1) * T
+    assert (fused.launch_count() - n0) + saved == plain.launch_count() - p0
+    sa, ha = fused.get_state()
+    sb, hb = plain.get_state()
+    assert np.array_equal(ha, hb) and state_rel_err(sa, sb) <= 1e-6
+    for s in [0, S - 1]:
+        od = orc.Decoder(om)
+        for t in range(T):
+            ref = od.step(ids[s, t])
+        assert np.abs(a[s] - ref).max() <= 1e-3, s
+    toks = ids[:, -1].copy()
+    assert np.array_equal(fused.step_greedy(toks), plain.step_greedy(toks))
