@@ -935,23 +935,51 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    // Prologue done: let the next kernel in the stream start its own, then
-    // wait until the previous one has finished writing this one's inputs.
+    // Prologue done: let the next kernel in the stream start its own.  The
+    // weights do not depend on the previous kernel, so the producer issues
+    // the weight tiles of its first STAGES K-blocks before it waits for that
+    // kernel to finish writing this one's activations.
     pdl_trigger();
+    const uint64_t pol_w = policy_evict_last();
+    auto load_b = [&](uint8_t *st, uint32_t full, int kx, int n0) {
+        if (p.l2hints) {
+            tma_load_2d_hint(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0, pol_w);
+            tma_load_2d_hint(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0, pol_w);
+        } else {
+            tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
+            tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
+        }
+    };
+    int pre = 0, cursor0 = 0;
+    Piece pc0;
+    bool have0 = false;
+    if (warp == 0 && lane == 0) {
+        have0 = next_piece(p, n_tiles, kblocks, cursor0, pc0);
+        if (have0) {
+            const int n0 = (pc0.t % n_tiles_n) * BN;
+            for (int kb = pc0.kb0; kb < pc0.kb1 && pre < STAGES; ++kb, ++pre) {
+                const uint32_t full = bar_full0 + 8 * pre;
+                mbar_expect_tx(full, STAGE_BYTES);
+                load_b(smem + pre * STAGE_BYTES, full, kb * BK, n0);
+            }
+        }
+    }
     pdl_wait();
 
     if (warp == 0 && lane == 0) {
         // ---- TMA producer: runs ahead into the next piece's K-blocks while
-        // the epilogue drains the current one.
-        const uint64_t pol_w = policy_evict_last();
+        // the epilogue drains the current one.  The first `pre` stages have
+        // their weight tiles and byte counts in place already.
         int stage = 0;
         uint32_t phase = 0;
-        int issued = 0, cursor = 0;
-        Piece pc;
-        while (!*(volatile int *)&s_abort && next_piece(p, n_tiles, kblocks, cursor, pc)) {
+        int issued = 0, cursor = cursor0;
+        Piece pc = pc0;
+        bool have = have0;
+        while (!*(volatile int *)&s_abort && have) {
             const int m0 = (pc.t / n_tiles_n) * BM, n0 = (pc.t % n_tiles_n) * BN;
             for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
-                if (!mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
+                const bool fresh = issued >= pre;
+                if (fresh && !mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
                     atomicExch(p.err, 101);
                     s_abort = 1;
                     break;
@@ -959,31 +987,28 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
                 if (*(volatile int *)&s_abort) break;
                 uint8_t *st = smem + stage * STAGE_BYTES;
                 const uint32_t full = bar_full0 + 8 * stage;
-                mbar_expect_tx(full, STAGE_BYTES);
+                if (fresh) mbar_expect_tx(full, STAGE_BYTES);
                 const int kx = kb * BK;
                 tma_load_2d(smem_u32(st), &mapAh, full, kx, m0);
                 tma_load_2d(smem_u32(st + A_BYTES), &mapAl, full, kx, m0);
-                if (p.l2hints) {
-                    tma_load_2d_hint(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0, pol_w);
-                    tma_load_2d_hint(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0, pol_w);
-                } else {
-                    tma_load_2d(smem_u32(st + 2 * A_BYTES), &mapBh, full, kx, n0);
-                    tma_load_2d(smem_u32(st + 2 * A_BYTES + B_BYTES), &mapBl, full, kx, n0);
-                }
+                if (fresh) load_b(st, full, kx, n0);
                 ++issued;
                 if (++stage == STAGES) {
                     stage = 0;
                     phase ^= 1;
                 }
             }
+            have = next_piece(p, n_tiles, kblocks, cursor, pc);
         }
         // Drain: wait (bounded) until the last issued stages have landed, so
-        // no copy is still writing this CTA's shared memory when it exits.
+        // no copy is still writing this CTA's shared memory when it exits
+        // (stages whose weight tiles went out before the wait included).
         {
             int s2 = 0;
             uint32_t ph2 = 0;
-            for (int i = 0; i < issued; ++i) {
-                if (i >= issued - STAGES) mbar_wait(bar_full0 + 8 * s2, ph2);
+            const int n_drain = issued > pre ? issued : pre;
+            for (int i = 0; i < n_drain; ++i) {
+                if (i >= n_drain - STAGES) mbar_wait(bar_full0 + 8 * s2, ph2);
                 if (++s2 == STAGES) {
                     s2 = 0;
                     ph2 ^= 1;
@@ -2004,7 +2029,13 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
         const long tiles = (long)tc_tiles_n(W.N, 128) * ((M + BM - 1) / BM);
         const int kblocks = (K + BK - 1) / BK;
         if (tiles * 2 <= slots && kblocks >= 4) {
-            splits = (int)std::min<long>(kblocks / 2, std::max<long>(2, slots / tiles));
+            // Pieces: one per CTA slot, or one per SM up to 128 rows, where a
+            // piece's fixed cost (pipeline fill, partial tile written and
+            // re-read) outweighs its share of the weight stream (measured
+            // at the d768 widths: 0.80 vs 0.89 ms per step at 16 streams,
+            // 0.96 vs 1.02 at 64, but 1.40 vs 1.37 at 256).
+            const long pieces = M <= 128 ? slots / 2 : slots;
+            splits = (int)std::min<long>(kblocks / 2, std::max<long>(2, pieces / tiles));
             kps = (kblocks + splits - 1) / splits;
             splits = (kblocks + kps - 1) / kps;
             while (splits > 1 && (size_t)splits * M * W.N > ep.ws_floats) {
