@@ -708,7 +708,7 @@ constexpr int ENGINE_FOLD = 16384;
 // above 512 streams).
 constexpr int ENGINE_NO_POST_NORM = 65536;
 constexpr int ENGINE_NO_POST_SSM = 131072;
-constexpr int POST_NORM_MIN_ROWS = 128;  // streams from which the reductions take over RMSNorm
+constexpr int POST_NORM_MIN_ROWS = 384;  // streams from which the reductions take over RMSNorm
 constexpr uint64_t TEST_WAIT_NS = 2000000ull;
 void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
     if (dec->engine & ENGINE_NO_TMA_STORE) ep.no_tma_store = true;
@@ -1234,9 +1234,10 @@ void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint3
                      &p_ssm))
             launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w), m->dp(L.conv_b),
                                           gated.out(t_out), S, E, k, st), "ssm step");
-        // The norm-taking reduction runs one CTA per row: with fewer rows than
-        // SMs it is slower than the separate kernels (measured 1.070 vs 1.019
-        // ms per step at 64 streams, 1.657 vs 1.724 at 512).
+        // The norm-taking reduction runs one CTA per row: with few rows it is
+        // slower than the separate kernels (measured, ms per step, with / without:
+        // d768 1.070 / 1.019 at 64 streams and 1.657 / 1.763 at 512; d192 at 256
+        // streams 0.214 / 0.194).
         const bool post_norm = S >= POST_NORM_MIN_ROWS;
         Post p_n2;
         p_n2.norm_gain = post_norm ? m->dp(L.n2) : nullptr;

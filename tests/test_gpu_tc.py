@@ -300,7 +300,7 @@ def test_folded_rmsnorm_matches_standalone_norms(gpu, orc, S):
 @pytest.mark.parametrize("S", [16, 64, 512])
 def test_split_k_reductions_take_over_norm_and_recurrence(gpu, orc, S):
     """When the projections are split along K (up to 512 streams here), the
-    input projection's reduction also runs the recurrent branch and, from 128
+    input projection's reduction also runs the recurrent branch and, from 384
     streams on, the residual projections' reductions the next RMSNorm.  Both repeat the
     separate kernels' operations (ssm_decode, rmsnorm_rows), so the steps
     equal those with the separate kernels (engine bits 16, 17) -- logits, greedy
@@ -317,9 +317,9 @@ def test_split_k_reductions_take_over_norm_and_recurrence(gpu, orc, S):
         a = fused.step(ids[:, t]).copy()
         b = plain.step(ids[:, t])
         assert np.abs(a - b).max() <= 1e-6 * max(1.0, float(np.abs(b).max())), t
-    # Per layer and step the ssm step's launch is saved, from 128 streams on
+    # Per layer and step the ssm step's launch is saved, from 384 streams on
     # also the two RMSNorms' (below that the separate norms are faster).
-    saved = 3 * (3 if S >= 128 else 1) * T
+    saved = 3 * (3 if S >= 384 else 1) * T
     assert (fused.launch_count() - n0) + saved == plain.launch_count() - p0
     sa, ha = fused.get_state()
     sb, hb = plain.get_state()
