@@ -242,7 +242,7 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * epilogue is not overlapped with the main loop.
  * Bit 15: the 256-wide projection epilogues store from the threads through
  * a transposing buffer instead of the default bulk tensor stores.
- * Bits 16 / 17: with projections split along K (up to 512 streams), the
+ * Bits 16 / 17: with projections split along K (up to 2048 streams), the
  * reductions do not apply the next RMSNorm (taken over from 384 streams) /
  * do not run the recurrent branch; the separate kernels run instead, with
  * the same results. */

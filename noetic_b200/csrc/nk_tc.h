@@ -106,7 +106,7 @@ struct TcEpilogue {
     // stores (C 16-byte aligned, ldc a multiple of 4) unless this is set.
     bool no_tma_store = false;
     // Work taken over by the split-K reduction when the projection is split
-    // along K (one row of tiles, M <= 512); *post_done (nullable) is set to 1
+    // along K (128-wide tiles in one wave, M <= 2048); *post_done (nullable) is set to 1
     // when it was, else 0 and the caller runs the separate kernel.
     //  - post_norm (store mode with N = d): after the row x is stored, its
     //    RMSNorm x * r * gain, r = 1 / sqrt(mean(x^2) + eps) (tensor.rs:298-312,

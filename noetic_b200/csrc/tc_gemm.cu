@@ -54,7 +54,11 @@ namespace {
 // stages of 32 KiB, 256 TMEM columns each, so one CTA's epilogue overlaps the
 // other's main loop and small grids still cover every SM).
 constexpr int BM = 128, BK = 16;
-constexpr int SPLIT_MAX_M = 512;  // rows up to which small projections are split along K
+// Rows up to which projections whose 128-wide tiles fit one wave are split
+// along K (decode of up to 2048 streams; measured at the headline widths, ms
+// per step against stream-K 256-wide tiles: 6.2 vs 7.7 at 1024 streams,
+// 9.73 vs 10.0-10.2 at 2048).
+constexpr int SPLIT_MAX_M = 2048;
 constexpr int ROWRED_COLS = 1024; // columns per partial of the split-K argmax / sampling reduction
 constexpr int SWIZZLE_BYTES = BK * 4;                       // 64
 constexpr int ATOM_BYTES = 8 * SWIZZLE_BYTES;               // 8 rows: 512
