@@ -237,15 +237,18 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * Bit 14: RMSNorm folded into the tensor-core decode step's projections
  * (each residual projection's epilogue writes the next projection's
  * gain-scaled operand and the rows' sums of squares, and the consumer scales
- * its rows by the RMSNorm factor) instead of the stand-alone kernels; 47
- * fewer launches per step, but measured slower on B200 because the longer
- * epilogue is not overlapped with the main loop.
+ * its rows by the RMSNorm factor) instead of the stand-alone kernels, at
+ * every batch; 47 fewer launches per step.  The default folds below 384
+ * streams at model widths of 512 and more (where the projections are split
+ * along K and the rows are wide enough), not otherwise: above, the longer
+ * epilogue, not overlapped with the main loop, measured slower.
  * Bit 15: the 256-wide projection epilogues store from the threads through
  * a transposing buffer instead of the default bulk tensor stores.
  * Bits 16 / 17: with projections split along K (up to 2048 streams), the
  * reductions do not apply the next RMSNorm (taken over from 384 streams) /
  * do not run the recurrent branch; the separate kernels run instead, with
- * the same results. */
+ * the same results.
+ * Bit 18: no RMSNorm folding below 384 streams (stand-alone norm kernels). */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

@@ -698,10 +698,12 @@ struct SampScope {
 constexpr int ENGINE_NO_TMA_STORE = 32768;  // epilogue stores from the threads instead of bulk stores
 constexpr int ENGINE_WITHHOLD_PUBLISH = 4096;
 constexpr int ENGINE_WITHHOLD_ARRIVAL = 8192;
-// RMSNorm folded into the projection epilogues (opt-in): measured slower on
-// B200 (77 vs 70 ms per step at 16384 streams, 12.7 vs 10.9 at 2048), since
-// the 256-wide tile's epilogue is not overlapped with the next tile's main
-// loop and the extra stores lengthen it by more than the norm kernels cost.
+// RMSNorm folded into the projection epilogues (forced at every batch; the
+// default only below POST_NORM_MIN_ROWS streams): measured slower on B200 at
+// large batches (77 vs 70 ms per step at 16384 streams, 12.7 vs 10.9 at
+// 2048), since the 256-wide tile's epilogue is not overlapped with the next
+// tile's main loop and the extra stores lengthen it by more than the norm
+// kernels cost.
 constexpr int ENGINE_FOLD = 16384;
 // Engine bits 16 / 17: the split-K reductions of small projections do not
 // take over the next RMSNorm / the recurrent branch (separate kernels, as
@@ -709,6 +711,9 @@ constexpr int ENGINE_FOLD = 16384;
 constexpr int ENGINE_NO_POST_NORM = 65536;
 constexpr int ENGINE_NO_POST_SSM = 131072;
 constexpr int POST_NORM_MIN_ROWS = 384;  // streams from which the reductions take over RMSNorm
+// Engine bit 18: no RMSNorm folding below POST_NORM_MIN_ROWS streams (the
+// stand-alone norm kernels instead).
+constexpr int ENGINE_NO_AUTO_FOLD = 262144;
 constexpr uint64_t TEST_WAIT_NS = 2000000ull;
 void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
     if (dec->engine & ENGINE_NO_TMA_STORE) ep.no_tma_store = true;
@@ -1147,8 +1152,17 @@ void step_device(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint
 // widths on the 32-column grid.
 bool fold_norms(const nk_decoder *dec) {
     const nk_model *m = dec->model;
-    if (!(dec->engine & ENGINE_FOLD) || (dec->engine & 128)) return false;  // (no folded CTA-pair epilogue)
     const int S = (int)dec->S, d = (int)m->d(), E = (int)m->e(), H = (int)m->hidden(), V = (int)m->cfg.vocab;
+    // Folded by default below POST_NORM_MIN_ROWS streams at widths of 512 and
+    // more, where every projection is split along K and its reduction applies
+    // the row scale (measured, ms per step, folded / stand-alone norms: d768
+    // 0.677 / 0.762 at 16 streams, 0.876 / 0.916 at 64, 1.335 / 1.377 at 256,
+    // but 1.711 / 1.611 at 512 where the reductions take the norms over; the
+    // headline widths 1.97 / 2.04 at 64 streams, 7.17 / 6.24 at 1024; d192 at
+    // 256 streams 0.218 / 0.194).
+    const bool want = (dec->engine & ENGINE_FOLD) ||
+                      (S < POST_NORM_MIN_ROWS && d >= 512 && !(dec->engine & ENGINE_NO_AUTO_FOLD));
+    if (!want || (dec->engine & 128)) return false;  // (no folded CTA-pair epilogue)
     if (d % 32 != 0 || m->cfg.n_layer == 0) return false;
     for (size_t i = 0; i < 4 * m->cfg.n_layer + 1; ++i)
         if (!tc_op(const_cast<nk_model *>(m), i)) return false;
@@ -1185,10 +1199,15 @@ void eager_step(nk_decoder *dec, const uint32_t *tokens, bool want_logits, uint3
             const LayerIx &L = m->layers[l];
             const Fold f_in{l ? dec->nss : nullptr, nullptr}, f_out{nullptr, m->dp(L.n2)}, f_up{dec->nss, nullptr},
                 f_dn{nullptr, l + 1 < m->cfg.n_layer ? m->dp(m->layers[l + 1].n1) : m->dp(m->norm_f)};
-            project(dec, true, nx, S, d, m->dp(L.in_w), tc_op(m, 4 * l + 0), 3 * E, m->dp(L.in_b), dec->u, nullptr,
-                    &f_in);
-            launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w), m->dp(L.conv_b),
-                                          gated.out(true), S, E, k, st), "ssm step");
+            Post p_ssm;
+            p_ssm.state = dec->layer_state(l);
+            p_ssm.conv_w = m->dp(L.conv_w);
+            p_ssm.conv_b = m->dp(L.conv_b);
+            p_ssm.g_out = gated.out(true);
+            if (!project(dec, true, nx, S, d, m->dp(L.in_w), tc_op(m, 4 * l + 0), 3 * E, m->dp(L.in_b), dec->u,
+                         nullptr, &f_in, &p_ssm))
+                launch_ok(dec, nk::ssm_decode(dec->u, dec->layer_state(l), dec->heads, m->dp(L.conv_w),
+                                              m->dp(L.conv_b), gated.out(true), S, E, k, st), "ssm step");
             project(dec, true, gated, S, E, m->dp(L.out_w), tc_op(m, 4 * l + 1), d, m->dp(L.out_b), dec->x, dec->x,
                     &f_out);
             const Act s_act = project_swiglu(dec, true, nx, S, d, m->dp(L.up_w), tc_op(m, 4 * l + 2), H,
@@ -2451,7 +2470,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 262143) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 524287) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

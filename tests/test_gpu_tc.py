@@ -271,15 +271,17 @@ def test_long_prompt_model_widths_at_serving_batches(gpu, orc, S):
 
 @pytest.mark.parametrize("S", [64, 384, 2048])
 def test_folded_rmsnorm_matches_standalone_norms(gpu, orc, S):
-    """RMSNorm folded into the projections (engine bit 14) against the
-    stand-alone RMSNorm kernels (the default) and the oracle, at split-K (64,
-    384 streams) and stream-K (2048) tilings, greedy steps included."""
+    """RMSNorm folded into the projections (engine bit 14; the default below
+    384 streams at widths >= 512) against the stand-alone RMSNorm kernels
+    (engine bit 18 below 384 streams, the default above) and the oracle, at
+    split-K (64, 384, 2048 streams) tilings, greedy steps included."""
     kw = dict(vocab=2048, d_model=512, n_layer=3, expand=1, conv_k=4, mlp_mult=3, eps=1e-5, tau_max=128.0)
     om, gm = same_model(orc, gpu, kw, seed=21)
     T = 3
     ids = _ids(S, T, kw["vocab"], 900)
     fold, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
     fold.set_engine(16384)
+    plain.set_engine(262144)  # below 384 streams the default folds too
     for t in range(T):
         a = fold.step(ids[:, t]).copy()
         b = plain.step(ids[:, t])
@@ -310,8 +312,9 @@ def test_split_k_reductions_take_over_norm_and_recurrence(gpu, orc, S):
     T = 3
     ids = _ids(S, T, kw["vocab"], 910)
     fused, plain = gpu.Decoder(gm, S), gpu.Decoder(gm, S)
-    fused.set_engine(0)
-    plain.set_engine(65536 | 131072)
+    # stand-alone norms (below 384 streams the default folds them instead)
+    fused.set_engine(262144)
+    plain.set_engine(262144 | 65536 | 131072)
     n0, p0 = fused.launch_count(), plain.launch_count()
     for t in range(T):
         a = fused.step(ids[:, t]).copy()
