@@ -248,7 +248,9 @@ nk_status nk_decoder_sync(nk_decoder *dec);
  * reductions do not apply the next RMSNorm (taken over from 384 streams) /
  * do not run the recurrent branch; the separate kernels run instead, with
  * the same results.
- * Bit 18: no RMSNorm folding below 384 streams (stand-alone norm kernels). */
+ * Bit 18: no RMSNorm folding below 384 streams (stand-alone norm kernels).
+ * Bit 19: projection tiles in plain row-major order instead of groups of
+ * column blocks whose weights fit in L2. */
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine);
 
 /* Number of kernels this decoder has launched so far. */

@@ -105,6 +105,9 @@ struct TcEpilogue {
     // 256-wide store / SwiGLU / sampling epilogues write through bulk tensor
     // stores (C 16-byte aligned, ldc a multiple of 4) unless this is set.
     bool no_tma_store = false;
+    // Tiles in the plain row-major order instead of groups of column blocks
+    // whose weights fit in 24 MB of L2.
+    bool no_tile_group = false;
     // Work taken over by the split-K reduction when the projection is split
     // along K (128-wide tiles in one wave, M <= 2048); *post_done (nullable) is set to 1
     // when it was, else 0 and the caller runs the separate kernel.

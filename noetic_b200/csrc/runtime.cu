@@ -714,9 +714,12 @@ constexpr int POST_NORM_MIN_ROWS = 384;  // streams from which the reductions ta
 // Engine bit 18: no RMSNorm folding below POST_NORM_MIN_ROWS streams (the
 // stand-alone norm kernels instead).
 constexpr int ENGINE_NO_AUTO_FOLD = 262144;
+// Engine bit 19: projection tiles in plain row-major order (no column groups).
+constexpr int ENGINE_NO_TILE_GROUP = 524288;
 constexpr uint64_t TEST_WAIT_NS = 2000000ull;
 void test_controls(const nk_decoder *dec, nk::TcEpilogue &ep) {
     if (dec->engine & ENGINE_NO_TMA_STORE) ep.no_tma_store = true;
+    if (dec->engine & ENGINE_NO_TILE_GROUP) ep.no_tile_group = true;
     if (dec->engine & ENGINE_WITHHOLD_PUBLISH) {
         ep.withhold_publish = true;
         ep.handoff_wait_ns = TEST_WAIT_NS;
@@ -876,6 +879,7 @@ void project_argmax(nk_decoder *dec, bool tc, const Act &a, int M, int K, const 
             ep.best_val = dec->best_val;
             ep.best_idx = dec->best_idx;
             ep.l2hints = false;  // the tied embedding (268 MB as hi + lo) does not fit L2
+            ep.no_tile_group = (dec->engine & ENGINE_NO_TILE_GROUP) != 0;
             ep.launches = &dec->launches;
             ep.parts_out = &parts;
             if (!(dec->engine & 256)) {  // small projections split along K use the workspace
@@ -2470,7 +2474,7 @@ nk_status nk_decoder_sync(nk_decoder *dec) {
 nk_status nk_decoder_set_engine(nk_decoder *dec, int engine) {
     return guard([&] {
         if (!dec) fail(NK_ERR_INVALID, "null decoder");
-        if (engine < 0 || engine > 524287) fail(NK_ERR_INVALID, "unknown engine flags");
+        if (engine < 0 || engine > 1048575) fail(NK_ERR_INVALID, "unknown engine flags");
         dec->engine = engine;
         cudaSetDevice(dec->model->device);
         for (auto &gph : dec->graphs) cudaGraphExecDestroy(gph.exec);

@@ -160,7 +160,25 @@ struct TcArgs {
     // with a TMA bulk store from the warp's staging buffer (mapC / mapClo),
     // so the stores drain while the next tile's MMAs run.
     int tma_store;
+    // Tile order: tiles go in groups of group_n column blocks (0: one group),
+    // column blocks fastest within a group, so the CTAs running at once read
+    // one group's weight columns, which stay in L2 from wave to wave.
+    int group_n;
 };
+
+// Tile t -> (row block tm, column block tn) in the grouped order.
+__device__ __forceinline__ void tile_coords(int t, int n_tiles_n, int m_tiles, int group_n, int &tm, int &tn) {
+    if (group_n <= 0 || group_n >= n_tiles_n) {
+        tm = t / n_tiles_n;
+        tn = t - tm * n_tiles_n;
+        return;
+    }
+    const int per_group = group_n * m_tiles;
+    const int g = t / per_group, r = t - g * per_group;
+    const int width = min(group_n, n_tiles_n - g * group_n);
+    tm = r / width;
+    tn = g * group_n + (r - tm * width);
+}
 
 // 1 / sqrt(ms / d + eps) of a row from its partial sums of squares (1 when
 // the projection's input was normalised already).
@@ -905,7 +923,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles_n = (p.N + BN - 1) / BN;
-    const int n_tiles = n_tiles_n * ((p.M + BM - 1) / BM);
+    const int m_tiles = (p.M + BM - 1) / BM;
+    const int n_tiles = n_tiles_n * m_tiles;
     const int kblocks = (p.K + BK - 1) / BK;
 
     const uint32_t bar_full0 = smem_u32(&bars[0]);
@@ -960,7 +979,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
     if (warp == 0 && lane == 0) {
         have0 = next_piece(p, n_tiles, kblocks, cursor0, pc0);
         if (have0) {
-            const int n0 = (pc0.t % n_tiles_n) * BN;
+            int tm0, tn0;
+            tile_coords(pc0.t, n_tiles_n, m_tiles, p.group_n, tm0, tn0);
+            const int n0 = tn0 * BN;
             for (int kb = pc0.kb0; kb < pc0.kb1 && pre < STAGES; ++kb, ++pre) {
                 const uint32_t full = bar_full0 + 8 * pre;
                 mbar_expect_tx(full, STAGE_BYTES);
@@ -980,7 +1001,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         Piece pc = pc0;
         bool have = have0;
         while (!*(volatile int *)&s_abort && have) {
-            const int m0 = (pc.t / n_tiles_n) * BM, n0 = (pc.t % n_tiles_n) * BN;
+            int tm, tn;
+            tile_coords(pc.t, n_tiles_n, m_tiles, p.group_n, tm, tn);
+            const int m0 = tm * BM, n0 = tn * BN;
             for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
                 const bool fresh = issued >= pre;
                 if (fresh && !mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
@@ -1076,7 +1099,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
         int i = 0, cursor = 0, n_part = 0, n_fin = 0;
         Piece pc;
         for (; next_piece(p, n_tiles, kblocks, cursor, pc); ++i) {
-            const int m0 = (pc.t / n_tiles_n) * BM, tn = pc.t % n_tiles_n, n0 = tn * BN;
+            int tm, tn;
+            tile_coords(pc.t, n_tiles_n, m_tiles, p.group_n, tm, tn);
+            const int m0 = tm * BM, n0 = tn * BN;
             const bool ok = mbar_wait(bar_acc_full, (uint32_t)(i & 1)) && !*(volatile int *)&s_abort;
             __syncwarp();
             if (!ok) {
@@ -2016,6 +2041,16 @@ cudaError_t tc_gemm(const float *A_hi, const float *A_lo, int M, int K, const Tc
                  (ep.nx_hi && (!ep.nx_lo || !ep.nx_gain || !ep.nx_ss || ep.swiglu || ep.best_val || prep ||
                                W.N % 32 != 0))))
         return cudaErrorInvalidValue;
+    // Grouped tile order: the column blocks whose weight pair (W_hi + W_lo,
+    // 8 bytes per element) fits in 24 MB form a group, so a wave reads one
+    // group's weights, which L2 keeps for the next wave, while the A rows
+    // stream once per group.
+    if (bn != TC_PAIR && !ep.no_tile_group) {
+        const int w = bn == 256 ? 256 : 128;
+        const size_t col_bytes = (size_t)w * K * 8;
+        const int gn = (int)std::max<size_t>(1, ((size_t)24 << 20) / col_bytes);
+        a.group_n = gn < tc_tiles_n(W.N, bn) ? gn : 0;
+    }
     if (a.ws) {
         // Stream-K needs one partial slot and one counter per SM.
         const int sms = sm_count_cached();
