@@ -1004,6 +1004,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap mapAh, const __grid_constant_
             int tm, tn;
             tile_coords(pc.t, n_tiles_n, m_tiles, p.group_n, tm, tn);
             const int m0 = tm * BM, n0 = tn * BN;
+            if (p.R && p.splits <= 0 && pc.np >= 0 && p.ldr % 4 == 0) {
+                // The residual rows this piece's epilogue will add go to L2
+                // while its K-blocks stream, so the epilogue finds them there.
+                const int cols = min(BN, p.N - n0), rows = min(BM, p.M - m0);
+                const uint32_t bytes = (uint32_t)((cols * 4) & ~15);
+                for (int r = 0; bytes && r < rows; ++r)
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(
+                                     (uint64_t)(p.R + (size_t)(m0 + r) * p.ldr + n0)),
+                                 "r"(bytes)
+                                 : "memory");
+            }
             for (int kb = pc.kb0; kb < pc.kb1; ++kb) {
                 const bool fresh = issued >= pre;
                 if (fresh && !mbar_wait(bar_empty0 + 8 * stage, phase ^ 1)) {
